@@ -1,0 +1,295 @@
+// asa_capi.cu -- the extern "C" entry points declared in include/asa.h:
+// argument checks, workspace layout, backend choice and launch order.
+//
+// Reference host launchers replaced: forward_splash / backward_splash
+// (source/adasplashattention.cu:537-700).  Differences by design: nothing is
+// allocated here (the caller passes every buffer), nothing synchronises the
+// device, launches go on the caller's stream, and errors come back as status
+// codes instead of exceptions.
+#include "asa_internal.h"
+#include <climits>
+#include <cmath>
+#include <cstring>
+
+namespace asa {
+// tcgen05 kernels (asa_tc.cu)
+bool tc_supported(const Shape& s);
+size_t tc_fwd_workspace(const Shape& s);
+size_t tc_bwd_workspace(const Shape& s);
+cudaError_t tc_tau_mask(const Shape& s, const void* Q, const void* K, const int32_t* Qidx,
+                        const int32_t* Kidx, float* tau, uint8_t* M, void* ws, int* err,
+                        cudaStream_t st);
+cudaError_t tc_forward(const Shape& s, const void* Q, const void* K, const void* V,
+                       const int32_t* Qidx, const int32_t* Kidx, const float* tau,
+                       const int32_t* ptr, const int32_t* idx, void* O, float* O32,
+                       float* rownorm, void* ws, int* err, cudaStream_t st);
+cudaError_t tc_backward(const Shape& s, const void* Q, const void* K, const void* V,
+                        const int32_t* Qidx, const int32_t* Kidx, const float* O32,
+                        const float* tau, const int32_t* ptr, const int32_t* idx,
+                        const int32_t* cptr, const int32_t* cidx, const float* rownorm,
+                        const void* dO, void* dQ, void* dK, void* dV, void* ws, int* err,
+                        cudaStream_t st);
+}  // namespace asa
+
+__device__ int g_asa_error;
+
+namespace {
+
+using asa::Shape;
+
+constexpr int kMaxDevices = 64;
+int* g_err_ptr[kMaxDevices];
+
+int* error_word() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+    if (!g_err_ptr[dev]) {
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_asa_error) != cudaSuccess) return nullptr;
+        g_err_ptr[dev] = (int*)p;
+    }
+    return g_err_ptr[dev];
+}
+
+size_t align16(size_t x) { return (x + 15) & ~size_t(15); }
+
+int check_params(const asa_params* p) {
+    if (!p) return ASA_ERR_INVALID;
+    if (p->B < 1 || p->H < 1 || p->NQ < 0 || p->NK < 0) return ASA_ERR_INVALID;
+    if (p->d < 1 || p->block_m < 1 || p->block_n < 1) return ASA_ERR_INVALID;
+    if (p->k_keep < 1 || p->k_keep > p->block_n) return ASA_ERR_INVALID;   // reference :32
+    if (!std::isfinite(p->alpha) || !std::isfinite(p->sm_scale)) return ASA_ERR_INVALID;
+    if ((p->in_dtype != ASA_DTYPE_F32 && p->in_dtype != ASA_DTYPE_BF16) ||
+        (p->out_dtype != ASA_DTYPE_F32 && p->out_dtype != ASA_DTYPE_BF16))
+        return ASA_ERR_INVALID;
+    if (p->backend < ASA_BACKEND_AUTO || p->backend > ASA_BACKEND_TC) return ASA_ERR_INVALID;
+    if (p->precision != ASA_PREC_SPLIT && p->precision != ASA_PREC_BF16) return ASA_ERR_INVALID;
+    if (p->d > 128) return ASA_ERR_UNSUPPORTED;        // reference D_MAX (:14-16)
+    if (p->k_keep > 32) return ASA_ERR_UNSUPPORTED;
+    const long long BH = (long long)p->B * p->H;
+    if (BH > INT_MAX / 2 || BH * p->NQ * p->d > (1LL << 40) || BH * p->NK * p->d > (1LL << 40))
+        return ASA_ERR_UNSUPPORTED;
+    return ASA_OK;
+}
+
+Shape make_shape(const asa_params* p) {
+    Shape s;
+    s.BH = p->B * p->H;
+    s.NQ = p->NQ;
+    s.NK = p->NK;
+    s.d = p->d;
+    s.BM = p->block_m;
+    s.BN = p->block_n;
+    s.k = p->k_keep;
+    s.causal = p->causal ? 1 : 0;
+    s.nQB = (p->NQ + p->block_m - 1) / p->block_m;
+    s.nKB = (p->NK + p->block_n - 1) / p->block_n;
+    s.alpha = std::fmax(1.05f, std::fmin(p->alpha, 3.0f));               // :547
+    s.am1 = s.alpha - 1.0f;
+    s.inv_am1b = 1.0f / (s.alpha - 1.0f);
+    s.scale = p->sm_scale;
+    s.pinv = asa::make_pow(1.0f / s.am1);
+    s.pe2 = asa::make_pow((2.0f - s.alpha) / (s.alpha - 1.0f));          // :495
+    s.spins = p->timeout_spins > 0 ? p->timeout_spins : (1LL << 26);
+    s.in_dtype = p->in_dtype;
+    s.out_dtype = p->out_dtype;
+    return s;
+}
+
+int resolve(const asa_params* p, const Shape& s) {
+    if (p->backend == ASA_BACKEND_SIMT) return ASA_BACKEND_SIMT;
+    const bool tc = asa::tc_supported(s);
+    if (p->backend == ASA_BACKEND_TC) return tc ? ASA_BACKEND_TC : -ASA_ERR_UNSUPPORTED;
+    return tc ? ASA_BACKEND_TC : ASA_BACKEND_SIMT;
+}
+
+// Backward workspace: [invN | accdO | csc_ptr | csc_idx | backend extra]
+struct BwdLayout {
+    size_t invN, accdO, cptr, cidx, extra, total;
+};
+BwdLayout bwd_layout(const Shape& s, int backend) {
+    BwdLayout L;
+    size_t o = 0;
+    const size_t rows = (size_t)s.BH * s.NQ;
+    L.invN = o; o = align16(o + rows * 4);
+    L.accdO = o; o = align16(o + rows * 4);
+    L.cptr = o; o = align16(o + (size_t)s.BH * (s.nKB + 1) * 4);
+    L.cidx = o; o = align16(o + (size_t)s.BH * s.nKB * s.nQB * 4);
+    L.extra = o;
+    if (backend == ASA_BACKEND_TC) o = align16(o + asa::tc_bwd_workspace(s));
+    L.total = o + 16;
+    return L;
+}
+size_t fwd_bytes(const Shape& s, int backend) {
+    size_t o = 16;
+    if (backend == ASA_BACKEND_TC) o = align16(o + asa::tc_fwd_workspace(s));
+    return o;
+}
+
+int cuda_status(cudaError_t e) { return e == cudaSuccess ? ASA_OK : ASA_ERR_CUDA; }
+
+}  // namespace
+
+extern "C" {
+
+void asa_params_default(asa_params* p) {
+    if (!p) return;
+    std::memset(p, 0, sizeof(*p));
+    p->B = p->H = 1;
+    p->block_m = p->block_n = 128;
+    p->k_keep = 8;
+    p->alpha = 1.5f;
+    p->causal = 1;
+    p->in_dtype = ASA_DTYPE_BF16;
+    p->out_dtype = ASA_DTYPE_BF16;
+    p->backend = ASA_BACKEND_AUTO;
+    p->precision = ASA_PREC_SPLIT;
+}
+
+int asa_resolve_backend(const asa_params* p) {
+    int rc = check_params(p);
+    if (rc) return -rc;
+    return resolve(p, make_shape(p));
+}
+
+int asa_workspace_bytes(const asa_params* p, size_t* fwd, size_t* bwd) {
+    int rc = check_params(p);
+    if (rc) return rc;
+    Shape s = make_shape(p);
+    int b = resolve(p, s);
+    if (b < 0) return -b;
+    if (fwd) *fwd = fwd_bytes(s, b);
+    if (bwd) *bwd = bwd_layout(s, b).total;
+    return ASA_OK;
+}
+
+int asa_tau_mask(const asa_params* p, const void* Q, const void* K, const int32_t* Qidx,
+                 const int32_t* Kidx, float* tau, uint8_t* M, int32_t* csr_ptr, int32_t* csr_idx,
+                 void* ws, size_t ws_bytes, asa_stream_t stream) {
+    int rc = check_params(p);
+    if (rc) return rc;
+    Shape s = make_shape(p);
+    int b = resolve(p, s);
+    if (b < 0) return -b;
+    if (s.NQ == 0) return ASA_OK;
+    if (!Q || (!K && s.NK) || !tau || !M || (p->causal && (!Qidx || (!Kidx && s.NK))))
+        return ASA_ERR_INVALID;
+    if (ws_bytes < fwd_bytes(s, b) || !ws) return ASA_ERR_WORKSPACE;
+    cudaStream_t st = (cudaStream_t)stream;
+    cudaError_t e;
+    if (b == ASA_BACKEND_TC)
+        e = asa::tc_tau_mask(s, Q, K, Qidx, Kidx, tau, M, ws, error_word(), st);
+    else
+        e = asa::simt_tau_mask(s, Q, K, Qidx, Kidx, tau, M, st);
+    if (e != cudaSuccess) return ASA_ERR_CUDA;
+    if (csr_ptr && csr_idx) e = asa::build_lists(s, M, csr_ptr, csr_idx, nullptr, nullptr, st);
+    return cuda_status(e);
+}
+
+int asa_forward(const asa_params* p, const void* Q, const void* K, const void* V,
+                const int32_t* Qidx, const int32_t* Kidx, void* O, float* O32, float* tau,
+                uint8_t* M, int32_t* csr_ptr, int32_t* csr_idx, float* rownorm, void* ws,
+                size_t ws_bytes, asa_stream_t stream) {
+    int rc = check_params(p);
+    if (rc) return rc;
+    Shape s = make_shape(p);
+    int b = resolve(p, s);
+    if (b < 0) return -b;
+    if (s.NQ == 0) return ASA_OK;
+    if (!O || !csr_ptr || !csr_idx || !rownorm) return ASA_ERR_INVALID;
+    if (!V && s.NK) return ASA_ERR_INVALID;
+    rc = asa_tau_mask(p, Q, K, Qidx, Kidx, tau, M, csr_ptr, csr_idx, ws, ws_bytes, stream);
+    if (rc) return rc;
+    cudaStream_t st = (cudaStream_t)stream;
+    cudaError_t e;
+    if (b == ASA_BACKEND_TC)
+        e = asa::tc_forward(s, Q, K, V, Qidx, Kidx, tau, csr_ptr, csr_idx, O, O32, rownorm, ws,
+                            error_word(), st);
+    else
+        e = asa::simt_forward(s, Q, K, V, Qidx, Kidx, tau, csr_ptr, csr_idx, O, O32, rownorm, st);
+    return cuda_status(e);
+}
+
+int asa_backward(const asa_params* p, const void* Q, const void* K, const void* V,
+                 const int32_t* Qidx, const int32_t* Kidx, const float* O32, const float* tau,
+                 const uint8_t* M, const int32_t* csr_ptr, const int32_t* csr_idx,
+                 const float* rownorm, const void* dO, void* dQ, void* dK, void* dV, void* ws,
+                 size_t ws_bytes, asa_stream_t stream) {
+    int rc = check_params(p);
+    if (rc) return rc;
+    Shape s = make_shape(p);
+    int b = resolve(p, s);
+    if (b < 0) return -b;
+    if (!ws) return ASA_ERR_WORKSPACE;
+    BwdLayout L = bwd_layout(s, b);
+    if (ws_bytes < L.total) return ASA_ERR_WORKSPACE;
+    cudaStream_t st = (cudaStream_t)stream;
+    const size_t kbytes = (size_t)s.BH * s.NK * s.d * (p->out_dtype == ASA_DTYPE_F32 ? 4 : 2);
+    if (s.NQ == 0) {   // no queries: every key gradient is zero
+        if (kbytes) {
+            if (!dK || !dV) return ASA_ERR_INVALID;
+            cudaError_t e = cudaMemsetAsync(dK, 0, kbytes, st);
+            if (e == cudaSuccess) e = cudaMemsetAsync(dV, 0, kbytes, st);
+            return cuda_status(e);
+        }
+        return ASA_OK;
+    }
+    if (!Q || !dO || !dQ || !tau || !M || !csr_ptr || !csr_idx) return ASA_ERR_INVALID;
+    if (s.NK && (!K || !V || !dK || !dV)) return ASA_ERR_INVALID;
+    if (p->causal && (!Qidx || (!Kidx && s.NK))) return ASA_ERR_INVALID;
+    char* w = (char*)ws;
+    float* invN = (float*)(w + L.invN);
+    float* accdO = (float*)(w + L.accdO);
+    int32_t* cptr = (int32_t*)(w + L.cptr);
+    int32_t* cidx = (int32_t*)(w + L.cidx);
+    cudaError_t e = asa::build_lists(s, M, nullptr, nullptr, cptr, cidx, st);
+    if (e != cudaSuccess) return ASA_ERR_CUDA;
+    if (b == ASA_BACKEND_TC) {
+        if (!O32 || !rownorm) return ASA_ERR_INVALID;
+        e = asa::tc_backward(s, Q, K, V, Qidx, Kidx, O32, tau, csr_ptr, csr_idx, cptr, cidx,
+                             rownorm, dO, dQ, dK, dV, w + L.extra, error_word(), st);
+        return cuda_status(e);
+    }
+    e = asa::simt_rowstats(s, Q, K, V, Qidx, Kidx, tau, csr_ptr, csr_idx, dO, invN, accdO, st);
+    if (e == cudaSuccess)
+        e = asa::simt_dq(s, Q, K, V, Qidx, Kidx, tau, csr_ptr, csr_idx, dO, invN, accdO, dQ, st);
+    if (e == cudaSuccess && s.NK)
+        e = asa::simt_dkdv(s, Q, K, V, Qidx, Kidx, tau, cptr, cidx, dO, invN, accdO, dK, dV, st);
+    return cuda_status(e);
+}
+
+int asa_scrub(int dtype, void* x, size_t n, void* ws, asa_stream_t stream) {
+    if ((dtype != ASA_DTYPE_F32 && dtype != ASA_DTYPE_BF16) || (n && !x) || !ws)
+        return ASA_ERR_INVALID;
+    return cuda_status(asa::scrub(dtype, x, n, (int*)ws, (cudaStream_t)stream));
+}
+
+int asa_device_error(asa_stream_t stream, int* code) {
+    if (!code) return ASA_ERR_INVALID;
+    int* w = error_word();
+    if (!w) return ASA_ERR_CUDA;
+    cudaStream_t st = (cudaStream_t)stream;
+    int v = 0;
+    cudaError_t e = cudaMemcpyAsync(&v, w, sizeof(int), cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    if (e == cudaSuccess) e = cudaMemsetAsync(w, 0, sizeof(int), st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    *code = v;
+    return cuda_status(e);
+}
+
+const char* asa_status_string(int status) {
+    switch (status) {
+        case ASA_OK: return "ok";
+        case ASA_ERR_INVALID: return "invalid argument";
+        case ASA_ERR_UNSUPPORTED: return "unsupported configuration";
+        case ASA_ERR_WORKSPACE: return "workspace too small";
+        case ASA_ERR_CUDA: return "CUDA error";
+        case ASA_ERR_DEVICE_TIMEOUT: return "device-side wait timed out";
+        default: return "unknown status";
+    }
+}
+
+int asa_version(void) { return 100; }
+
+}  // extern "C"

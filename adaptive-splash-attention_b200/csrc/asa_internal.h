@@ -1,0 +1,57 @@
+// asa_internal.h -- launch-side declarations shared by the C-ABI translation
+// unit and the kernel translation units.  Not part of the public ABI.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include "asa_device.cuh"
+#include "../../include/asa.h"
+
+namespace asa {
+
+// Everything a kernel needs to know about one call, resolved on the host.
+struct Shape {
+    int BH, NQ, NK, d;
+    int BM, BN, k;
+    int causal;
+    int nQB, nKB;
+    float alpha;     // clamped to [1.05, 3] (reference :547)
+    float am1;       // α - 1
+    float inv_am1b;  // 1/(α-1) as the backward forms it (:499)
+    float scale;
+    PowSpec pinv;    // exponent 1/(α-1)          (:312)
+    PowSpec pe2;     // exponent (2-α)/(α-1)      (:495)
+    long long spins; // bound on device-side waits
+    int in_dtype, out_dtype;
+};
+
+// ---- SIMT kernels (asa_simt.cu) -------------------------------------------
+cudaError_t simt_tau_mask(const Shape& s, const void* Q, const void* K, const int32_t* Qidx,
+                          const int32_t* Kidx, float* tau, uint8_t* M, cudaStream_t st);
+cudaError_t simt_forward(const Shape& s, const void* Q, const void* K, const void* V,
+                         const int32_t* Qidx, const int32_t* Kidx, const float* tau,
+                         const int32_t* ptr, const int32_t* idx, void* O, float* O32,
+                         float* rownorm, cudaStream_t st);
+cudaError_t simt_rowstats(const Shape& s, const void* Q, const void* K, const void* V,
+                          const int32_t* Qidx, const int32_t* Kidx, const float* tau,
+                          const int32_t* ptr, const int32_t* idx, const void* dO,
+                          float* invN, float* accdO, cudaStream_t st);
+cudaError_t simt_dq(const Shape& s, const void* Q, const void* K, const void* V,
+                    const int32_t* Qidx, const int32_t* Kidx, const float* tau,
+                    const int32_t* ptr, const int32_t* idx, const void* dO,
+                    const float* invN, const float* accdO, void* dQ, cudaStream_t st);
+cudaError_t simt_dkdv(const Shape& s, const void* Q, const void* K, const void* V,
+                      const int32_t* Qidx, const int32_t* Kidx, const float* tau,
+                      const int32_t* cptr, const int32_t* cidx, const void* dO,
+                      const float* invN, const float* accdO, void* dK, void* dV,
+                      cudaStream_t st);
+
+// ---- tile lists (asa_compact.cu) --------------------------------------------
+// CSR of M in the reference's format (build_lookup_kernel :219-242), and the
+// transposed list (per key block, the query blocks that use it) the backward
+// walks.  Either output pair may be null.
+cudaError_t build_lists(const Shape& s, const uint8_t* M, int32_t* csr_ptr, int32_t* csr_idx,
+                        int32_t* csc_ptr, int32_t* csc_idx, cudaStream_t st);
+// Device-side version of the reference host scrub (:599-606).
+cudaError_t scrub(int dtype, void* x, size_t n, int* flag, cudaStream_t st);
+
+}  // namespace asa

@@ -1,0 +1,123 @@
+"""splash_attention -- B200 α-entmax block-sparse attention (AdaSplash path).
+
+Drop-in surface of mvideet/Adaptive-Splash-Attention:
+
+* ``AdaptiveSplashAttention(head_dim, alpha, k_keep, adaptive_threshold,
+  sm_scale)`` called as ``attention(Q, K, V, Q_idx, K_idx)`` with autograd
+  backward -- the module the reference's README describes
+  (README.md:100-124; it ships no implementation of it);
+* module-level ``forward(Q, K, V, Q_idx, K_idx, sm_scale, alpha)`` and
+  ``backward(Q, K, V, Q_idx, K_idx, sm_scale, alpha, dOut)`` with the
+  signatures of the reference's pybind module
+  (source/adasplashattention.cu:702-705), using the reference's default
+  build settings (BLOCK_M=32, BLOCK_N=64, K_KEEP=8, :8-19) and its host-side
+  NaN/Inf scrub.
+
+Every computation runs in hand-written CUDA kernels for sm_100a behind the C
+ABI of include/asa.h (libasa.so).  There is no CPU fallback.
+"""
+import torch
+
+from . import _lib
+from .ops import Settings, forward_saved, backward_saved, tau_mask, scrub_, device_error, \
+    resolved_backend, make_params
+
+_lib.lib()  # fail at import time if the native library is missing
+
+__all__ = ["AdaptiveSplashAttention", "splash_attention", "forward", "backward", "tau_mask",
+           "Settings", "device_error"]
+
+# Reference compile-time defaults (adasplashattention.cu:8-19).
+REF_BLOCK_M, REF_BLOCK_N, REF_K_KEEP = 32, 64, 8
+
+
+class _SplashFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, Q, K, V, Q_idx, K_idx, st):
+        O, saved = forward_saved(Q, K, V, Q_idx, K_idx, st,
+                                 need_o32=any(ctx.needs_input_grad[:3]))
+        ctx.saved = saved
+        ctx.save_for_backward(Q, K, V)
+        return O
+
+    @staticmethod
+    def backward(ctx, dO):
+        Q, K, V = ctx.saved_tensors
+        dQ, dK, dV = backward_saved(Q, K, V, dO, ctx.saved)
+        dQ, dK, dV = (g.to(t.dtype) for g, t in zip((dQ, dK, dV), (Q, K, V)))
+        return dQ, dK, dV, None, None, None
+
+
+def splash_attention(Q, K, V, Q_idx=None, K_idx=None, *, alpha=1.5, sm_scale=None, k_keep=8,
+                     block_m=128, block_n=128, causal=True, backend="auto", precision="split",
+                     out_dtype=None):
+    """α-entmax block-sparse attention with autograd.  Q, K, V: [B, H, N, d]
+    float32 or bfloat16 on CUDA; Q_idx / K_idx: positions [B*H, N] (any
+    integer dtype; [N] broadcasts).  Key k is visible to query q iff
+    K_idx[k] <= Q_idx[q] (causal=False: every key)."""
+    st = Settings(alpha=alpha, sm_scale=sm_scale, k_keep=k_keep, block_m=block_m,
+                  block_n=block_n, causal=causal, backend=backend, precision=precision,
+                  out_dtype=out_dtype)
+    return _SplashFn.apply(Q, K, V, Q_idx, K_idx, st)
+
+
+class AdaptiveSplashAttention(torch.nn.Module):
+    """The README's module (README.md:104-124).
+
+    ``adaptive_threshold``: the reference has no implementation of it (the τ
+    solve always runs).  True is accepted and means exactly that; False is
+    rejected because no fixed-threshold semantics exist to reproduce.
+    The module holds no parameters."""
+
+    def __init__(self, head_dim, alpha=1.5, k_keep=8, adaptive_threshold=True, sm_scale=None,
+                 block_m=128, block_n=128, causal=True, backend="auto", precision="split",
+                 out_dtype=None):
+        super().__init__()
+        if not adaptive_threshold:
+            raise ValueError("AdaptiveSplashAttention: adaptive_threshold=False has no "
+                             "reference semantics; only the per-query τ solve exists")
+        if not 1 <= head_dim <= 128:
+            raise ValueError("AdaptiveSplashAttention: head_dim must be in [1, 128]")
+        self.head_dim = head_dim
+        self.alpha = alpha
+        self.k_keep = k_keep
+        self.adaptive_threshold = adaptive_threshold
+        self.sm_scale = sm_scale if sm_scale is not None else head_dim ** -0.5
+        self.block_m, self.block_n = block_m, block_n
+        self.causal = causal
+        self.backend, self.precision, self.out_dtype = backend, precision, out_dtype
+
+    def forward(self, Q, K, V, Q_idx=None, K_idx=None):
+        if Q.shape[-1] != self.head_dim:
+            raise ValueError(f"expected head_dim {self.head_dim}, got {Q.shape[-1]}")
+        return splash_attention(Q, K, V, Q_idx, K_idx, alpha=self.alpha, sm_scale=self.sm_scale,
+                                k_keep=self.k_keep, block_m=self.block_m,
+                                block_n=self.block_n, causal=self.causal, backend=self.backend,
+                                precision=self.precision, out_dtype=self.out_dtype)
+
+    def extra_repr(self):
+        return (f"head_dim={self.head_dim}, alpha={self.alpha}, k_keep={self.k_keep}, "
+                f"sm_scale={self.sm_scale}, block=({self.block_m},{self.block_n}), "
+                f"causal={self.causal}, backend={self.backend}, precision={self.precision}")
+
+
+def _ref_settings(sm_scale, alpha):
+    return Settings(alpha=alpha, sm_scale=sm_scale, k_keep=REF_K_KEEP, block_m=REF_BLOCK_M,
+                    block_n=REF_BLOCK_N, causal=True)
+
+
+def forward(Q, K, V, Q_idx, K_idx, sm_scale, alpha):
+    """Reference pybind ``forward`` (adasplashattention.cu:537-609, :703):
+    returns O in Q's dtype, scrubbed as the reference's host code does."""
+    O, _ = forward_saved(Q, K, V, Q_idx, K_idx, _ref_settings(sm_scale, alpha), need_o32=False)
+    return scrub_(O)
+
+
+def backward(Q, K, V, Q_idx, K_idx, sm_scale, alpha, dOut):
+    """Reference pybind ``backward`` (adasplashattention.cu:611-700, :704):
+    recomputes τ, the mask and the tile lists from scratch, returns
+    [dQ, dK, dV] scrubbed like the reference's host code."""
+    st = _ref_settings(sm_scale, alpha)
+    _, saved = forward_saved(Q, K, V, Q_idx, K_idx, st, need_o32=True)
+    grads = backward_saved(Q, K, V, dOut, saved)
+    return [scrub_(g) for g in grads]

@@ -1,0 +1,216 @@
+"""Tensor-level operations over the C ABI: τ/mask, forward, backward.
+
+All buffers are allocated here with torch (device memory and the current
+stream are torch's); every computation runs in libasa.so's CUDA kernels.
+
+Reference surface mirrored (mvideet/Adaptive-Splash-Attention,
+source/adasplashattention.cu): ``forward(Q, K, V, Q_idx, K_idx, sm_scale,
+alpha)`` (:537-609, :703) and ``backward(Q, K, V, Q_idx, K_idx, sm_scale,
+alpha, dOut)`` (:611-700, :704).
+"""
+import ctypes
+import math
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib as L
+
+
+def _ptr(t):
+    return ctypes.c_void_p(t.data_ptr()) if t is not None else None
+
+
+def _dtype_code(dt):
+    if dt == torch.float32:
+        return L.DTYPE_F32
+    if dt == torch.bfloat16:
+        return L.DTYPE_BF16
+    raise TypeError(f"splash_attention: unsupported dtype {dt} (float32 or bfloat16)")
+
+
+def _torch_dtype(code):
+    return torch.float32 if code == L.DTYPE_F32 else torch.bfloat16
+
+
+@dataclass
+class Settings:
+    """Per-call settings; the reference fixes most of these at compile time
+    (BLOCK_M, BLOCK_N, K_KEEP: adasplashattention.cu:8-19)."""
+    alpha: float = 1.5
+    sm_scale: float = None
+    k_keep: int = 8
+    block_m: int = 128
+    block_n: int = 128
+    causal: bool = True
+    backend: str = "auto"
+    precision: str = "split"
+    out_dtype: torch.dtype = None
+    timeout_spins: int = 0
+
+
+def make_params(Q, K, st: Settings):
+    if Q.dim() != 4 or K.dim() != 4:
+        raise ValueError("splash_attention: Q, K, V must be [B, H, N, d]")
+    B, H, NQ, d = Q.shape
+    NK = K.shape[2]
+    if K.shape[0] != B or K.shape[1] != H or K.shape[3] != d:
+        raise ValueError("splash_attention: K must be [B, H, NK, d] matching Q")
+    p = L.Params()
+    L.lib().asa_params_default(ctypes.byref(p))
+    p.B, p.H, p.NQ, p.NK, p.d = B, H, NQ, NK, d
+    p.block_m, p.block_n, p.k_keep = int(st.block_m), int(st.block_n), int(st.k_keep)
+    p.alpha = float(st.alpha)
+    p.sm_scale = float(st.sm_scale if st.sm_scale is not None else 1.0 / math.sqrt(d))
+    p.causal = 1 if st.causal else 0
+    p.in_dtype = _dtype_code(Q.dtype)
+    p.out_dtype = _dtype_code(st.out_dtype if st.out_dtype is not None else Q.dtype)
+    p.backend = L.BACKEND[st.backend]
+    p.precision = L.PRECISION[st.precision]
+    p.timeout_spins = int(st.timeout_spins)
+    return p
+
+
+def resolved_backend(p):
+    b = L.lib().asa_resolve_backend(ctypes.byref(p))
+    if b < 0:
+        L.check(-b, "asa_resolve_backend")
+    return L.BACKEND_NAME[b]
+
+
+def _workspace(p, device):
+    fwd = ctypes.c_size_t()
+    bwd = ctypes.c_size_t()
+    L.check(L.lib().asa_workspace_bytes(ctypes.byref(p), ctypes.byref(fwd), ctypes.byref(bwd)),
+            "asa_workspace_bytes")
+    return fwd.value, bwd.value
+
+
+def _index(idx, BH, N, device, name):
+    """Position indices as contiguous int32 [B*H, N] (the reference requires
+    int32 [B*H, N], :571-572; the README passes int64 arange, so it is cast)."""
+    if idx is None:
+        raise ValueError(f"splash_attention: {name} is required when causal=True")
+    if not isinstance(idx, torch.Tensor):
+        idx = torch.as_tensor(idx)
+    idx = idx.to(device=device)
+    if idx.dim() == 1:
+        idx = idx.unsqueeze(0).expand(BH, N)
+    idx = idx.reshape(BH, N)
+    if idx.dtype != torch.int32:
+        idx = idx.to(torch.int32)
+    return idx.contiguous()
+
+
+def _check_inputs(*ts):
+    dev = ts[0].device
+    if dev.type != "cuda":
+        raise RuntimeError("splash_attention: tensors must be on a CUDA device")  # reference :543
+    for t in ts:
+        if t is not None and t.device != dev:
+            raise RuntimeError("splash_attention: all tensors must be on the same device")
+
+
+def _stream():
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+class Saved:
+    """What the forward hands the backward: τ, the block mask and its CSR,
+    Σp per query and the fp32 output."""
+    __slots__ = ("tau", "M", "csr_ptr", "csr_idx", "rownorm", "O32", "params")
+
+
+def tau_mask(Q, K, Q_idx, K_idx, st: Settings):
+    """τ [B*H, NQ] fp32, block mask M uint8 [B*H, nQB, nKB], CSR (ptr, idx)."""
+    _check_inputs(Q, K)
+    Q, K = Q.contiguous(), K.contiguous()
+    p = make_params(Q, K, st)
+    BH = p.B * p.H
+    nQB = -(-p.NQ // p.block_m)
+    nKB = -(-p.NK // p.block_n)
+    dev = Q.device
+    qi = _index(Q_idx, BH, p.NQ, dev, "Q_idx") if st.causal else None
+    ki = _index(K_idx, BH, p.NK, dev, "K_idx") if st.causal else None
+    tau = torch.empty(BH, p.NQ, device=dev, dtype=torch.float32)
+    M = torch.empty(BH, nQB, nKB, device=dev, dtype=torch.uint8)
+    ptr = torch.empty(BH, nQB + 1, device=dev, dtype=torch.int32)
+    idx = torch.empty(BH, nQB * nKB, device=dev, dtype=torch.int32)
+    fwd, _ = _workspace(p, dev)
+    ws = torch.empty(fwd, device=dev, dtype=torch.uint8)
+    L.check(L.lib().asa_tau_mask(ctypes.byref(p), _ptr(Q), _ptr(K), _ptr(qi), _ptr(ki), _ptr(tau),
+                                 _ptr(M), _ptr(ptr), _ptr(idx), _ptr(ws), fwd, _stream()),
+            "asa_tau_mask")
+    return tau, M, ptr, idx
+
+
+def forward_saved(Q, K, V, Q_idx, K_idx, st: Settings, need_o32=True):
+    """Forward pass; returns (O, Saved)."""
+    _check_inputs(Q, K, V)
+    Q, K, V = Q.contiguous(), K.contiguous(), V.contiguous()
+    if V.shape != K.shape or V.dtype != Q.dtype or K.dtype != Q.dtype:
+        raise ValueError("splash_attention: V must match K in shape and Q in dtype")
+    p = make_params(Q, K, st)
+    BH = p.B * p.H
+    nQB = -(-p.NQ // p.block_m)
+    nKB = -(-p.NK // p.block_n)
+    dev = Q.device
+    qi = _index(Q_idx, BH, p.NQ, dev, "Q_idx") if st.causal else None
+    ki = _index(K_idx, BH, p.NK, dev, "K_idx") if st.causal else None
+    out_dt = _torch_dtype(p.out_dtype)
+    O = torch.empty(p.B, p.H, p.NQ, p.d, device=dev, dtype=out_dt)
+    if out_dt == torch.float32:
+        O32 = O
+    else:
+        O32 = torch.empty(p.B, p.H, p.NQ, p.d, device=dev, dtype=torch.float32) if need_o32 else None
+    s = Saved()
+    s.tau = torch.empty(BH, p.NQ, device=dev, dtype=torch.float32)
+    s.M = torch.empty(BH, nQB, nKB, device=dev, dtype=torch.uint8)
+    s.csr_ptr = torch.empty(BH, nQB + 1, device=dev, dtype=torch.int32)
+    s.csr_idx = torch.empty(BH, nQB * nKB, device=dev, dtype=torch.int32)
+    s.rownorm = torch.empty(BH, p.NQ, device=dev, dtype=torch.float32)
+    s.O32 = O32
+    s.params = (p, qi, ki)
+    fwd, _ = _workspace(p, dev)
+    ws = torch.empty(fwd, device=dev, dtype=torch.uint8)
+    L.check(L.lib().asa_forward(ctypes.byref(p), _ptr(Q), _ptr(K), _ptr(V), _ptr(qi), _ptr(ki),
+                                _ptr(O), _ptr(O32), _ptr(s.tau), _ptr(s.M), _ptr(s.csr_ptr),
+                                _ptr(s.csr_idx), _ptr(s.rownorm), _ptr(ws), fwd, _stream()),
+            "asa_forward")
+    return O, s
+
+
+def backward_saved(Q, K, V, dO, s: Saved):
+    """Backward from a forward's Saved state; returns (dQ, dK, dV)."""
+    p, qi, ki = s.params
+    Q, K, V = Q.contiguous(), K.contiguous(), V.contiguous()
+    dO = dO.to(Q.dtype).contiguous()
+    dev = Q.device
+    out_dt = _torch_dtype(p.out_dtype)
+    dQ = torch.empty(Q.shape, device=dev, dtype=out_dt)
+    dK = torch.empty(K.shape, device=dev, dtype=out_dt)
+    dV = torch.empty(V.shape, device=dev, dtype=out_dt)
+    _, bwd = _workspace(p, dev)
+    ws = torch.empty(bwd, device=dev, dtype=torch.uint8)
+    L.check(L.lib().asa_backward(ctypes.byref(p), _ptr(Q), _ptr(K), _ptr(V), _ptr(qi), _ptr(ki),
+                                 _ptr(s.O32), _ptr(s.tau), _ptr(s.M), _ptr(s.csr_ptr),
+                                 _ptr(s.csr_idx), _ptr(s.rownorm), _ptr(dO), _ptr(dQ), _ptr(dK),
+                                 _ptr(dV), _ptr(ws), bwd, _stream()),
+            "asa_backward")
+    return dQ, dK, dV
+
+
+def scrub_(x):
+    """In-place device version of the reference's host scrub (:599-606)."""
+    ws = torch.empty(16, device=x.device, dtype=torch.uint8)
+    L.check(L.lib().asa_scrub(_dtype_code(x.dtype), _ptr(x), x.numel(), _ptr(ws), _stream()),
+            "asa_scrub")
+    return x
+
+
+def device_error(device=None):
+    """Read and clear the device error word (bounded waits that ran out)."""
+    code = ctypes.c_int()
+    with torch.cuda.device(device):
+        L.check(L.lib().asa_device_error(_stream(), ctypes.byref(code)), "asa_device_error")
+    return code.value

@@ -1,0 +1,64 @@
+"""Shared helpers for the parity tests: seeded inputs, oracle runs, engine
+runs and the tolerances the tests assert."""
+import numpy as np
+import torch
+
+from oracle import oracle as orc
+
+INT32_MAX = 2 ** 31 - 1
+
+# Tolerances (north_star): τ within 1e-5 relative; O/dQ/dK/dV within 1e-5
+# max-abs for fp32 inputs and 1e-3 max-abs for bf16 inputs; block mask and
+# tile lists bit-exact.
+TAU_RTOL, TAU_ATOL = 1e-5, 1e-6
+OUT_ATOL = {torch.float32: 1e-5, torch.bfloat16: 1e-3}
+
+
+def make_inputs(B, H, NQ, NK, d, seed=0, sigma=1.0, dtype=torch.float32, causal=True, qoff=0,
+                centroids=0):
+    g = torch.Generator().manual_seed(seed)
+    Q = torch.randn(B, H, NQ, d, generator=g) * sigma
+    K = torch.randn(B, H, NK, d, generator=g) * sigma
+    V = torch.randn(B, H, NK, d, generator=g)
+    dO = torch.randn(B, H, NQ, d, generator=g)
+    if centroids:
+        cent = 2.0 * torch.randn(centroids, d, generator=g)
+        c = (torch.arange(NK) * centroids) // NK
+        K = K + cent[c]
+    Q, K, V, dO = (x.to(dtype) for x in (Q, K, V, dO))
+    BH = B * H
+    Qi = (torch.arange(NQ, dtype=torch.int32) + qoff).expand(BH, NQ).contiguous()
+    Ki = torch.arange(NK, dtype=torch.int32).expand(BH, NK).contiguous()
+    return Q, K, V, dO, Qi, Ki
+
+
+def oracle_run(Q, K, V, dO, Qi, Ki, BM, BN, k_keep, alpha, sm_scale, causal=True, grads=True):
+    B, H, NQ, d = Q.shape
+    NK = K.shape[2]
+    cfg = orc.Config(B * H, NQ, NK, d, BM, BN, k_keep, alpha, sm_scale, causal)
+    f = lambda x: x.float().reshape(x.shape[0] * x.shape[1], x.shape[2], x.shape[3]).numpy()
+    return orc.run_all(cfg, f(Q), f(K), f(V), Qi.numpy(), Ki.numpy(),
+                       f(dO) if grads else None)
+
+
+def assert_tau(got, ref):
+    got, ref = np.asarray(got, np.float64), np.asarray(ref, np.float64)
+    err = np.abs(got - ref) - (TAU_ATOL + TAU_RTOL * np.abs(ref))
+    bad = int((err > 0).sum())
+    assert bad == 0, f"τ: {bad} rows outside rtol {TAU_RTOL}; worst excess {err.max():.3g}"
+
+
+def assert_close(name, got, ref, atol):
+    got = np.asarray(got, np.float64)
+    ref = np.asarray(ref, np.float64)
+    assert got.shape == ref.shape, (name, got.shape, ref.shape)
+    err = np.abs(got - ref).max() if got.size else 0.0
+    assert err <= atol, f"{name}: max-abs error {err:.3g} > {atol:g}"
+
+
+def csr_equal(ptr, idx, rptr, ridx):
+    ptr, idx, rptr, ridx = (np.asarray(x) for x in (ptr, idx, rptr, ridx))
+    assert np.array_equal(ptr, rptr), "CSR ptr differs"
+    for b in range(ptr.shape[0]):
+        n = ptr[b, -1]
+        assert np.array_equal(idx[b, :n], ridx[b, :n]), f"CSR idx differs in row {b}"
