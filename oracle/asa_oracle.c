@@ -39,6 +39,7 @@ typedef struct {
     float alpha;     /* entmax alpha (clamped to [1.05, 3] inside)    */
     float sm_scale;  /* score scale                                   */
     int causal;      /* 0 => every key visible (reference: Q_idx = INT32_MAX) */
+    int ref_tile_load; /* 1 => reproduce the reference's tile-load zeroing (below) */
 } asa_oracle_cfg;
 
 static float clamp_alpha(float a) {            /* adasplashattention.cu:52, :547 */
@@ -64,6 +65,33 @@ static float score(const asa_oracle_cfg* c, const float* q, const float* k) {
     s = fmaxf(s, -10.0f);                      /* :196 */
     s = fminf(s, 10.0f);                       /* :197 */
     return s;
+}
+
+/* The reference stages each K (and V) tile in shared memory with one
+ * thread per query of the query block, and each loading thread zeroes the
+ * elements of keys that ITS OWN query cannot see:
+ *   Ktile[x] = (K_idx[kn] <= seq_q_of_loader) ? K[kn][dim] : 0
+ * with x = col*d + dim, loader thread x % BLOCK_M, i.e. loader query
+ * qb*BLOCK_M + (x % BLOCK_M)  (adasplashattention.cu:176-183, 285-294,
+ * 398-406, 442-450).  Consumers then skip only the keys invisible to
+ * themselves (:187-189), so a visible key's row may be read with some
+ * elements zeroed.  This reproduces that: row_of() returns key kn's row as
+ * the consumers of query block qb see it.  A loader query >= NQ belongs to
+ * a thread that exited before loading (:156-158, :258, :368); the
+ * reference then reads stale shared memory, which cannot be reproduced, and
+ * here such an element is taken as loaded. */
+static const float* row_of(const asa_oracle_cfg* c, const float* src, int bh, int qb, int kn,
+                           const int32_t* Qidx, const int32_t* Kidx, float* buf) {
+    const float* r = src + ((size_t)bh * c->NK + kn) * c->d;
+    if (!c->ref_tile_load || !c->causal) return r;
+    const int col = kn % c->BN;
+    const int kpos = Kidx[(size_t)bh * c->NK + kn];
+    for (int t = 0; t < c->d; ++t) {
+        const int lq = qb * c->BM + (int)(((long long)col * c->d + t) % c->BM);
+        const int keep = lq >= c->NQ || kpos <= Qidx[(size_t)bh * c->NQ + lq];
+        buf[t] = keep ? r[t] : 0.0f;
+    }
+    return buf;
 }
 
 /* adasplashattention.cu:35-49: descending list, strict '>' so the earlier
@@ -148,13 +176,14 @@ void asa_oracle_tau_mask(const asa_oracle_cfg* c, const float* Q, const float* K
     for (int bh = 0; bh < c->BH; ++bh) {
         for (int q = 0; q < c->NQ; ++q) {
             float vals[ASA_KMAX]; int inds[ASA_KMAX];
+            float kbuf[512];
             for (int i = 0; i < k; ++i) { vals[i] = -1e6f; inds[i] = -1; }   /* :166-172 */
             const size_t qi = (size_t)bh * c->NQ + q;
             const float* qrow = Q + qi * c->d;
             const int qpos = Qidx[qi];
             for (int kn = 0; kn < c->NK; ++kn) {
                 if (!visible(c, qpos, Kidx[(size_t)bh * c->NK + kn])) continue;
-                float s = score(c, qrow, K + ((size_t)bh * c->NK + kn) * c->d);
+                float s = score(c, qrow, row_of(c, K, bh, q / c->BM, kn, Qidx, Kidx, kbuf));
                 insert_topk(s, kn, vals, inds, k);
             }
             tau[qi] = asa_oracle_entmax_tau(vals, k, alpha);
@@ -226,11 +255,12 @@ static float row_accumulate(const asa_oracle_cfg* c, int bh, int q,
             if (kn >= c->NK) break;
             const size_t ki = (size_t)bh * c->NK + kn;
             if (!visible(c, qpos, Kidx[ki])) continue;
-            float s = score(c, qrow, K + ki * c->d);
+            float kbuf[512], vbuf[512];
+            float s = score(c, qrow, row_of(c, K, bh, qb, kn, Qidx, Kidx, kbuf));
             float u = fmaf(am1, s, -tq);
             float pr = entmax_p(u, inv);
             n += pr;
-            const float* v = V + ki * c->d;
+            const float* v = row_of(c, V, bh, qb, kn, Qidx, Kidx, vbuf);
             for (int t = 0; t < c->d; ++t) acc[t] = fmaf(pr, v[t], acc[t]);
         }
     }
@@ -348,10 +378,11 @@ void asa_oracle_backward(const asa_oracle_cfg* c, const float* Q, const float* K
                     if (kn >= c->NK) break;
                     const size_t ki = (size_t)bh * c->NK + kn;
                     if (!visible(c, qpos, Kidx[ki])) continue;
-                    float pr;
-                    float gs = pair_grad(c, Q + qi * d, K + ki * d, V + ki * d, dO + qi * d,
+                    float pr, kbuf[512], vbuf[512];
+                    const float* kr = row_of(c, K, bh, qb, kn, Qidx, Kidx, kbuf);
+                    const float* vr = row_of(c, V, bh, qb, kn, Qidx, Kidx, vbuf);
+                    float gs = pair_grad(c, Q + qi * d, kr, vr, dO + qi * d,
                                          tau[qi], invN[qi], accdO[qi], &pr);
-                    const float* kr = K + ki * d;
                     for (int t = 0; t < d; ++t) {
                         float v = gs * kr[t] * c->sm_scale;
                         if (isfinite(v)) dq[t] += v;
@@ -374,8 +405,10 @@ void asa_oracle_backward(const asa_oracle_cfg* c, const float* Q, const float* K
                 const size_t qi = (size_t)bh * c->NQ + q;
                 if (!active[((size_t)bh * nQB + q / c->BM) * nKB + kb]) continue;
                 if (!visible(c, Qidx[qi], kpos)) continue;
-                float pr;
-                float gs = pair_grad(c, Q + qi * d, K + ki * d, V + ki * d, dO + qi * d,
+                float pr, kbuf[512], vbuf[512];
+                const float* kr = row_of(c, K, bh, q / c->BM, kn, Qidx, Kidx, kbuf);
+                const float* vr = row_of(c, V, bh, q / c->BM, kn, Qidx, Kidx, vbuf);
+                float gs = pair_grad(c, Q + qi * d, kr, vr, dO + qi * d,
                                      tau[qi], invN[qi], accdO[qi], &pr);
                 const float pb = pr * invN[qi];
                 const float* g = dO + qi * d;

@@ -16,7 +16,8 @@ class _Cfg(ctypes.Structure):
     _fields_ = [("BH", ctypes.c_int), ("NQ", ctypes.c_int), ("NK", ctypes.c_int),
                 ("d", ctypes.c_int), ("BM", ctypes.c_int), ("BN", ctypes.c_int),
                 ("k_keep", ctypes.c_int), ("alpha", ctypes.c_float),
-                ("sm_scale", ctypes.c_float), ("causal", ctypes.c_int)]
+                ("sm_scale", ctypes.c_float), ("causal", ctypes.c_int),
+                ("ref_tile_load", ctypes.c_int)]
 
 
 _lib = None
@@ -51,18 +52,20 @@ class Config:
     fields here."""
 
     def __init__(self, BH, NQ, NK, d, BM=128, BN=128, k_keep=8, alpha=1.5, sm_scale=None,
-                 causal=True):
+                 causal=True, ref_tile_load=True):
         self.BH, self.NQ, self.NK, self.d = int(BH), int(NQ), int(NK), int(d)
         self.BM, self.BN, self.k_keep = int(BM), int(BN), int(k_keep)
         self.alpha = float(alpha)
         self.sm_scale = float(sm_scale if sm_scale is not None else d ** -0.5)
         self.causal = bool(causal)
+        # reproduce the reference's tile-load zeroing (asa_oracle.c row_of)
+        self.ref_tile_load = bool(ref_tile_load)
         self.nQB = -(-self.NQ // self.BM)
         self.nKB = -(-self.NK // self.BN)
 
     def c(self):
         return _Cfg(self.BH, self.NQ, self.NK, self.d, self.BM, self.BN, self.k_keep,
-                    self.alpha, self.sm_scale, int(self.causal))
+                    self.alpha, self.sm_scale, int(self.causal), int(self.ref_tile_load))
 
 
 def _f32(a):

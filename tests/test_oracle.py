@@ -94,7 +94,7 @@ def test_backward_is_fixed_tau_gradient(alpha):
     B, H, N, d, BM, BN = 1, 2, 96, 16, 32, 32
     Q, K, V, dO, Qi, Ki = make_inputs(B, H, N, N, d, seed=5, sigma=0.7)
     sc = 0.3
-    r = oracle_run(Q, K, V, dO, Qi, Ki, BM, BN, 8, alpha, sc)
+    r = oracle_run(Q, K, V, dO, Qi, Ki, BM, BN, 8, alpha, sc, ref_tile_load=False)
     tau = torch.from_numpy(r["tau"]).double()
     act = torch.from_numpy(r["M"]).bool()
     q, k, v = (x.double().reshape(B * H, N, d).requires_grad_() for x in (Q, K, V))
@@ -113,7 +113,7 @@ def test_backward_is_fixed_tau_gradient(alpha):
 
 def test_forward_matches_dense_restatement():
     Q, K, V, dO, Qi, Ki = make_inputs(1, 2, 160, 160, 32, seed=7)
-    r = oracle_run(Q, K, V, dO, Qi, Ki, 32, 64, 8, 1.5, 0.2, grads=False)
+    r = oracle_run(Q, K, V, dO, Qi, Ki, 32, 64, 8, 1.5, 0.2, grads=False, ref_tile_load=False)
     BH, N, d = 2, 160, 32
     q, k, v = (x.double().reshape(BH, N, d) for x in (Q, K, V))
     s = torch.clamp(q @ k.transpose(1, 2) * 0.2, -10, 10)
