@@ -93,6 +93,7 @@ Shape make_shape(const asa_params* p) {
     s.spins = p->timeout_spins > 0 ? p->timeout_spins : (1LL << 26);
     s.in_dtype = p->in_dtype;
     s.out_dtype = p->out_dtype;
+    s.ref_load = (p->ref_tile_load && p->causal) ? 1 : 0;
     return s;
 }
 
@@ -144,6 +145,7 @@ void asa_params_default(asa_params* p) {
     p->out_dtype = ASA_DTYPE_BF16;
     p->backend = ASA_BACKEND_AUTO;
     p->precision = ASA_PREC_SPLIT;
+    p->ref_tile_load = 1;
 }
 
 int asa_resolve_backend(const asa_params* p) {

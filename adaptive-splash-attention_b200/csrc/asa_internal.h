@@ -22,7 +22,20 @@ struct Shape {
     PowSpec pe2;     // exponent (2-α)/(α-1)      (:495)
     long long spins; // bound on device-side waits
     int in_dtype, out_dtype;
+    int ref_load;    // reproduce the reference's tile-load zeroing (causal only)
 };
+
+// Whether element `t` of key row `kn` survives the reference's tile staging
+// for consumers in query block `qb`: the reference thread that stages it
+// serves query qb*BM + ((kn % BN)*d + t) % BM and zeroes it when that query
+// cannot see the key (source/adasplashattention.cu:176-183, :285-294,
+// :398-406, :442-450).  A staging query >= NQ has no reference thread (it
+// exits first, :156-158); the element is then kept.
+__device__ __forceinline__ bool ref_keep(const Shape& s, const int32_t* __restrict__ Qidx_bh,
+                                         int qb, int kn, int t, int kpos) {
+    const int lq = qb * s.BM + (int)(((long long)(kn % s.BN) * s.d + t) % s.BM);
+    return lq >= s.NQ || kpos <= __ldg(Qidx_bh + lq);
+}
 
 // ---- SIMT kernels (asa_simt.cu) -------------------------------------------
 cudaError_t simt_tau_mask(const Shape& s, const void* Q, const void* K, const int32_t* Qidx,

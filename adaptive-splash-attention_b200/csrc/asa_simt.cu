@@ -24,6 +24,48 @@ constexpr int QTHREADS = 128;
 // key (K staged 32 rows at a time in shared memory, read as broadcasts).
 // Reference: build_mask_kernel :150-217.
 // ---------------------------------------------------------------------------
+// Smallest query position in query block qb (the reference's tile-load
+// zeroing can only touch keys whose position exceeds it).
+__device__ __forceinline__ int block_qmin(const Shape& sh, const int32_t* __restrict__ Qidx_bh,
+                                          int qb, int* red) {
+    int m = INT_MAX;
+    for (int i = threadIdx.x; i < sh.BM && qb * sh.BM + i < sh.NQ; i += blockDim.x)
+        m = min(m, Qidx_bh[qb * sh.BM + i]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = min(m, __shfl_xor_sync(0xffffffffu, m, o));
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+    __syncthreads();
+    int r = red[0];
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w) r = min(r, red[w]);
+    return r;
+}
+
+__device__ __forceinline__ int block_qmax(int v, int* red) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = max(v, __shfl_xor_sync(0xffffffffu, v, o));
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    int r = red[0];
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w) r = max(r, red[w]);
+    return r;
+}
+
+// Threads per CTA for query-major kernels: the CTA covers (part of) one
+// query block so all its queries share one tile list and one tile staging.
+inline int qthreads(int BM) {
+    int t = BM < QTHREADS ? BM : QTHREADS;
+    return (t + 31) / 32 * 32;
+}
+
+// ---------------------------------------------------------------------------
+// τ / block mask.  One thread per query; the CTA's queries (one query
+// block, or a 128-query part of it) stream every key, K staged 32 rows at a
+// time in shared memory and read as broadcasts.  The staging reproduces the
+// reference's tile-load zeroing when sh.ref_load is set.
+// Reference: build_mask_kernel :150-217.
+// ---------------------------------------------------------------------------
 template <typename T, int DM, int KM>
 __global__ void __launch_bounds__(QTHREADS)
 simt_tau_mask_kernel(Shape sh, const T* __restrict__ Q, const T* __restrict__ K,
@@ -32,34 +74,28 @@ simt_tau_mask_kernel(Shape sh, const T* __restrict__ Q, const T* __restrict__ K,
     __shared__ float Ks[KT][DM];
     __shared__ int Kp[KT];
     __shared__ int red[QTHREADS / 32];
+    const int QT = blockDim.x;
     const int tid = threadIdx.x;
     const int bh = blockIdx.y;
-    const int q = blockIdx.x * QTHREADS + tid;
-    const bool qv = q < sh.NQ;
+    const int subs = (sh.BM + QT - 1) / QT;
+    const int qb = blockIdx.x / subs;
+    const int inblk = (blockIdx.x % subs) * QT + tid;
+    const int q = qb * sh.BM + inblk;
+    const bool qv = inblk < sh.BM && q < sh.NQ;
     const int d = sh.d;
     const size_t qrow = (size_t)bh * sh.NQ + (qv ? q : 0);
+    const int32_t* Qidx_bh = Qidx + (size_t)bh * sh.NQ;
 
     float qr[DM];
 #pragma unroll
     for (int t = 0; t < DM; ++t) qr[t] = (qv && t < d) ? to_f(Q[qrow * d + t]) : 0.0f;
     const int qpos = !qv ? INT_MIN : (sh.causal ? Qidx[qrow] : INT_MAX);
-
-    int m = qpos;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
-    if ((tid & 31) == 0) red[tid >> 5] = m;
-    __syncthreads();
-    int cta_max = red[0];
-#pragma unroll
-    for (int w = 1; w < QTHREADS / 32; ++w) cta_max = max(cta_max, red[w]);
+    const int cta_max = block_qmax(qpos, red);
+    const int qmin = sh.ref_load ? block_qmin(sh, Qidx_bh, qb, red) : INT_MAX;
 
     TopK<KM> tk;
     tk.init(sh.k);
     for (int start = 0; start < sh.NK; start += KT) {
-        for (int x = tid; x < KT * DM; x += QTHREADS) {
-            const int j = x / DM, t = x % DM, kn = start + j;
-            Ks[j][t] = (kn < sh.NK && t < d) ? to_f(K[((size_t)bh * sh.NK + kn) * d + t]) : 0.0f;
-        }
         int any = 0;
         if (tid < KT) {
             const int kn = start + tid;
@@ -68,6 +104,13 @@ simt_tau_mask_kernel(Shape sh, const T* __restrict__ Q, const T* __restrict__ K,
             any = (kn < sh.NK) && kp <= cta_max;
         }
         if (!__syncthreads_or(any)) continue;
+        for (int x = tid; x < KT * DM; x += QT) {
+            const int j = x / DM, t = x % DM, kn = start + j;
+            bool ok = kn < sh.NK && t < d;
+            if (ok && sh.ref_load && Kp[j] > qmin) ok = ref_keep(sh, Qidx_bh, qb, kn, t, Kp[j]);
+            Ks[j][t] = ok ? to_f(K[((size_t)bh * sh.NK + kn) * d + t]) : 0.0f;
+        }
+        __syncthreads();
         if (qv) {
             for (int j = 0; j < KT; j += 2) {
                 const int kn0 = start + j, kn1 = kn0 + 1;
@@ -96,18 +139,12 @@ simt_tau_mask_kernel(Shape sh, const T* __restrict__ Q, const T* __restrict__ K,
     }
     if (!qv) return;
     tau[qrow] = ref_tau<KM>(tk.v, sh.k, sh.alpha);
-    const size_t base = ((size_t)bh * sh.nQB + q / sh.BM) * sh.nKB;
+    const size_t base = ((size_t)bh * sh.nQB + qb) * sh.nKB;
 #pragma unroll
     for (int j = 0; j < KM; ++j)
         if (tk.i[j] >= 0) M[base + tk.i[j] / sh.BN] = 1;   // same-value writes, as :215
 }
 
-// Threads per CTA for query-major kernels: the CTA covers (part of) one
-// query block so all its queries share one tile list.
-inline int qthreads(int BM) {
-    int t = BM < QTHREADS ? BM : QTHREADS;
-    return (t + 31) / 32 * 32;
-}
 
 // ---------------------------------------------------------------------------
 // Query-major walk over a query block's active tiles (CSR order, keys
@@ -143,6 +180,9 @@ simt_rows_kernel(Shape sh, const T* __restrict__ Q, const T* __restrict__ K,
     float* Ks = gs_ + (MODE == 2 ? QT * LD : 0);
     float* Vs = Ks + KT * DM;
     __shared__ int Kp[KT];
+    __shared__ int red[QTHREADS / 32];
+    const int32_t* Qidx_bh = Qidx + (size_t)bh * sh.NQ;
+    const int qmin = sh.ref_load ? block_qmin(sh, Qidx_bh, qb, red) : INT_MAX;
 
     for (int t = 0; t < DM; ++t) {
         qs[tid * LD + t] = (qv && t < d) ? to_f(Q[qrow * d + t]) : 0.0f;
@@ -167,17 +207,19 @@ simt_rows_kernel(Shape sh, const T* __restrict__ Q, const T* __restrict__ K,
         for (int c0 = 0; c0 < sh.BN; c0 += KT) {
             const int cn = min(KT, sh.BN - c0);
             __syncthreads();
-            for (int x = tid; x < KT * DM; x += QT) {
-                const int j = x / DM, t = x % DM, kn = start + c0 + j;
-                const bool ok = j < cn && kn < sh.NK && t < d;
-                const size_t off = ((size_t)bh * sh.NK + kn) * d + t;
-                Ks[j * DM + t] = ok ? to_f(K[off]) : 0.0f;
-                Vs[j * DM + t] = ok ? to_f(V[off]) : 0.0f;
-            }
             if (tid < KT) {
                 const int kn = start + c0 + tid;
                 Kp[tid] = (tid < cn && kn < sh.NK)
                               ? (sh.causal ? Kidx[(size_t)bh * sh.NK + kn] : INT_MIN) : INT_MAX;
+            }
+            __syncthreads();
+            for (int x = tid; x < KT * DM; x += QT) {
+                const int j = x / DM, t = x % DM, kn = start + c0 + j;
+                bool ok = j < cn && kn < sh.NK && t < d;
+                if (ok && sh.ref_load && Kp[j] > qmin) ok = ref_keep(sh, Qidx_bh, qb, kn, t, Kp[j]);
+                const size_t off = ((size_t)bh * sh.NK + kn) * d + t;
+                Ks[j * DM + t] = ok ? to_f(K[off]) : 0.0f;
+                Vs[j * DM + t] = ok ? to_f(V[off]) : 0.0f;
             }
             __syncthreads();
             if (!qv) continue;
@@ -285,6 +327,7 @@ simt_dkdv_kernel(Shape sh, const T* __restrict__ Q, const T* __restrict__ K,
     float* Gc = Qc + QC * DM;       // [QC][DM]
     __shared__ float tq_s[QC], in_s[QC], ad_s[QC];
     __shared__ int qp_s[QC];
+    __shared__ int red[QTHREADS / 32];
 
     for (int t = 0; t < DM; ++t) {
         ks[tid * LD + t] = (kv && t < d) ? to_f(K[krow * d + t]) : 0.0f;
@@ -300,8 +343,24 @@ simt_dkdv_kernel(Shape sh, const T* __restrict__ Q, const T* __restrict__ K,
     const int32_t* cp = cptr + (size_t)bh * (sh.nKB + 1);
     const int32_t* cx = cidx + (size_t)bh * sh.nKB * sh.nQB;
     const int e0 = cp[kb], e1 = cp[kb + 1];
+    const int32_t* Qidx_bh = Qidx + (size_t)bh * sh.NQ;
+    bool dirty = false;
     for (int e = e0; e < e1; ++e) {
         const int qb = cx[e];
+        // rows as the consumers of query block qb see them (reference tile-load
+        // zeroing); rebuilt only when this key can be touched by it
+        const int qmin = sh.ref_load ? block_qmin(sh, Qidx_bh, qb, red) : INT_MAX;
+        if (kv) {
+            const bool need = sh.ref_load && kpos > qmin;
+            if (need || dirty) {
+                for (int t = 0; t < DM; ++t) {
+                    const bool keep = t < d && (!need || ref_keep(sh, Qidx_bh, qb, kn, t, kpos));
+                    ks[tid * LD + t] = keep ? to_f(K[krow * d + t]) : 0.0f;
+                    vs[tid * LD + t] = keep ? to_f(V[krow * d + t]) : 0.0f;
+                }
+                dirty = need;
+            }
+        }
         const int q0 = qb * sh.BM;
         const int qend = min(q0 + sh.BM, sh.NQ);
         for (int c0 = q0; c0 < qend; c0 += QC) {
@@ -399,8 +458,9 @@ cudaError_t set_smem(F* f, size_t bytes) {
 template <typename T, int DM, int KM>
 cudaError_t launch_tau_mask(const Shape& s, const void* Q, const void* K, const int32_t* Qidx,
                             const int32_t* Kidx, float* tau, uint8_t* M, cudaStream_t st) {
-    dim3 grid((s.NQ + QTHREADS - 1) / QTHREADS, s.BH);
-    simt_tau_mask_kernel<T, DM, KM><<<grid, QTHREADS, 0, st>>>(
+    const int QT = qthreads(s.BM);
+    dim3 grid(s.nQB * ((s.BM + QT - 1) / QT), s.BH);
+    simt_tau_mask_kernel<T, DM, KM><<<grid, QT, 0, st>>>(
         s, (const T*)Q, (const T*)K, Qidx, Kidx, tau, M);
     return cudaGetLastError();
 }

@@ -50,14 +50,19 @@ class _SplashFn(torch.autograd.Function):
 
 def splash_attention(Q, K, V, Q_idx=None, K_idx=None, *, alpha=1.5, sm_scale=None, k_keep=8,
                      block_m=128, block_n=128, causal=True, backend="auto", precision="split",
-                     out_dtype=None):
+                     out_dtype=None, ref_tile_load=True):
     """α-entmax block-sparse attention with autograd.  Q, K, V: [B, H, N, d]
     float32 or bfloat16 on CUDA; Q_idx / K_idx: positions [B*H, N] (any
     integer dtype; [N] broadcasts).  Key k is visible to query q iff
-    K_idx[k] <= Q_idx[q] (causal=False: every key)."""
+    K_idx[k] <= Q_idx[q] (causal=False: every key).
+
+    ref_tile_load=True reproduces the reference kernels' tile staging, in
+    which a visible key's K/V elements are zeroed when the reference thread
+    that loads them serves a query that cannot see the key; False reads every
+    visible key in full."""
     st = Settings(alpha=alpha, sm_scale=sm_scale, k_keep=k_keep, block_m=block_m,
                   block_n=block_n, causal=causal, backend=backend, precision=precision,
-                  out_dtype=out_dtype)
+                  out_dtype=out_dtype, ref_tile_load=ref_tile_load)
     return _SplashFn.apply(Q, K, V, Q_idx, K_idx, st)
 
 
@@ -71,7 +76,7 @@ class AdaptiveSplashAttention(torch.nn.Module):
 
     def __init__(self, head_dim, alpha=1.5, k_keep=8, adaptive_threshold=True, sm_scale=None,
                  block_m=128, block_n=128, causal=True, backend="auto", precision="split",
-                 out_dtype=None):
+                 out_dtype=None, ref_tile_load=True):
         super().__init__()
         if not adaptive_threshold:
             raise ValueError("AdaptiveSplashAttention: adaptive_threshold=False has no "
@@ -86,6 +91,7 @@ class AdaptiveSplashAttention(torch.nn.Module):
         self.block_m, self.block_n = block_m, block_n
         self.causal = causal
         self.backend, self.precision, self.out_dtype = backend, precision, out_dtype
+        self.ref_tile_load = ref_tile_load
 
     def forward(self, Q, K, V, Q_idx=None, K_idx=None):
         if Q.shape[-1] != self.head_dim:
@@ -93,7 +99,8 @@ class AdaptiveSplashAttention(torch.nn.Module):
         return splash_attention(Q, K, V, Q_idx, K_idx, alpha=self.alpha, sm_scale=self.sm_scale,
                                 k_keep=self.k_keep, block_m=self.block_m,
                                 block_n=self.block_n, causal=self.causal, backend=self.backend,
-                                precision=self.precision, out_dtype=self.out_dtype)
+                                precision=self.precision, out_dtype=self.out_dtype,
+                                ref_tile_load=self.ref_tile_load)
 
     def extra_repr(self):
         return (f"head_dim={self.head_dim}, alpha={self.alpha}, k_keep={self.k_keep}, "

@@ -30,7 +30,7 @@ class Params(ctypes.Structure):
                 ("sm_scale", ctypes.c_float), ("causal", ctypes.c_int),
                 ("in_dtype", ctypes.c_int), ("out_dtype", ctypes.c_int),
                 ("backend", ctypes.c_int), ("precision", ctypes.c_int),
-                ("timeout_spins", ctypes.c_longlong)]
+                ("timeout_spins", ctypes.c_longlong), ("ref_tile_load", ctypes.c_int)]
 
 
 class AsaError(RuntimeError):

@@ -47,6 +47,8 @@ class Settings:
     precision: str = "split"
     out_dtype: torch.dtype = None
     timeout_spins: int = 0
+    # reproduce the reference's tile-load zeroing (include/asa.h ref_tile_load)
+    ref_tile_load: bool = True
 
 
 def make_params(Q, K, st: Settings):
@@ -68,6 +70,7 @@ def make_params(Q, K, st: Settings):
     p.backend = L.BACKEND[st.backend]
     p.precision = L.PRECISION[st.precision]
     p.timeout_spins = int(st.timeout_spins)
+    p.ref_tile_load = 1 if st.ref_tile_load else 0
     return p
 
 

@@ -75,10 +75,16 @@ typedef struct asa_params {
     int backend;           /* asa_backend                                        */
     int precision;         /* asa_precision (tcgen05 backend only)               */
     long long timeout_spins; /* bound on every device-side wait; 0 = default     */
+    int ref_tile_load;     /* 1 (default): reproduce the reference's tile-load   */
+                           /* zeroing -- each K/V tile element is zeroed when the */
+                           /* reference thread that stages it (query             */
+                           /* qb*block_m + (col*d + dim) % block_m) cannot see    */
+                           /* that key (:176-183, :285-294, :398-406, :442-450);  */
+                           /* 0: every visible key is read in full.              */
 } asa_params;
 
-/* Defaults: block 128x128, k_keep 8, α 1.5, sm_scale 1/sqrt(d) when d is set
- * later (left 0 here), causal, bf16 in / bf16 out, AUTO backend, SPLIT. */
+/* Defaults: block 128x128, k_keep 8, α 1.5, sm_scale 0 (set it), causal,
+ * bf16 in / bf16 out, AUTO backend, SPLIT precision, ref_tile_load 1. */
 void asa_params_default(asa_params* p);
 
 /* Workspace each call needs, in bytes (16-byte multiples).

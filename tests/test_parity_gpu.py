@@ -28,10 +28,12 @@ CASES = {
 }
 
 
-def run_engine(Q, K, V, dO, Qi, Ki, BM, BN, kk, alpha, sc, causal, backend, precision="split"):
+def run_engine(Q, K, V, dO, Qi, Ki, BM, BN, kk, alpha, sc, causal, backend, precision="split",
+               ref_tile_load=True):
     from splash_attention import ops
     st = ops.Settings(alpha=alpha, sm_scale=sc, k_keep=kk, block_m=BM, block_n=BN, causal=causal,
-                      backend=backend, precision=precision, out_dtype=torch.float32)
+                      backend=backend, precision=precision, out_dtype=torch.float32,
+                      ref_tile_load=ref_tile_load)
     dev = "cuda"
     Qd, Kd, Vd, dOd = (x.to(dev) for x in (Q, K, V, dO))
     O, s = ops.forward_saved(Qd, Kd, Vd, Qi.to(dev), Ki.to(dev), st)
@@ -74,3 +76,16 @@ def test_backward_is_deterministic(cuda, dt):
     b = run_engine(Q, K, V, dO, Qi, Ki, 128, 128, 8, 1.5, 0.09, True, "auto")
     for k in ("dQ", "dK", "dV", "O"):
         assert np.array_equal(a[k], b[k]), k
+
+
+@pytest.mark.parametrize("dt,BM,BN,d", [(torch.float32, 32, 64, 64), (torch.bfloat16, 128, 128, 128)])
+def test_full_rows_mode_matches_oracle(cuda, dt, BM, BN, d):
+    # ref_tile_load=False: every visible key is read in full
+    Q, K, V, dO, Qi, Ki = make_inputs(1, 2, 384, 384, d, seed=13, dtype=dt)
+    ref = oracle_run(Q, K, V, dO, Qi, Ki, BM, BN, 8, 1.5, d ** -0.5, True, ref_tile_load=False)
+    got = run_engine(Q, K, V, dO, Qi, Ki, BM, BN, 8, 1.5, d ** -0.5, True, "auto",
+                     ref_tile_load=False)
+    assert np.array_equal(got["M"], ref["M"])
+    assert_tau(got["tau"], ref["tau"])
+    for k in ("O", "dQ", "dK", "dV"):
+        assert_close(k, got[k], ref[k], OUT_ATOL[dt])
