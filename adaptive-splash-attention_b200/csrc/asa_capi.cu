@@ -7,9 +7,12 @@
 // device, launches go on the caller's stream, and errors come back as status
 // codes instead of exceptions.
 #include "asa_internal.h"
+#include <atomic>
 #include <climits>
 #include <cmath>
 #include <cstring>
+#include <string>
+#include <vector>
 
 namespace asa {
 // tcgen05 kernels (asa_tc.cu)
@@ -34,6 +37,49 @@ cudaError_t tc_backward(const Shape& s, const void* Q, const void* K, const void
 __device__ int g_asa_error;
 
 namespace {
+std::atomic<long long> g_launches{0};
+}
+void asa::note_launch(int n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+
+namespace {
+
+// ---- launch profiler: events around each internal launch (per host thread)
+struct ProfMark {
+    const char* label;
+    cudaEvent_t start, stop;
+    long long launches;
+};
+struct ProfState {
+    bool on = false;
+    std::vector<ProfMark> marks;
+    std::vector<std::string> labels;
+    std::vector<double> ms;
+    std::vector<int> counts;
+};
+thread_local ProfState g_prof;
+
+// Scope that times everything launched on `st` between its construction and
+// destruction under `label` when profiling is on.
+struct ProfScope {
+    ProfMark m{};
+    cudaStream_t st;
+    bool on;
+    ProfScope(const char* label, cudaStream_t s) : st(s), on(g_prof.on) {
+        if (!on) return;
+        m.label = label;
+        m.launches = g_launches.load();
+        cudaEventCreate(&m.start);
+        cudaEventCreate(&m.stop);
+        cudaEventRecord(m.start, st);
+    }
+    ~ProfScope() {
+        if (!on) return;
+        cudaEventRecord(m.stop, st);
+        m.launches = g_launches.load() - m.launches;
+        g_prof.marks.push_back(m);
+    }
+};
+
 
 using asa::Shape;
 
@@ -179,12 +225,18 @@ int asa_tau_mask(const asa_params* p, const void* Q, const void* K, const int32_
     if (ws_bytes < fwd_bytes(s, b) || !ws) return ASA_ERR_WORKSPACE;
     cudaStream_t st = (cudaStream_t)stream;
     cudaError_t e;
-    if (b == ASA_BACKEND_TC)
-        e = asa::tc_tau_mask(s, Q, K, Qidx, Kidx, tau, M, ws, error_word(), st);
-    else
-        e = asa::simt_tau_mask(s, Q, K, Qidx, Kidx, tau, M, st);
+    {
+        ProfScope ps("tau_mask", st);
+        if (b == ASA_BACKEND_TC)
+            e = asa::tc_tau_mask(s, Q, K, Qidx, Kidx, tau, M, ws, error_word(), st);
+        else
+            e = asa::simt_tau_mask(s, Q, K, Qidx, Kidx, tau, M, st);
+    }
     if (e != cudaSuccess) return ASA_ERR_CUDA;
-    if (csr_ptr && csr_idx) e = asa::build_lists(s, M, csr_ptr, csr_idx, nullptr, nullptr, st);
+    if (csr_ptr && csr_idx) {
+        ProfScope ps("tile_lists", st);
+        e = asa::build_lists(s, M, csr_ptr, csr_idx, nullptr, nullptr, st);
+    }
     return cuda_status(e);
 }
 
@@ -204,6 +256,7 @@ int asa_forward(const asa_params* p, const void* Q, const void* K, const void* V
     if (rc) return rc;
     cudaStream_t st = (cudaStream_t)stream;
     cudaError_t e;
+    ProfScope ps("forward", st);
     if (b == ASA_BACKEND_TC)
         e = asa::tc_forward(s, Q, K, V, Qidx, Kidx, tau, csr_ptr, csr_idx, O, O32, rownorm, ws,
                             error_word(), st);
@@ -244,19 +297,31 @@ int asa_backward(const asa_params* p, const void* Q, const void* K, const void* 
     float* accdO = (float*)(w + L.accdO);
     int32_t* cptr = (int32_t*)(w + L.cptr);
     int32_t* cidx = (int32_t*)(w + L.cidx);
-    cudaError_t e = asa::build_lists(s, M, nullptr, nullptr, cptr, cidx, st);
+    cudaError_t e;
+    {
+        ProfScope ps("tile_lists_t", st);
+        e = asa::build_lists(s, M, nullptr, nullptr, cptr, cidx, st);
+    }
     if (e != cudaSuccess) return ASA_ERR_CUDA;
     if (b == ASA_BACKEND_TC) {
+        ProfScope ps("backward", st);
         if (!O32 || !rownorm) return ASA_ERR_INVALID;
         e = asa::tc_backward(s, Q, K, V, Qidx, Kidx, O32, tau, csr_ptr, csr_idx, cptr, cidx,
                              rownorm, dO, dQ, dK, dV, w + L.extra, error_word(), st);
         return cuda_status(e);
     }
-    e = asa::simt_rowstats(s, Q, K, V, Qidx, Kidx, tau, csr_ptr, csr_idx, dO, invN, accdO, st);
-    if (e == cudaSuccess)
+    {
+        ProfScope ps("bwd_rowstats", st);
+        e = asa::simt_rowstats(s, Q, K, V, Qidx, Kidx, tau, csr_ptr, csr_idx, dO, invN, accdO, st);
+    }
+    if (e == cudaSuccess) {
+        ProfScope ps("bwd_dq", st);
         e = asa::simt_dq(s, Q, K, V, Qidx, Kidx, tau, csr_ptr, csr_idx, dO, invN, accdO, dQ, st);
-    if (e == cudaSuccess && s.NK)
+    }
+    if (e == cudaSuccess && s.NK) {
+        ProfScope ps("bwd_dkdv", st);
         e = asa::simt_dkdv(s, Q, K, V, Qidx, Kidx, tau, cptr, cidx, dO, invN, accdO, dK, dV, st);
+    }
     return cuda_status(e);
 }
 
@@ -279,6 +344,53 @@ int asa_device_error(asa_stream_t stream, int* code) {
     *code = v;
     return cuda_status(e);
 }
+
+int asa_profile_begin(int enable) {
+    for (auto& m : g_prof.marks) {
+        cudaEventDestroy(m.start);
+        cudaEventDestroy(m.stop);
+    }
+    g_prof.marks.clear();
+    g_prof.labels.clear();
+    g_prof.ms.clear();
+    g_prof.counts.clear();
+    g_prof.on = enable != 0;
+    return ASA_OK;
+}
+
+int asa_profile_end(void) {
+    g_prof.on = false;
+    int rc = ASA_OK;
+    for (auto& m : g_prof.marks) {
+        float ms = 0.0f;
+        if (cudaEventSynchronize(m.stop) != cudaSuccess ||
+            cudaEventElapsedTime(&ms, m.start, m.stop) != cudaSuccess)
+            rc = ASA_ERR_CUDA;
+        size_t i = 0;
+        while (i < g_prof.labels.size() && g_prof.labels[i] != m.label) ++i;
+        if (i == g_prof.labels.size()) {
+            g_prof.labels.push_back(m.label);
+            g_prof.ms.push_back(0.0);
+            g_prof.counts.push_back(0);
+        }
+        g_prof.ms[i] += ms;
+        g_prof.counts[i] += (int)m.launches;
+        cudaEventDestroy(m.start);
+        cudaEventDestroy(m.stop);
+    }
+    g_prof.marks.clear();
+    return rc;
+}
+
+int asa_profile_get(int i, const char** label, double* total_ms, int* launches) {
+    if (i < 0 || i >= (int)g_prof.labels.size()) return ASA_ERR_INVALID;
+    if (label) *label = g_prof.labels[i].c_str();
+    if (total_ms) *total_ms = g_prof.ms[i];
+    if (launches) *launches = g_prof.counts[i];
+    return ASA_OK;
+}
+
+long long asa_launch_count(void) { return g_launches.load(); }
 
 const char* asa_status_string(int status) {
     switch (status) {

@@ -101,6 +101,7 @@ cudaError_t build_lists(const Shape& s, const uint8_t* M, int32_t* csr_ptr, int3
         if (e != cudaSuccess) return e;
     }
     build_lists_kernel<<<s.BH, LT, smem, st>>>(s.nQB, s.nKB, M, csr_ptr, csr_idx, csc_ptr, csc_idx);
+    note_launch();
     return cudaGetLastError();
 }
 
@@ -116,6 +117,7 @@ cudaError_t scrub(int dtype, void* x, size_t n, int* flag, cudaStream_t st) {
         scrub_detect<__nv_bfloat16><<<blocks, 256, 0, st>>>((const __nv_bfloat16*)x, n, flag);
         scrub_apply<__nv_bfloat16><<<blocks, 256, 0, st>>>((__nv_bfloat16*)x, n, flag);
     }
+    note_launch(2);
     return cudaGetLastError();
 }
 

@@ -37,6 +37,10 @@ __device__ __forceinline__ bool ref_keep(const Shape& s, const int32_t* __restri
     return lq >= s.NQ || kpos <= __ldg(Qidx_bh + lq);
 }
 
+// Count of kernels this library has launched (for the bench's launch
+// count); every launch site calls note_launch().
+void note_launch(int n = 1);
+
 // ---- SIMT kernels (asa_simt.cu) -------------------------------------------
 cudaError_t simt_tau_mask(const Shape& s, const void* Q, const void* K, const int32_t* Qidx,
                           const int32_t* Kidx, float* tau, uint8_t* M, cudaStream_t st);

@@ -462,6 +462,7 @@ cudaError_t launch_tau_mask(const Shape& s, const void* Q, const void* K, const 
     dim3 grid(s.nQB * ((s.BM + QT - 1) / QT), s.BH);
     simt_tau_mask_kernel<T, DM, KM><<<grid, QT, 0, st>>>(
         s, (const T*)Q, (const T*)K, Qidx, Kidx, tau, M);
+    note_launch();
     return cudaGetLastError();
 }
 
@@ -480,6 +481,7 @@ cudaError_t launch_rows(const Shape& s, const void* Q, const void* K, const void
     dim3 grid(s.nQB * subs, s.BH);
     kern<<<grid, QT, smem, st>>>(s, (const T*)Q, (const T*)K, (const T*)V, Qidx, Kidx, tau, ptr,
                                  idx, (const T*)dO, invN, accdO, (TO*)out, out32, r0, r1);
+    note_launch();
     return cudaGetLastError();
 }
 
@@ -498,6 +500,7 @@ cudaError_t launch_dkdv(const Shape& s, const void* Q, const void* K, const void
     dim3 grid(s.nKB * subs, s.BH);
     kern<<<grid, KTH, smem, st>>>(s, (const T*)Q, (const T*)K, (const T*)V, Qidx, Kidx, tau, cptr,
                                   cidx, (const T*)dO, invN, accdO, (TO*)dK, (TO*)dV);
+    note_launch();
     return cudaGetLastError();
 }
 

@@ -19,7 +19,8 @@ PRECISION = {"split": 0, "bf16": 1}
 #: the exported symbols include/asa.h declares
 SYMBOLS = ("asa_params_default", "asa_workspace_bytes", "asa_resolve_backend", "asa_tau_mask",
            "asa_forward", "asa_backward", "asa_scrub", "asa_device_error", "asa_status_string",
-           "asa_version")
+           "asa_version", "asa_profile_begin", "asa_profile_end", "asa_profile_get",
+           "asa_launch_count")
 
 
 class Params(ctypes.Structure):
@@ -67,6 +68,12 @@ def lib():
         L.asa_status_string.argtypes = [ctypes.c_int]
         L.asa_status_string.restype = ctypes.c_char_p
         L.asa_version.argtypes = []
+        L.asa_profile_begin.argtypes = [ctypes.c_int]
+        L.asa_profile_end.argtypes = []
+        L.asa_profile_get.argtypes = [ctypes.c_int, ctypes.POINTER(ctypes.c_char_p),
+                                      ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_int)]
+        L.asa_launch_count.argtypes = []
+        L.asa_launch_count.restype = ctypes.c_longlong
         for name in SYMBOLS:
             getattr(L, name)
         _lib = L

@@ -217,3 +217,27 @@ def device_error(device=None):
     with torch.cuda.device(device):
         L.check(L.lib().asa_device_error(_stream(), ctypes.byref(code)), "asa_device_error")
     return code.value
+
+
+class profile:
+    """Context manager over asa_profile_begin/end: per-kernel-label device
+    time (ms) and launch counts of everything the library launches inside
+    the block on this thread.  ``.result`` maps label -> (total_ms, launches)."""
+
+    def __enter__(self):
+        L.check(L.lib().asa_profile_begin(1), "asa_profile_begin")
+        self.result = {}
+        return self
+
+    def __exit__(self, *exc):
+        L.check(L.lib().asa_profile_end(), "asa_profile_end")
+        i = 0
+        lab, ms, n = ctypes.c_char_p(), ctypes.c_double(), ctypes.c_int()
+        while L.lib().asa_profile_get(i, ctypes.byref(lab), ctypes.byref(ms), ctypes.byref(n)) == 0:
+            self.result[lab.value.decode()] = (ms.value, n.value)
+            i += 1
+        return False
+
+
+def launch_count():
+    return int(L.lib().asa_launch_count())

@@ -135,6 +135,20 @@ int asa_scrub(int dtype, void* x, size_t n, void* ws, asa_stream_t stream);
  * wait runs out.  Synchronises the stream.  *code is 0 when no error. */
 int asa_device_error(asa_stream_t stream, int* code);
 
+/* Per-launch timing for benchmarks and tracing (no counterpart in the
+ * reference, which only wall-clocks whole calls, nb:1791-1796).
+ * asa_profile_begin(1) makes every entry point record a CUDA event before
+ * and after each kernel it launches on its stream; asa_profile_end()
+ * synchronises on those events and aggregates per kernel label; then
+ * asa_profile_get(i, ...) returns label i's total milliseconds and launch
+ * count (ASA_ERR_INVALID past the last label).  Recording is per host
+ * thread.  asa_launch_count() is the number of kernels the library has
+ * launched since load. */
+int asa_profile_begin(int enable);
+int asa_profile_end(void);
+int asa_profile_get(int i, const char** label, double* total_ms, int* launches);
+long long asa_launch_count(void);
+
 /* Human-readable text of an asa_status. */
 const char* asa_status_string(int status);
 

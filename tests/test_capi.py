@@ -13,7 +13,7 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 def header_functions():
     text = open(os.path.join(ROOT, "include", "asa.h")).read()
-    return set(re.findall(r"^\s*(?:int|void|const char\*)\s+(asa_\w+)\s*\(", text, re.M))
+    return set(re.findall(r"^\s*(?:int|void|const char\*|long long)\s+(asa_\w+)\s*\(", text, re.M))
 
 
 def test_exports_every_declared_symbol():
