@@ -8,6 +8,7 @@
 // codes instead of exceptions.
 #include "asa_internal.h"
 #include <atomic>
+#include <mutex>
 #include <climits>
 #include <cmath>
 #include <cstring>
@@ -56,7 +57,8 @@ struct ProfState {
     std::vector<double> ms;
     std::vector<int> counts;
 };
-thread_local ProfState g_prof;
+ProfState g_prof;
+std::mutex g_prof_mu;
 
 // Scope that times everything launched on `st` between its construction and
 // destruction under `label` when profiling is on.
@@ -76,6 +78,7 @@ struct ProfScope {
         if (!on) return;
         cudaEventRecord(m.stop, st);
         m.launches = g_launches.load() - m.launches;
+        std::lock_guard<std::mutex> lk(g_prof_mu);
         g_prof.marks.push_back(m);
     }
 };
@@ -346,6 +349,7 @@ int asa_device_error(asa_stream_t stream, int* code) {
 }
 
 int asa_profile_begin(int enable) {
+    std::lock_guard<std::mutex> lk(g_prof_mu);
     for (auto& m : g_prof.marks) {
         cudaEventDestroy(m.start);
         cudaEventDestroy(m.stop);
@@ -359,6 +363,7 @@ int asa_profile_begin(int enable) {
 }
 
 int asa_profile_end(void) {
+    std::lock_guard<std::mutex> lk(g_prof_mu);
     g_prof.on = false;
     int rc = ASA_OK;
     for (auto& m : g_prof.marks) {

@@ -141,8 +141,8 @@ int asa_device_error(asa_stream_t stream, int* code);
  * and after each kernel it launches on its stream; asa_profile_end()
  * synchronises on those events and aggregates per kernel label; then
  * asa_profile_get(i, ...) returns label i's total milliseconds and launch
- * count (ASA_ERR_INVALID past the last label).  Recording is per host
- * thread.  asa_launch_count() is the number of kernels the library has
+ * count (ASA_ERR_INVALID past the last label).  Recording is process-wide
+ * (launches from every host thread).  asa_launch_count() is the number of kernels the library has
  * launched since load. */
 int asa_profile_begin(int enable);
 int asa_profile_end(void);
