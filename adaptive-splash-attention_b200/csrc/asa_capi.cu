@@ -139,10 +139,11 @@ Shape make_shape(const asa_params* p) {
     s.scale = p->sm_scale;
     s.pinv = asa::make_pow(1.0f / s.am1);
     s.pe2 = asa::make_pow((2.0f - s.alpha) / (s.alpha - 1.0f));          // :495
-    s.spins = p->timeout_spins > 0 ? p->timeout_spins : (1LL << 26);
+    s.spins = p->timeout_spins > 0 ? p->timeout_spins : (1LL << 22);
     s.in_dtype = p->in_dtype;
     s.out_dtype = p->out_dtype;
     s.ref_load = (p->ref_tile_load && p->causal) ? 1 : 0;
+    s.split = p->precision == ASA_PREC_SPLIT ? 1 : 0;
     return s;
 }
 
@@ -176,7 +177,12 @@ size_t fwd_bytes(const Shape& s, int backend) {
     return o;
 }
 
-int cuda_status(cudaError_t e) { return e == cudaSuccess ? ASA_OK : ASA_ERR_CUDA; }
+thread_local cudaError_t g_last_cuda = cudaSuccess;
+int cuda_status(cudaError_t e) {
+    if (e == cudaSuccess) return ASA_OK;
+    g_last_cuda = e;
+    return ASA_ERR_CUDA;
+}
 
 }  // namespace
 
@@ -235,7 +241,7 @@ int asa_tau_mask(const asa_params* p, const void* Q, const void* K, const int32_
         else
             e = asa::simt_tau_mask(s, Q, K, Qidx, Kidx, tau, M, st);
     }
-    if (e != cudaSuccess) return ASA_ERR_CUDA;
+    if (e != cudaSuccess) return cuda_status(e);
     if (csr_ptr && csr_idx) {
         ProfScope ps("tile_lists", st);
         e = asa::build_lists(s, M, csr_ptr, csr_idx, nullptr, nullptr, st);
@@ -305,7 +311,7 @@ int asa_backward(const asa_params* p, const void* Q, const void* K, const void* 
         ProfScope ps("tile_lists_t", st);
         e = asa::build_lists(s, M, nullptr, nullptr, cptr, cidx, st);
     }
-    if (e != cudaSuccess) return ASA_ERR_CUDA;
+    if (e != cudaSuccess) return cuda_status(e);
     if (b == ASA_BACKEND_TC) {
         ProfScope ps("backward", st);
         if (!O32 || !rownorm) return ASA_ERR_INVALID;
@@ -396,6 +402,8 @@ int asa_profile_get(int i, const char** label, double* total_ms, int* launches) 
 }
 
 long long asa_launch_count(void) { return g_launches.load(); }
+
+const char* asa_last_cuda_error(void) { return cudaGetErrorString(g_last_cuda); }
 
 const char* asa_status_string(int status) {
     switch (status) {

@@ -23,6 +23,7 @@ struct Shape {
     long long spins; // bound on device-side waits
     int in_dtype, out_dtype;
     int ref_load;    // reproduce the reference's tile-load zeroing (causal only)
+    int split;       // tcgen05 path: P and dS enter the MMAs as bf16 hi+lo pairs
 };
 
 // Whether element `t` of key row `kn` survives the reference's tile staging

@@ -224,7 +224,7 @@ simt_rows_kernel(Shape sh, const T* __restrict__ Q, const T* __restrict__ K,
             __syncthreads();
             if (!qv) continue;
             for (int j = 0; j < cn; ++j) {
-                if (!(Kp[j] <= qpos)) continue;
+                if (start + c0 + j >= sh.NK || !(Kp[j] <= qpos)) continue;
                 float a = 0.0f;
 #pragma unroll
                 for (int t = 0; t < DM; ++t)

@@ -1,25 +1,1305 @@
-// asa_tc.cu -- tcgen05 / TMEM / TMA kernels (bf16, d in {64,128}, 128x128 tiles).
+// asa_tc.cu -- tcgen05 / TMEM / TMA kernels for bf16 inputs, head dim 64 or
+// 128, 128x128 mask tiles.
+//
+// Kernels (one CTA per 128-row block, warp-specialised, 192 threads):
+//   tc_bounds   per-block min/max of the position indices (tile visibility)
+//   k1_tau_mask τ and block mask: S = Q·K^T over every visible tile into
+//               TMEM (double-buffered), 4 epilogue warps stream each score
+//               row through the reference top-k, then solve τ
+//               (reference build_mask_kernel :150-217)
+//   k3_forward  O = Σ p v / (Σ p + EPS) over the CSR tile list: S = Q·K^T,
+//               entmax p in the epilogue warps, P written to shared memory as
+//               a bf16 hi/lo pair, O += P_hi·V + P_lo·V in TMEM
+//               (reference splash_forward_sparse :244-341)
+//   k4_pre      D_q = O·dO per query (the acc·dO/n term of :487-491)
+//   k4_dq       dQ = Σ dS·K over the CSR list (query-major)
+//   k4_dkdv     dV = Σ P^T·dO/n, dK = Σ dS^T·Q over the transposed list
+//               (key-major; no atomics)
+//               (reference splash_backward_sparse :343-535)
+//
+// Warp roles: warp 0 issues TMA loads, warp 1 owns TMEM and issues the MMAs
+// (lane 0) -- its 32 lanes also apply the reference's tile-load zeroing to
+// freshly loaded K/V tiles when a tile needs it -- and warps 2..5 are the
+// epilogue: thread (warp%4)*32+lane owns TMEM lane = tile row.
+//
+// Every mbarrier wait is bounded (Shape::spins polls); when one runs out the
+// kernel records ASA_ERR_DEVICE_TIMEOUT in the device error word and carries
+// on without the data, so it always terminates.
 #include "asa_internal.h"
+#include "asa_sm100.cuh"
+#include <climits>
+#include <cudaTypedefs.h>
 
 namespace asa {
+namespace {
 
-bool tc_supported(const Shape& s) { (void)s; return false; }
-size_t tc_fwd_workspace(const Shape&) { return 0; }
-size_t tc_bwd_workspace(const Shape&) { return 0; }
-cudaError_t tc_tau_mask(const Shape&, const void*, const void*, const int32_t*, const int32_t*,
-                        float*, uint8_t*, void*, int*, cudaStream_t) {
-    return cudaErrorNotSupported;
+using namespace sm100;
+
+constexpr int TILE = 128;
+constexpr int BOX = 64;                    // bf16 elements per 128-byte swizzle row
+constexpr int BOX_BYTES = TILE * 128;      // one 64-column box of 128 rows
+constexpr int NTHREADS = 192;
+constexpr int EPI0 = 64;                   // first epilogue thread
+
+struct Bounds {
+    const int* qmin;   // [BH][nQB]
+    const int* qmax;
+    const int* kmin;   // [BH][nKB]
+    const int* kmax;
+};
+
+// Dynamic shared memory starts at the bottom of the CTA's window (these
+// kernels declare no static __shared__ data), which is 1024-byte aligned as
+// the 128-byte swizzle atoms require.  A misaligned base is reported, not
+// silently mis-swizzled.
+__device__ __forceinline__ uint8_t* align1024(uint8_t* p, int* err) {
+    if ((smem_u32(p) & 1023u) != 0 && threadIdx.x == 0 && err) atomicCAS(err, 0, ASA_ERR_UNSUPPORTED);
+    return p;
 }
-cudaError_t tc_forward(const Shape&, const void*, const void*, const void*, const int32_t*,
-                       const int32_t*, const float*, const int32_t*, const int32_t*, void*, float*,
-                       float*, void*, int*, cudaStream_t) {
-    return cudaErrorNotSupported;
+
+__device__ __forceinline__ void epi_bar() {
+    asm volatile("bar.sync 1, 128;" ::: "memory");
 }
-cudaError_t tc_backward(const Shape&, const void*, const void*, const void*, const int32_t*,
-                        const int32_t*, const float*, const float*, const int32_t*,
-                        const int32_t*, const int32_t*, const int32_t*, const float*, const void*,
-                        void*, void*, void*, void*, int*, cudaStream_t) {
-    return cudaErrorNotSupported;
+
+__device__ __forceinline__ float neg_inf() { return __int_as_float(0xff800000); }
+
+// ---- tile classification (identical in every role) --------------------------
+__device__ __forceinline__ bool vis_any(const Shape& s, const Bounds& b, int bh, int qb, int kb) {
+    if (!s.causal) return true;
+    return b.kmin[bh * s.nKB + kb] <= b.qmax[bh * s.nQB + qb];
+}
+__device__ __forceinline__ bool vis_all(const Shape& s, const Bounds& b, int bh, int qb, int kb) {
+    if ((kb + 1) * TILE > s.NK) return false;
+    if (!s.causal) return true;
+    return b.kmax[bh * s.nKB + kb] <= b.qmin[bh * s.nQB + qb];
+}
+__device__ __forceinline__ bool needs_fix(const Shape& s, const Bounds& b, int bh, int qb, int kb) {
+    if (!s.ref_load) return false;
+    return b.kmax[bh * s.nKB + kb] > b.qmin[bh * s.nQB + qb];
+}
+
+// ---- the reference's tile-load zeroing on a swizzled 128-row tile ------------
+// Element (row r, dim t) of key kb*128+r is zeroed for query block qb when the
+// reference thread that stages it (query qb*128 + ((r*d + t) % 128)) cannot
+// see the key.  qidx_blk holds that block's 128 positions (INT_MAX past NQ,
+// which keeps the element, see ref_keep).  Executed by one full warp.
+template <int D>
+__device__ void fix_tile(uint8_t* tile, const int* qidx_blk, int qmin_blk,
+                         const int32_t* __restrict__ Kidx_bh, int kb, int NK, int lane) {
+    for (int r = lane; r < TILE; r += 32) {
+        const int kn = kb * TILE + r;
+        if (kn >= NK) continue;
+        const int kpos = Kidx_bh[kn];
+        if (kpos <= qmin_blk) continue;
+#pragma unroll 1
+        for (int ch = 0; ch < D / 8; ++ch) {
+            const int t0 = ch * 8;
+            uint32_t keep = 0;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                const int off = (r * D + t0 + e) & (TILE - 1);
+                keep |= (kpos <= qidx_blk[off] ? 1u : 0u) << e;
+            }
+            if (keep == 0xffu) continue;
+            const int box = t0 / BOX;
+            const int phys = ((t0 % BOX) / 8) ^ (r & 7);
+            uint4* p = reinterpret_cast<uint4*>(tile + box * BOX_BYTES + r * 128 + phys * 16);
+            uint4 v = *p;
+            uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int e = 0; e < 8; ++e)
+                if (!((keep >> e) & 1u)) w[e >> 1] &= (e & 1) ? 0x0000ffffu : 0xffff0000u;
+            *p = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+    }
+}
+
+// ---- descriptors ---------------------------------------------------------------
+// K-major operand tile (128 rows, D columns as D/64 boxes of 16 KB): k-step kk
+// covers columns [16kk, 16kk+16).
+__device__ __forceinline__ uint64_t kdesc(const uint8_t* tile, int kk) {
+    return sdesc(smem_u32(tile + (kk >> 2) * BOX_BYTES + (kk & 3) * 32), 16, 1024);
+}
+// MN-major operand tile (128 K-rows of 128 bytes per 64-wide M/N box): k-step
+// kk covers rows [16kk, 16kk+16); boxes are BOX_BYTES apart along M/N.
+__device__ __forceinline__ uint64_t mndesc(const uint8_t* tile, int kk) {
+    return sdesc(smem_u32(tile + kk * 16 * 128), BOX_BYTES, 1024);
+}
+
+// Store 32 consecutive columns [32c, 32c+32) of row `row` of a 128x128 bf16
+// K-major swizzled tile from packed pairs (pk[m] = cols 2m, 2m+1).
+__device__ __forceinline__ void store_row_chunk(uint8_t* tile, int row, int c, const uint32_t (&pk)[16]) {
+    const int box = c >> 1;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int ch = (c & 1) * 4 + i;
+        const int phys = ch ^ (row & 7);
+        uint4* p = reinterpret_cast<uint4*>(tile + box * BOX_BYTES + row * 128 + phys * 16);
+        *p = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+    }
+}
+
+__device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// hi/lo split of 32 values: hi = bf16(x), lo = bf16(x - hi).  With split=false
+// only hi is produced (lo left untouched).
+__device__ __forceinline__ void split_pack(const float (&x)[32], uint32_t (&hi)[16], uint32_t (&lo)[16]) {
+#pragma unroll
+    for (int m = 0; m < 16; ++m) {
+        const __nv_bfloat162 h = __floats2bfloat162_rn(x[2 * m], x[2 * m + 1]);
+        hi[m] = *reinterpret_cast<const uint32_t*>(&h);
+        const float2 hf = __bfloat1622float2(h);
+        lo[m] = pack_bf16(x[2 * m] - hf.x, x[2 * m + 1] - hf.y);
+    }
+}
+
+// p = u^e for the entmax transform inside the tile loops (fp32; the result is
+// rounded to a bf16 pair afterwards, so 1-2 ulp here do not matter).
+__device__ __forceinline__ float pow_fast(float x, const PowSpec& s) {
+    switch (s.kind) {
+        case 1: return x;
+        case 2: return x * x;
+        case 3: return x * x * x;
+        case 4: { const float y = x * x; return y * y; }
+        case 5: return 1.0f;
+        case 6: return 1.0f / x;
+        default: return powf(x, s.e);
+    }
+}
+
+__device__ __forceinline__ uint32_t tmem_lane_base(uint32_t tbase, int warp) {
+    return tbase + ((uint32_t)((warp & 3) * 32) << 16);
+}
+
+// ===========================================================================
+// tc_bounds: per query block min/max of Q_idx, per key block min/max of K_idx
+// ===========================================================================
+__global__ void tc_bounds_kernel(Shape s, const int32_t* __restrict__ Qidx,
+                                 const int32_t* __restrict__ Kidx, int* qmin, int* qmax, int* kmin,
+                                 int* kmax) {
+    const int bh = blockIdx.y;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nwarps = blockDim.x >> 5;
+    const int total = s.nQB + s.nKB;
+    for (int blk = blockIdx.x * nwarps + warp; blk < total; blk += gridDim.x * nwarps) {
+        const bool isq = blk < s.nQB;
+        const int b = isq ? blk : blk - s.nQB;
+        const int N = isq ? s.NQ : s.NK;
+        const int32_t* idx = (isq ? Qidx + (size_t)bh * s.NQ : Kidx + (size_t)bh * s.NK);
+        int mn = INT_MAX, mx = INT_MIN;
+        for (int i = lane; i < TILE; i += 32) {
+            const int n = b * TILE + i;
+            if (n < N) {
+                const int v = idx[n];
+                mn = min(mn, v);
+                mx = max(mx, v);
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            mn = min(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+            mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        }
+        if (lane == 0) {
+            if (isq) { qmin[bh * s.nQB + b] = mn; qmax[bh * s.nQB + b] = mx; }
+            else { kmin[bh * s.nKB + b] = mn; kmax[bh * s.nKB + b] = mx; }
+        }
+    }
+}
+
+// ===========================================================================
+// K1: τ and block mask
+// ===========================================================================
+template <int D, int KM>
+__global__ void __launch_bounds__(NTHREADS, 1)
+k1_tau_mask(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK, Shape s,
+            const int32_t* __restrict__ Qidx, const int32_t* __restrict__ Kidx, Bounds bd,
+            float* __restrict__ tau, uint8_t* __restrict__ M, int* err) {
+    constexpr int S = 4;
+    constexpr int TB = D * TILE * 2;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* base = align1024(smem_raw, err);
+    uint8_t* sQ = base;
+    uint8_t* sK = base + TB;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sK + S * TB);
+    uint64_t* q_full = bars;
+    uint64_t* k_full = bars + 1;
+    uint64_t* k_empty = bars + 1 + S;
+    uint64_t* s_full = bars + 1 + 2 * S;
+    uint64_t* s_free = bars + 3 + 2 * S;
+    uint32_t* holder = reinterpret_cast<uint32_t*>(bars + 16);
+    int* kidx_s = reinterpret_cast<int*>(holder + 4);      // [2][128]
+    int* qidx_blk = kidx_s + 256;                            // [128]
+    uint8_t* flags = reinterpret_cast<uint8_t*>(qidx_blk + TILE);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int bh = blockIdx.y;
+    const int qb = s.causal ? (int)(gridDim.x - 1 - blockIdx.x) : (int)blockIdx.x;
+    const int32_t* Kidx_bh = Kidx + (size_t)bh * s.NK;
+
+    if (threadIdx.x == 0) {
+        mbar_init(q_full, 1);
+        for (int i = 0; i < S; ++i) { mbar_init(&k_full[i], 1); mbar_init(&k_empty[i], 1); }
+        for (int i = 0; i < 2; ++i) { mbar_init(&s_full[i], 1); mbar_init(&s_free[i], 128); }
+        fence_barrier_init();
+    }
+    if (warp == 1) { tmem_alloc(holder, 256); tmem_relinquish(); }
+    if (threadIdx.x >= EPI0) {
+        const int r = threadIdx.x - EPI0;
+        const int q = qb * TILE + r;
+        qidx_blk[r] = (q < s.NQ && s.causal) ? Qidx[(size_t)bh * s.NQ + q] : INT_MAX;
+        for (int i = r; i < s.nKB; i += 128) flags[i] = 0;
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tbase = *holder;
+    const int qmin_blk = s.causal ? bd.qmin[bh * s.nQB + qb] : INT_MIN;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            tma_prefetch_desc(&tmQ);
+            tma_prefetch_desc(&tmK);
+            mbar_expect_tx(q_full, TB);
+            for (int bx = 0; bx < D / BOX; ++bx)
+                tma_load_3d(sQ + bx * BOX_BYTES, &tmQ, q_full, bx * BOX, qb * TILE, bh);
+            int j = 0;
+            for (int kb = 0; kb < s.nKB; ++kb) {
+                if (!vis_any(s, bd, bh, qb, kb)) continue;
+                const int st = j % S;
+                mbar_wait(&k_empty[st], ((j / S) & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+                mbar_expect_tx(&k_full[st], TB);
+                for (int bx = 0; bx < D / BOX; ++bx)
+                    tma_load_3d(sK + st * TB + bx * BOX_BYTES, &tmK, &k_full[st], bx * BOX, kb * TILE, bh);
+                ++j;
+            }
+        }
+    } else if (warp == 1) {
+        constexpr uint32_t idesc = idesc_bf16(128, 128, 0, 0);
+        mbar_wait(q_full, 0, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+        int j = 0;
+        for (int kb = 0; kb < s.nKB; ++kb) {
+            if (!vis_any(s, bd, bh, qb, kb)) continue;
+            const int st = j % S, b = j & 1;
+            uint8_t* kt = sK + st * TB;
+            mbar_wait(&k_full[st], (j / S) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+            if (needs_fix(s, bd, bh, qb, kb)) {
+                fix_tile<D>(kt, qidx_blk, qmin_blk, Kidx_bh, kb, s.NK, lane);
+                fence_async_smem();
+            }
+            __syncwarp();
+            mbar_wait(&s_free[b], ((j >> 1) & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+            tc_fence_after();
+            if (lane == 0) {
+#pragma unroll
+                for (int kk = 0; kk < D / 16; ++kk)
+                    mma_bf16_ss(tbase + b * 128, kdesc(sQ, kk), kdesc(kt, kk), idesc, kk > 0);
+                mma_commit(&s_full[b]);
+                mma_commit(&k_empty[st]);
+            }
+            __syncwarp();
+            ++j;
+        }
+    } else {
+        const int row = (warp & 3) * 32 + lane;
+        const int et = threadIdx.x - EPI0;
+        const int q = qb * TILE + row;
+        const bool qv = q < s.NQ;
+        const int qpos = !qv ? INT_MIN : (s.causal ? Qidx[(size_t)bh * s.NQ + q] : INT_MAX);
+        const uint32_t tl = tmem_lane_base(tbase, warp);
+        TopK<KM> tk;
+        tk.init(s.k);
+        int j = 0;
+        for (int kb = 0; kb < s.nKB; ++kb) {
+            if (!vis_any(s, bd, bh, qb, kb)) continue;
+            const int b = j & 1;
+            const bool all = vis_all(s, bd, bh, qb, kb);
+            {
+                const int kn = kb * TILE + et;
+                kidx_s[b * TILE + et] = kn < s.NK ? (s.causal ? Kidx_bh[kn] : INT_MIN) : INT_MAX;
+            }
+            epi_bar();
+            mbar_wait(&s_full[b], (j >> 1) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+            tc_fence_after();
+#pragma unroll 1
+            for (int c = 0; c < 4; ++c) {
+                uint32_t r[32];
+                tmem_ld32(tl + b * 128 + c * 32, r);
+                tmem_ld_wait();
+                float sv[32];
+                float mx = neg_inf();
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                    const int col = c * 32 + i;
+                    const bool v = all || (kb * TILE + col < s.NK && kidx_s[b * TILE + col] <= qpos);
+                    sv[i] = v ? clamp_score(__uint_as_float(r[i]), s.scale) : neg_inf();
+                    mx = fmaxf(mx, sv[i]);
+                }
+                if (mx > tk.threshold()) {
+#pragma unroll 1
+                    for (int i = 0; i < 32; ++i)
+                        if (sv[i] > tk.threshold()) tk.insert(sv[i], kb * TILE + c * 32 + i);
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(&s_free[b]);
+            ++j;
+        }
+        if (qv) {
+            tau[(size_t)bh * s.NQ + q] = ref_tau<KM>(tk.v, s.k, s.alpha);
+#pragma unroll
+            for (int i = 0; i < KM; ++i)
+                if (tk.i[i] >= 0) flags[tk.i[i] / TILE] = 1;
+        }
+        epi_bar();
+        uint8_t* Mrow = M + ((size_t)bh * s.nQB + qb) * s.nKB;
+        for (int i = et; i < s.nKB; i += 128) Mrow[i] = flags[i];
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tbase, 256);
+    }
+}
+
+// ===========================================================================
+// K3: forward over the CSR tile list
+// ===========================================================================
+template <int D, typename TO>
+__global__ void __launch_bounds__(NTHREADS, 1)
+k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+           const __grid_constant__ CUtensorMap tmV, Shape s, const int32_t* __restrict__ Qidx,
+           const int32_t* __restrict__ Kidx, Bounds bd, const float* __restrict__ tau,
+           const int32_t* __restrict__ ptr, const int32_t* __restrict__ idx, TO* __restrict__ O,
+           float* __restrict__ O32, float* __restrict__ rownorm, int split, int* err) {
+    constexpr int S = 2;
+    constexpr int TB = D * TILE * 2;
+    constexpr int PB = TILE * TILE * 2;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* base = align1024(smem_raw, err);
+    uint8_t* sQ = base;
+    uint8_t* sKV = base + TB;                 // S stages of [K | V]
+    uint8_t* sPh = sKV + S * 2 * TB;
+    uint8_t* sPl = sPh + PB;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sPl + PB);
+    uint64_t* q_full = bars;
+    uint64_t* kv_full = bars + 1;
+    uint64_t* kv_empty = bars + 1 + S;
+    uint64_t* s_full = bars + 1 + 2 * S;
+    uint64_t* s_free = bars + 3 + 2 * S;
+    uint64_t* p_full = bars + 5 + 2 * S;
+    uint64_t* p_free = bars + 6 + 2 * S;
+    uint64_t* o_full = bars + 7 + 2 * S;
+    uint32_t* holder = reinterpret_cast<uint32_t*>(bars + 16);
+    int* kidx_s = reinterpret_cast<int*>(holder + 4);      // [2][128]
+    int* qidx_blk = kidx_s + 256;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int bh = blockIdx.y;
+    const int qb = s.causal ? (int)(gridDim.x - 1 - blockIdx.x) : (int)blockIdx.x;
+    const int32_t* Kidx_bh = Kidx + (size_t)bh * s.NK;
+    const int32_t* list = idx + (size_t)bh * s.nQB * s.nKB;
+    const int e0 = ptr[(size_t)bh * (s.nQB + 1) + qb];
+    const int T = ptr[(size_t)bh * (s.nQB + 1) + qb + 1] - e0;
+
+    if (threadIdx.x == 0) {
+        mbar_init(q_full, 1);
+        for (int i = 0; i < S; ++i) { mbar_init(&kv_full[i], 1); mbar_init(&kv_empty[i], 1); }
+        for (int i = 0; i < 2; ++i) { mbar_init(&s_full[i], 1); mbar_init(&s_free[i], 128); }
+        mbar_init(p_full, 128);
+        mbar_init(p_free, 1);
+        mbar_init(o_full, 1);
+        fence_barrier_init();
+    }
+    if (warp == 1) { tmem_alloc(holder, 512); tmem_relinquish(); }
+    if (threadIdx.x >= EPI0) {
+        const int r = threadIdx.x - EPI0;
+        const int q = qb * TILE + r;
+        qidx_blk[r] = (q < s.NQ && s.causal) ? Qidx[(size_t)bh * s.NQ + q] : INT_MAX;
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tbase = *holder;
+    const uint32_t tO = 256;
+    const int qmin_blk = s.causal ? bd.qmin[bh * s.nQB + qb] : INT_MIN;
+
+    if (warp == 0) {
+        if (lane == 0 && T > 0) {
+            tma_prefetch_desc(&tmQ);
+            tma_prefetch_desc(&tmK);
+            tma_prefetch_desc(&tmV);
+            mbar_expect_tx(q_full, TB);
+            for (int bx = 0; bx < D / BOX; ++bx)
+                tma_load_3d(sQ + bx * BOX_BYTES, &tmQ, q_full, bx * BOX, qb * TILE, bh);
+            for (int j = 0; j < T; ++j) {
+                const int kb = list[e0 + j];
+                const int st = j % S;
+                mbar_wait(&kv_empty[st], ((j / S) & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+                mbar_expect_tx(&kv_full[st], 2 * TB);
+                uint8_t* kt = sKV + st * 2 * TB;
+                for (int bx = 0; bx < D / BOX; ++bx) {
+                    tma_load_3d(kt + bx * BOX_BYTES, &tmK, &kv_full[st], bx * BOX, kb * TILE, bh);
+                    tma_load_3d(kt + TB + bx * BOX_BYTES, &tmV, &kv_full[st], bx * BOX, kb * TILE, bh);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        constexpr uint32_t idS = idesc_bf16(128, 128, 0, 0);
+        constexpr uint32_t idPV = idesc_bf16(128, D, 0, 1);
+        if (T > 0) mbar_wait(q_full, 0, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+        auto do_pv = [&](int i) {
+            const int st = i % S;
+            const uint8_t* vt = sKV + st * 2 * TB + TB;
+            mbar_wait(p_full, i & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+            tc_fence_after();
+            if (lane == 0) {
+#pragma unroll
+                for (int kk = 0; kk < TILE / 16; ++kk)
+                    mma_bf16_ss(tbase + tO, kdesc(sPh, kk), mndesc(vt, kk), idPV, (i > 0 || kk > 0));
+                if (split) {
+#pragma unroll
+                    for (int kk = 0; kk < TILE / 16; ++kk)
+                        mma_bf16_ss(tbase + tO, kdesc(sPl, kk), mndesc(vt, kk), idPV, 1);
+                }
+                mma_commit(p_free);
+                mma_commit(&kv_empty[st]);
+            }
+            __syncwarp();
+        };
+        for (int j = 0; j < T; ++j) {
+            const int kb = list[e0 + j];
+            const int st = j % S, b = j & 1;
+            uint8_t* kt = sKV + st * 2 * TB;
+            mbar_wait(&kv_full[st], (j / S) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+            if (needs_fix(s, bd, bh, qb, kb)) {
+                fix_tile<D>(kt, qidx_blk, qmin_blk, Kidx_bh, kb, s.NK, lane);
+                fix_tile<D>(kt + TB, qidx_blk, qmin_blk, Kidx_bh, kb, s.NK, lane);
+                fence_async_smem();
+            }
+            __syncwarp();
+            mbar_wait(&s_free[b], ((j >> 1) & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+            tc_fence_after();
+            if (lane == 0) {
+#pragma unroll
+                for (int kk = 0; kk < D / 16; ++kk)
+                    mma_bf16_ss(tbase + b * 128, kdesc(sQ, kk), kdesc(kt, kk), idS, kk > 0);
+                mma_commit(&s_full[b]);
+            }
+            __syncwarp();
+            if (j > 0) do_pv(j - 1);
+        }
+        if (T > 0) do_pv(T - 1);
+        if (lane == 0) mma_commit(o_full);
+        __syncwarp();
+    } else {
+        const int row = (warp & 3) * 32 + lane;
+        const int et = threadIdx.x - EPI0;
+        const int q = qb * TILE + row;
+        const bool qv = q < s.NQ;
+        const size_t qrow = (size_t)bh * s.NQ + (qv ? q : 0);
+        const int qpos = !qv ? INT_MIN : (s.causal ? Qidx[qrow] : INT_MAX);
+        const float tq = qv ? tau[qrow] : 0.0f;
+        const uint32_t tl = tmem_lane_base(tbase, warp);
+        float n = 0.0f;
+        for (int j = 0; j < T; ++j) {
+            const int kb = list[e0 + j];
+            const int b = j & 1;
+            const bool all = vis_all(s, bd, bh, qb, kb);
+            {
+                const int kn = kb * TILE + et;
+                kidx_s[b * TILE + et] = kn < s.NK ? (s.causal ? Kidx_bh[kn] : INT_MIN) : INT_MAX;
+            }
+            epi_bar();
+            mbar_wait(&s_full[b], (j >> 1) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+            tc_fence_after();
+            mbar_wait(p_free, (j & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+#pragma unroll 1
+            for (int c = 0; c < 4; ++c) {
+                uint32_t r[32];
+                tmem_ld32(tl + b * 128 + c * 32, r);
+                tmem_ld_wait();
+                float p[32];
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                    const int col = c * 32 + i;
+                    const bool v = all || (kb * TILE + col < s.NK && kidx_s[b * TILE + col] <= qpos);
+                    const float sc = clamp_score(__uint_as_float(r[i]), s.scale);
+                    const float u = __fmaf_rn(s.am1, sc, -tq);
+                    float pr = (v && u > 0.0f) ? pow_fast(fmaxf(u, ASA_EPS), s.pinv) : 0.0f;
+                    if (!isfinite(pr)) pr = 0.0f;
+                    p[i] = pr;
+                    n += pr;
+                }
+                uint32_t hi[16], lo[16];
+                split_pack(p, hi, lo);
+                store_row_chunk(sPh, row, c, hi);
+                if (split) store_row_chunk(sPl, row, c, lo);
+            }
+            tc_fence_before();
+            mbar_arrive(&s_free[b]);
+            fence_async_smem();
+            mbar_arrive(p_full);
+        }
+        mbar_wait(o_full, 0, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+        tc_fence_after();
+        const float inv = __fdiv_rn(1.0f, __fadd_rn(n, ASA_EPS));
+#pragma unroll 1
+        for (int c = 0; c < D / 32; ++c) {
+            uint32_t r[32];
+            tmem_ld32(tl + tO + c * 32, r);
+            tmem_ld_wait();
+            if (!qv) continue;
+            float o[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+                float v = T > 0 ? __uint_as_float(r[i]) * inv : 0.0f;
+                if (!isfinite(v)) v = 0.0f;
+                o[i] = v;
+            }
+            if (O32) {
+                float4* dst = reinterpret_cast<float4*>(O32 + qrow * D + c * 32);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) dst[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+            }
+            if constexpr (sizeof(TO) == 2) {
+                uint4* dst = reinterpret_cast<uint4*>(O + qrow * D + c * 32);
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+                    dst[i] = make_uint4(pack_bf16(o[8 * i], o[8 * i + 1]), pack_bf16(o[8 * i + 2], o[8 * i + 3]),
+                                        pack_bf16(o[8 * i + 4], o[8 * i + 5]), pack_bf16(o[8 * i + 6], o[8 * i + 7]));
+            } else {
+                if ((void*)O != (void*)O32) {
+                    float4* dst = reinterpret_cast<float4*>(O + qrow * D + c * 32);
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) dst[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+                }
+            }
+        }
+        if (qv) rownorm[qrow] = n;
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tbase, 512);
+    }
+}
+
+// ===========================================================================
+// K4 pre: D_q = Σ_t O_t · dO_t  (fp32 O, bf16 dO), one warp per row.
+// ===========================================================================
+template <int D>
+__global__ void k4_pre(const float* __restrict__ O32, const __nv_bfloat16* __restrict__ dO,
+                       float* __restrict__ Dq, size_t rows) {
+    const size_t r = (size_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (r >= rows) return;
+    float acc = 0.0f;
+#pragma unroll
+    for (int t = lane; t < D; t += 32) acc = fmaf(O32[r * D + t], __bfloat162float(dO[r * D + t]), acc);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (lane == 0) Dq[r] = acc;
+}
+
+// Gradient of one score (reference :481-507) from s (clamped), dP = dO·v,
+// the row's τ, 1/n and D = O·dO:  g = u^{(2-α)/(α-1)} · (dP - D)/n for
+// u > EPS, else 0.
+__device__ __forceinline__ float score_grad(const Shape& s, float sc, float dP, float tq, float invN,
+                                            float Dq, bool vis) {
+    const float u = __fmaf_rn(s.am1, sc, -tq);
+    if (!vis || !(u > ASA_EPS)) return 0.0f;
+    const float pw = pow_fast(fmaxf(u, ASA_EPS), s.pe2);
+    float g = pw * (dP - Dq) * invN;
+    return isfinite(g) ? g : 0.0f;
+}
+
+// ===========================================================================
+// K4 dQ: query-major over the CSR list.  S = Q·K^T, dP = dO·V^T; dS in the
+// epilogue; dQ += dS·K (K tile as the MN-major B operand).
+// ===========================================================================
+template <int D, typename TO>
+__global__ void __launch_bounds__(NTHREADS, 1)
+k4_dq(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+      const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO, Shape s,
+      const int32_t* __restrict__ Qidx, const int32_t* __restrict__ Kidx, Bounds bd,
+      const float* __restrict__ tau, const float* __restrict__ rownorm, const float* __restrict__ Dqv,
+      const int32_t* __restrict__ ptr, const int32_t* __restrict__ idx, TO* __restrict__ dQ, int split,
+      int* err) {
+    constexpr int TB = D * TILE * 2;
+    constexpr int PB = TILE * TILE * 2;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* base = align1024(smem_raw, err);
+    uint8_t* sQ = base;
+    uint8_t* sdO = base + TB;
+    uint8_t* sK = base + 2 * TB;
+    uint8_t* sV = base + 3 * TB;
+    uint8_t* sDh = base + 4 * TB;
+    uint8_t* sDl = sDh + PB;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sDl + PB);
+    uint64_t* q_full = bars;
+    uint64_t* kv_full = bars + 1;
+    uint64_t* kv_empty = bars + 2;
+    uint64_t* sd_full = bars + 3;
+    uint64_t* sd_free = bars + 4;
+    uint64_t* ds_full = bars + 5;
+    uint64_t* ds_free = bars + 6;
+    uint64_t* dq_full = bars + 7;
+    uint32_t* holder = reinterpret_cast<uint32_t*>(bars + 16);
+    int* kidx_s = reinterpret_cast<int*>(holder + 4);     // [2][128]
+    int* qidx_blk = kidx_s + 256;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int bh = blockIdx.y;
+    const int qb = s.causal ? (int)(gridDim.x - 1 - blockIdx.x) : (int)blockIdx.x;
+    const int32_t* Kidx_bh = Kidx + (size_t)bh * s.NK;
+    const int32_t* list = idx + (size_t)bh * s.nQB * s.nKB;
+    const int e0 = ptr[(size_t)bh * (s.nQB + 1) + qb];
+    const int T = ptr[(size_t)bh * (s.nQB + 1) + qb + 1] - e0;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < 8; ++i) mbar_init(&bars[i], 1);
+        mbar_init(sd_free, 128);
+        mbar_init(ds_full, 128);
+        fence_barrier_init();
+    }
+    if (warp == 1) { tmem_alloc(holder, 512); tmem_relinquish(); }
+    if (threadIdx.x >= EPI0) {
+        const int r = threadIdx.x - EPI0;
+        const int q = qb * TILE + r;
+        qidx_blk[r] = (q < s.NQ && s.causal) ? Qidx[(size_t)bh * s.NQ + q] : INT_MAX;
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tbase = *holder;
+    const uint32_t tS = 0, tP = 128, tQ = 256;
+    const int qmin_blk = s.causal ? bd.qmin[bh * s.nQB + qb] : INT_MIN;
+
+    if (warp == 0) {
+        if (lane == 0 && T > 0) {
+            mbar_expect_tx(q_full, 2 * TB);
+            for (int bx = 0; bx < D / BOX; ++bx) {
+                tma_load_3d(sQ + bx * BOX_BYTES, &tmQ, q_full, bx * BOX, qb * TILE, bh);
+                tma_load_3d(sdO + bx * BOX_BYTES, &tmdO, q_full, bx * BOX, qb * TILE, bh);
+            }
+            for (int j = 0; j < T; ++j) {
+                const int kb = list[e0 + j];
+                mbar_wait(kv_empty, (j & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+                mbar_expect_tx(kv_full, 2 * TB);
+                for (int bx = 0; bx < D / BOX; ++bx) {
+                    tma_load_3d(sK + bx * BOX_BYTES, &tmK, kv_full, bx * BOX, kb * TILE, bh);
+                    tma_load_3d(sV + bx * BOX_BYTES, &tmV, kv_full, bx * BOX, kb * TILE, bh);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        constexpr uint32_t idS = idesc_bf16(128, 128, 0, 0);
+        constexpr uint32_t idQ = idesc_bf16(128, D, 0, 1);
+        if (T > 0) mbar_wait(q_full, 0, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+        for (int j = 0; j < T; ++j) {
+            const int kb = list[e0 + j];
+            mbar_wait(kv_full, j & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+            if (needs_fix(s, bd, bh, qb, kb)) {
+                fix_tile<D>(sK, qidx_blk, qmin_blk, Kidx_bh, kb, s.NK, lane);
+                fix_tile<D>(sV, qidx_blk, qmin_blk, Kidx_bh, kb, s.NK, lane);
+                fence_async_smem();
+            }
+            __syncwarp();
+            mbar_wait(sd_free, (j & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+            tc_fence_after();
+            if (lane == 0) {
+#pragma unroll
+                for (int kk = 0; kk < D / 16; ++kk) {
+                    mma_bf16_ss(tbase + tS, kdesc(sQ, kk), kdesc(sK, kk), idS, kk > 0);
+                    mma_bf16_ss(tbase + tP, kdesc(sdO, kk), kdesc(sV, kk), idS, kk > 0);
+                }
+                mma_commit(sd_full);
+            }
+            __syncwarp();
+            mbar_wait(ds_full, j & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+            tc_fence_after();
+            if (lane == 0) {
+#pragma unroll
+                for (int kk = 0; kk < TILE / 16; ++kk)
+                    mma_bf16_ss(tbase + tQ, kdesc(sDh, kk), mndesc(sK, kk), idQ, (j > 0 || kk > 0));
+                if (split) {
+#pragma unroll
+                    for (int kk = 0; kk < TILE / 16; ++kk)
+                        mma_bf16_ss(tbase + tQ, kdesc(sDl, kk), mndesc(sK, kk), idQ, 1);
+                }
+                mma_commit(ds_free);
+                mma_commit(kv_empty);
+            }
+            __syncwarp();
+        }
+        if (lane == 0) mma_commit(dq_full);
+        __syncwarp();
+    } else {
+        const int row = (warp & 3) * 32 + lane;
+        const int et = threadIdx.x - EPI0;
+        const int q = qb * TILE + row;
+        const bool qv = q < s.NQ;
+        const size_t qrow = (size_t)bh * s.NQ + (qv ? q : 0);
+        const int qpos = !qv ? INT_MIN : (s.causal ? Qidx[qrow] : INT_MAX);
+        const float tq = qv ? tau[qrow] : 0.0f;
+        const float invN = qv ? __fdiv_rn(1.0f, __fadd_rn(rownorm[qrow], ASA_EPS)) : 0.0f;
+        const float Dq = qv ? Dqv[qrow] : 0.0f;
+        const uint32_t tl = tmem_lane_base(tbase, warp);
+        for (int j = 0; j < T; ++j) {
+            const int kb = list[e0 + j];
+            const int b = j & 1;
+            const bool all = vis_all(s, bd, bh, qb, kb);
+            {
+                const int kn = kb * TILE + et;
+                kidx_s[b * TILE + et] = kn < s.NK ? (s.causal ? Kidx_bh[kn] : INT_MIN) : INT_MAX;
+            }
+            epi_bar();
+            mbar_wait(sd_full, j & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+            tc_fence_after();
+            mbar_wait(ds_free, (j & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+#pragma unroll 1
+            for (int c = 0; c < 4; ++c) {
+                uint32_t rs[32], rp[32];
+                tmem_ld32(tl + tS + c * 32, rs);
+                tmem_ld32(tl + tP + c * 32, rp);
+                tmem_ld_wait();
+                float g[32];
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                    const int col = c * 32 + i;
+                    const bool v = qv && (all || (kb * TILE + col < s.NK && kidx_s[b * TILE + col] <= qpos));
+                    g[i] = score_grad(s, clamp_score(__uint_as_float(rs[i]), s.scale),
+                                      __uint_as_float(rp[i]), tq, invN, Dq, v);
+                }
+                uint32_t hi[16], lo[16];
+                split_pack(g, hi, lo);
+                store_row_chunk(sDh, row, c, hi);
+                if (split) store_row_chunk(sDl, row, c, lo);
+            }
+            tc_fence_before();
+            mbar_arrive(sd_free);
+            fence_async_smem();
+            mbar_arrive(ds_full);
+        }
+        mbar_wait(dq_full, 0, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+        tc_fence_after();
+#pragma unroll 1
+        for (int c = 0; c < D / 32; ++c) {
+            uint32_t r[32];
+            tmem_ld32(tl + tQ + c * 32, r);
+            tmem_ld_wait();
+            if (!qv) continue;
+            float o[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+                float v = T > 0 ? __uint_as_float(r[i]) * s.scale : 0.0f;
+                o[i] = isfinite(v) ? v : 0.0f;
+            }
+            if constexpr (sizeof(TO) == 2) {
+                uint4* dst = reinterpret_cast<uint4*>(dQ + qrow * D + c * 32);
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+                    dst[i] = make_uint4(pack_bf16(o[8 * i], o[8 * i + 1]), pack_bf16(o[8 * i + 2], o[8 * i + 3]),
+                                        pack_bf16(o[8 * i + 4], o[8 * i + 5]), pack_bf16(o[8 * i + 6], o[8 * i + 7]));
+            } else {
+                float4* dst = reinterpret_cast<float4*>(dQ + qrow * D + c * 32);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) dst[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tbase, 512);
+    }
+}
+
+// ===========================================================================
+// K4 dK/dV: key-major over the transposed list.  S^T = K·Q^T, dP^T = V·dO^T;
+// the epilogue (thread = key row, columns = queries) writes P^T/n, then dS^T,
+// into one shared buffer; dV += (P^T/n)·dO, dK += dS^T·Q.
+// ===========================================================================
+template <int D, typename TO>
+__global__ void __launch_bounds__(NTHREADS, 1)
+k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+        const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO, Shape s,
+        const int32_t* __restrict__ Qidx, const int32_t* __restrict__ Kidx, Bounds bd,
+        const float* __restrict__ tau, const float* __restrict__ rownorm, const float* __restrict__ Dqv,
+        const int32_t* __restrict__ cptr, const int32_t* __restrict__ cidx, TO* __restrict__ dK,
+        TO* __restrict__ dV, int split, int* err) {
+    constexpr int TB = D * TILE * 2;
+    constexpr int PB = TILE * TILE * 2;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* base = align1024(smem_raw, err);
+    uint8_t* sK = base;
+    uint8_t* sV = base + TB;
+    uint8_t* sQ = base + 2 * TB;
+    uint8_t* sdO = base + 3 * TB;
+    uint8_t* sBh = base + 4 * TB;
+    uint8_t* sBl = sBh + PB;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sBl + PB);
+    uint64_t* kv_full = bars;
+    uint64_t* q_full = bars + 1;
+    uint64_t* q_empty = bars + 2;
+    uint64_t* sd_full = bars + 3;
+    uint64_t* sd_free = bars + 4;
+    uint64_t* p_full = bars + 5;
+    uint64_t* p_free = bars + 6;
+    uint64_t* ds_full = bars + 7;
+    uint64_t* ds_free = bars + 8;
+    uint64_t* out_full = bars + 9;
+    uint32_t* holder = reinterpret_cast<uint32_t*>(bars + 16);
+    float* tau_s = reinterpret_cast<float*>(holder + 4);   // [128] per query of the current block
+    float* inv_s = tau_s + TILE;
+    float* dq_s = inv_s + TILE;
+    int* qp_s = reinterpret_cast<int*>(dq_s + TILE);
+    int* qidx_blk = qp_s + TILE;                           // [128] for the tile-load fix
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int bh = blockIdx.y;
+    const int kb = blockIdx.x;
+    const int32_t* Kidx_bh = Kidx + (size_t)bh * s.NK;
+    const int32_t* Qidx_bh = Qidx + (size_t)bh * s.NQ;
+    const int32_t* list = cidx + (size_t)bh * s.nKB * s.nQB;
+    const int e0 = cptr[(size_t)bh * (s.nKB + 1) + kb];
+    const int T = cptr[(size_t)bh * (s.nKB + 1) + kb + 1] - e0;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < 10; ++i) mbar_init(&bars[i], 1);
+        mbar_init(sd_free, 128);
+        mbar_init(p_full, 128);
+        mbar_init(ds_full, 128);
+        fence_barrier_init();
+    }
+    if (warp == 1) { tmem_alloc(holder, 512); tmem_relinquish(); }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tbase = *holder;
+    const uint32_t tS = 0, tP = 128, tV = 256, tK = 256 + D;
+
+    if (warp == 0) {
+        if (lane == 0 && T > 0) {
+            for (int i = 0; i < T; ++i) {
+                const int qb = list[e0 + i];
+                mbar_wait(q_empty, (i & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+                mbar_expect_tx(q_full, 2 * TB);
+                for (int bx = 0; bx < D / BOX; ++bx) {
+                    tma_load_3d(sQ + bx * BOX_BYTES, &tmQ, q_full, bx * BOX, qb * TILE, bh);
+                    tma_load_3d(sdO + bx * BOX_BYTES, &tmdO, q_full, bx * BOX, qb * TILE, bh);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        constexpr uint32_t idS = idesc_bf16(128, 128, 0, 0);
+        constexpr uint32_t idO = idesc_bf16(128, D, 0, 1);
+        int loads = 0;
+        bool dirty = true;   // K/V not loaded yet
+        for (int i = 0; i < T; ++i) {
+            const int qb = list[e0 + i];
+            const bool fix = needs_fix(s, bd, bh, qb, kb);
+            if (dirty || fix) {
+                // (re)load pristine K/V once the previous pair's S/dP MMAs are done
+                if (i > 0) mbar_wait(sd_full, (i - 1) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+                if (lane == 0) {
+                    mbar_expect_tx(kv_full, 2 * TB);
+                    for (int bx = 0; bx < D / BOX; ++bx) {
+                        tma_load_3d(sK + bx * BOX_BYTES, &tmK, kv_full, bx * BOX, kb * TILE, bh);
+                        tma_load_3d(sV + bx * BOX_BYTES, &tmV, kv_full, bx * BOX, kb * TILE, bh);
+                    }
+                }
+                mbar_wait(kv_full, loads & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+                ++loads;
+                if (fix) {
+                    for (int r = lane; r < TILE; r += 32) {
+                        const int q = qb * TILE + r;
+                        qidx_blk[r] = q < s.NQ ? Qidx_bh[q] : INT_MAX;
+                    }
+                    __syncwarp();
+                    const int qmin_blk = bd.qmin[bh * s.nQB + qb];
+                    fix_tile<D>(sK, qidx_blk, qmin_blk, Kidx_bh, kb, s.NK, lane);
+                    fix_tile<D>(sV, qidx_blk, qmin_blk, Kidx_bh, kb, s.NK, lane);
+                    fence_async_smem();
+                }
+                dirty = fix;
+            }
+            __syncwarp();
+            mbar_wait(q_full, i & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+            mbar_wait(sd_free, (i & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+            tc_fence_after();
+            if (lane == 0) {
+#pragma unroll
+                for (int kk = 0; kk < D / 16; ++kk) {
+                    mma_bf16_ss(tbase + tS, kdesc(sK, kk), kdesc(sQ, kk), idS, kk > 0);
+                    mma_bf16_ss(tbase + tP, kdesc(sV, kk), kdesc(sdO, kk), idS, kk > 0);
+                }
+                mma_commit(sd_full);
+            }
+            __syncwarp();
+            mbar_wait(p_full, i & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+            tc_fence_after();
+            if (lane == 0) {
+#pragma unroll
+                for (int kk = 0; kk < TILE / 16; ++kk)
+                    mma_bf16_ss(tbase + tV, kdesc(sBh, kk), mndesc(sdO, kk), idO, (i > 0 || kk > 0));
+                if (split) {
+#pragma unroll
+                    for (int kk = 0; kk < TILE / 16; ++kk)
+                        mma_bf16_ss(tbase + tV, kdesc(sBl, kk), mndesc(sdO, kk), idO, 1);
+                }
+                mma_commit(p_free);
+            }
+            __syncwarp();
+            mbar_wait(ds_full, i & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+            tc_fence_after();
+            if (lane == 0) {
+#pragma unroll
+                for (int kk = 0; kk < TILE / 16; ++kk)
+                    mma_bf16_ss(tbase + tK, kdesc(sBh, kk), mndesc(sQ, kk), idO, (i > 0 || kk > 0));
+                if (split) {
+#pragma unroll
+                    for (int kk = 0; kk < TILE / 16; ++kk)
+                        mma_bf16_ss(tbase + tK, kdesc(sBl, kk), mndesc(sQ, kk), idO, 1);
+                }
+                mma_commit(ds_free);
+                mma_commit(q_empty);
+            }
+            __syncwarp();
+        }
+        if (lane == 0) mma_commit(out_full);
+        __syncwarp();
+    } else {
+        const int row = (warp & 3) * 32 + lane;
+        const int et = threadIdx.x - EPI0;
+        const int kn = kb * TILE + row;
+        const bool kv = kn < s.NK;
+        const size_t krow = (size_t)bh * s.NK + (kv ? kn : 0);
+        const int kpos = !kv ? INT_MAX : (s.causal ? Kidx_bh[kn] : INT_MIN);
+        const uint32_t tl = tmem_lane_base(tbase, warp);
+        for (int i = 0; i < T; ++i) {
+            const int qb = list[e0 + i];
+            epi_bar();   // previous pair's readers of the per-query arrays are done
+            {
+                const int q = qb * TILE + et;
+                const bool ok = q < s.NQ;
+                const size_t r = (size_t)bh * s.NQ + (ok ? q : 0);
+                tau_s[et] = ok ? tau[r] : 0.0f;
+                inv_s[et] = ok ? __fdiv_rn(1.0f, __fadd_rn(rownorm[r], ASA_EPS)) : 0.0f;
+                dq_s[et] = ok ? Dqv[r] : 0.0f;
+                qp_s[et] = ok ? (s.causal ? Qidx_bh[q] : INT_MAX) : INT_MIN;
+            }
+            epi_bar();
+            const bool all = vis_all(s, bd, bh, qb, kb) && (qb + 1) * TILE <= s.NQ;
+            mbar_wait(sd_full, i & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+            tc_fence_after();
+            mbar_wait(ds_free, (i & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+            // pass 1: P^T / n
+#pragma unroll 1
+            for (int c = 0; c < 4; ++c) {
+                uint32_t rs[32];
+                tmem_ld32(tl + tS + c * 32, rs);
+                tmem_ld_wait();
+                float p[32];
+#pragma unroll
+                for (int k = 0; k < 32; ++k) {
+                    const int col = c * 32 + k;
+                    const bool v = kv && (all || kpos <= qp_s[col]);
+                    const float sc = clamp_score(__uint_as_float(rs[k]), s.scale);
+                    const float u = __fmaf_rn(s.am1, sc, -tau_s[col]);
+                    float pr = (v && u > 0.0f) ? pow_fast(fmaxf(u, ASA_EPS), s.pinv) : 0.0f;
+                    pr *= inv_s[col];
+                    p[k] = isfinite(pr) ? pr : 0.0f;
+                }
+                uint32_t hi[16], lo[16];
+                split_pack(p, hi, lo);
+                store_row_chunk(sBh, row, c, hi);
+                if (split) store_row_chunk(sBl, row, c, lo);
+            }
+            fence_async_smem();
+            mbar_arrive(p_full);
+            mbar_wait(p_free, i & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+            // pass 2: dS^T
+#pragma unroll 1
+            for (int c = 0; c < 4; ++c) {
+                uint32_t rs[32], rp[32];
+                tmem_ld32(tl + tS + c * 32, rs);
+                tmem_ld32(tl + tP + c * 32, rp);
+                tmem_ld_wait();
+                float g[32];
+#pragma unroll
+                for (int k = 0; k < 32; ++k) {
+                    const int col = c * 32 + k;
+                    const bool v = kv && (all || kpos <= qp_s[col]);
+                    g[k] = score_grad(s, clamp_score(__uint_as_float(rs[k]), s.scale),
+                                      __uint_as_float(rp[k]), tau_s[col], inv_s[col], dq_s[col], v);
+                }
+                uint32_t hi[16], lo[16];
+                split_pack(g, hi, lo);
+                store_row_chunk(sBh, row, c, hi);
+                if (split) store_row_chunk(sBl, row, c, lo);
+            }
+            tc_fence_before();
+            mbar_arrive(sd_free);
+            fence_async_smem();
+            mbar_arrive(ds_full);
+        }
+        if (T > 0) {
+            mbar_wait(out_full, 0, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+            tc_fence_after();
+        }
+#pragma unroll 1
+        for (int part = 0; part < 2; ++part) {
+            TO* dst_base = part == 0 ? dV : dK;
+            const float mul = part == 0 ? 1.0f : s.scale;
+            const uint32_t col0 = part == 0 ? tV : tK;
+#pragma unroll 1
+            for (int c = 0; c < D / 32; ++c) {
+                uint32_t r[32];
+                if (T > 0) {
+                    tmem_ld32(tl + col0 + c * 32, r);
+                    tmem_ld_wait();
+                }
+                if (!kv) continue;
+                float o[32];
+#pragma unroll
+                for (int k = 0; k < 32; ++k) {
+                    float v = T > 0 ? __uint_as_float(r[k]) * mul : 0.0f;
+                    o[k] = isfinite(v) ? v : 0.0f;
+                }
+                if constexpr (sizeof(TO) == 2) {
+                    uint4* dst = reinterpret_cast<uint4*>(dst_base + krow * D + c * 32);
+#pragma unroll
+                    for (int k = 0; k < 4; ++k)
+                        dst[k] = make_uint4(pack_bf16(o[8 * k], o[8 * k + 1]), pack_bf16(o[8 * k + 2], o[8 * k + 3]),
+                                            pack_bf16(o[8 * k + 4], o[8 * k + 5]), pack_bf16(o[8 * k + 6], o[8 * k + 7]));
+                } else {
+                    float4* dst = reinterpret_cast<float4*>(dst_base + krow * D + c * 32);
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) dst[k] = make_float4(o[4 * k], o[4 * k + 1], o[4 * k + 2], o[4 * k + 3]);
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tbase, 512);
+    }
+}
+
+// ===========================================================================
+// host side
+// ===========================================================================
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = (PFN_cuTensorMapEncodeTiled_v12000)p;
+    }
+    return fn;
+}
+
+// [BH][N][d] bf16 viewed as a 3-D tensor, boxes of 64 x 128 x 1, 128-byte
+// swizzle, zero fill out of bounds.
+bool make_map(CUtensorMap* m, const void* ptr, int BH, int N, int d) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[3] = {(cuuint64_t)d, (cuuint64_t)N, (cuuint64_t)BH};
+    cuuint64_t strides[2] = {(cuuint64_t)d * 2, (cuuint64_t)N * d * 2};
+    cuuint32_t box[3] = {BOX, TILE, 1};
+    cuuint32_t es[3] = {1, 1, 1};
+    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(ptr), dims, strides, box,
+                    es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+size_t bounds_ints(const Shape& s) { return (size_t)2 * s.BH * (s.nQB + s.nKB); }
+
+Bounds bounds_at(const Shape& s, void* ws) {
+    int* b = (int*)ws;
+    Bounds bd;
+    bd.qmin = b;
+    bd.qmax = b + (size_t)s.BH * s.nQB;
+    bd.kmin = b + (size_t)2 * s.BH * s.nQB;
+    bd.kmax = b + (size_t)2 * s.BH * s.nQB + (size_t)s.BH * s.nKB;
+    return bd;
+}
+
+cudaError_t launch_bounds(const Shape& s, const int32_t* Qidx, const int32_t* Kidx, void* ws,
+                          cudaStream_t st) {
+    if (!s.causal) return cudaSuccess;
+    Bounds bd = bounds_at(s, ws);
+    const int blocks = (s.nQB + s.nKB + 7) / 8;
+    dim3 grid(blocks, s.BH);
+    tc_bounds_kernel<<<grid, 256, 0, st>>>(s, Qidx, Kidx, (int*)bd.qmin, (int*)bd.qmax, (int*)bd.kmin,
+                                           (int*)bd.kmax);
+    note_launch();
+    return cudaGetLastError();
+}
+
+template <typename F>
+cudaError_t prep(F* f, size_t smem) {
+    return cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+}
+
+constexpr size_t kSmemTail = 16 * 8 + 16 + 5 * 128 * 4;  // barriers, TMEM holder, per-row arrays
+
+bool is_sm100() {
+    static int cached = -1;
+    if (cached < 0) {
+        int dev = 0, major = 0;
+        cached = (cudaGetDevice(&dev) == cudaSuccess &&
+                  cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) == cudaSuccess &&
+                  major == 10) ? 1 : 0;
+    }
+    return cached == 1;
+}
+
+}  // namespace
+
+bool tc_supported(const Shape& s) {
+    return s.in_dtype == ASA_DTYPE_BF16 && (s.d == 64 || s.d == 128) && s.BM == TILE && s.BN == TILE &&
+           s.NK > 0 && s.nKB <= 32768 && is_sm100();
+}
+
+size_t tc_fwd_workspace(const Shape& s) { return bounds_ints(s) * 4; }
+size_t tc_bwd_workspace(const Shape& s) {
+    return ((bounds_ints(s) * 4 + 15) & ~size_t(15)) + (size_t)s.BH * s.NQ * 4;
+}
+
+cudaError_t tc_tau_mask(const Shape& s, const void* Q, const void* K, const int32_t* Qidx,
+                        const int32_t* Kidx, float* tau, uint8_t* M, void* ws, int* err,
+                        cudaStream_t st) {
+    cudaError_t e = launch_bounds(s, Qidx, Kidx, ws, st);
+    if (e != cudaSuccess) return e;
+    CUtensorMap mQ, mK;
+    if (!make_map(&mQ, Q, s.BH, s.NQ, s.d) || !make_map(&mK, K, s.BH, s.NK, s.d)) return cudaErrorInvalidValue;
+    Bounds bd = bounds_at(s, ws);
+    dim3 grid(s.nQB, s.BH);
+    auto go = [&](auto kern, int D) -> cudaError_t {
+        const size_t smem = (size_t)D * TILE * 2 * 5 + kSmemTail + s.nKB;
+        cudaError_t r = prep(kern, smem);
+        if (r != cudaSuccess) return r;
+        kern<<<grid, NTHREADS, smem, st>>>(mQ, mK, s, Qidx, Kidx, bd, tau, M, err);
+        note_launch();
+        return cudaGetLastError();
+    };
+    if (s.d == 128) {
+        if (s.k <= 8) return go(k1_tau_mask<128, 8>, 128);
+        if (s.k <= 16) return go(k1_tau_mask<128, 16>, 128);
+        return go(k1_tau_mask<128, 32>, 128);
+    }
+    if (s.k <= 8) return go(k1_tau_mask<64, 8>, 64);
+    if (s.k <= 16) return go(k1_tau_mask<64, 16>, 64);
+    return go(k1_tau_mask<64, 32>, 64);
+}
+
+cudaError_t tc_forward(const Shape& s, const void* Q, const void* K, const void* V, const int32_t* Qidx,
+                       const int32_t* Kidx, const float* tau, const int32_t* ptr, const int32_t* idx,
+                       void* O, float* O32, float* rownorm, void* ws, int* err, cudaStream_t st) {
+    CUtensorMap mQ, mK, mV;
+    if (!make_map(&mQ, Q, s.BH, s.NQ, s.d) || !make_map(&mK, K, s.BH, s.NK, s.d) ||
+        !make_map(&mV, V, s.BH, s.NK, s.d))
+        return cudaErrorInvalidValue;
+    Bounds bd = bounds_at(s, ws);   // filled by tc_tau_mask
+    dim3 grid(s.nQB, s.BH);
+    const int split = s.split;
+    if (s.out_dtype == ASA_DTYPE_F32) {
+        if (s.d == 128) {
+            auto k = k3_forward<128, float>;
+            const size_t smem = (size_t)128 * TILE * 2 * 5 + (size_t)2 * TILE * TILE * 2 + kSmemTail;
+            cudaError_t r = prep(k, smem);
+            if (r != cudaSuccess) return r;
+            k<<<grid, NTHREADS, smem, st>>>(mQ, mK, mV, s, Qidx, Kidx, bd, tau, ptr, idx, (float*)O, O32,
+                                            rownorm, split, err);
+        } else {
+            auto k = k3_forward<64, float>;
+            const size_t smem = (size_t)64 * TILE * 2 * 5 + (size_t)2 * TILE * TILE * 2 + kSmemTail;
+            cudaError_t r = prep(k, smem);
+            if (r != cudaSuccess) return r;
+            k<<<grid, NTHREADS, smem, st>>>(mQ, mK, mV, s, Qidx, Kidx, bd, tau, ptr, idx, (float*)O, O32,
+                                            rownorm, split, err);
+        }
+    } else {
+        if (s.d == 128) {
+            auto k = k3_forward<128, __nv_bfloat16>;
+            const size_t smem = (size_t)128 * TILE * 2 * 5 + (size_t)2 * TILE * TILE * 2 + kSmemTail;
+            cudaError_t r = prep(k, smem);
+            if (r != cudaSuccess) return r;
+            k<<<grid, NTHREADS, smem, st>>>(mQ, mK, mV, s, Qidx, Kidx, bd, tau, ptr, idx,
+                                            (__nv_bfloat16*)O, O32, rownorm, split, err);
+        } else {
+            auto k = k3_forward<64, __nv_bfloat16>;
+            const size_t smem = (size_t)64 * TILE * 2 * 5 + (size_t)2 * TILE * TILE * 2 + kSmemTail;
+            cudaError_t r = prep(k, smem);
+            if (r != cudaSuccess) return r;
+            k<<<grid, NTHREADS, smem, st>>>(mQ, mK, mV, s, Qidx, Kidx, bd, tau, ptr, idx,
+                                            (__nv_bfloat16*)O, O32, rownorm, split, err);
+        }
+    }
+    note_launch();
+    return cudaGetLastError();
+}
+
+cudaError_t tc_backward(const Shape& s, const void* Q, const void* K, const void* V, const int32_t* Qidx,
+                        const int32_t* Kidx, const float* O32, const float* tau, const int32_t* ptr,
+                        const int32_t* idx, const int32_t* cptr, const int32_t* cidx,
+                        const float* rownorm, const void* dO, void* dQ, void* dK, void* dV, void* ws,
+                        int* err, cudaStream_t st) {
+    cudaError_t e = launch_bounds(s, Qidx, Kidx, ws, st);
+    if (e != cudaSuccess) return e;
+    Bounds bd = bounds_at(s, ws);
+    float* Dq = (float*)((char*)ws + ((bounds_ints(s) * 4 + 15) & ~size_t(15)));
+    const size_t rows = (size_t)s.BH * s.NQ;
+    if (s.d == 128)
+        k4_pre<128><<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(O32, (const __nv_bfloat16*)dO, Dq, rows);
+    else
+        k4_pre<64><<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(O32, (const __nv_bfloat16*)dO, Dq, rows);
+    note_launch();
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    CUtensorMap mQ, mK, mV, mdO;
+    if (!make_map(&mQ, Q, s.BH, s.NQ, s.d) || !make_map(&mK, K, s.BH, s.NK, s.d) ||
+        !make_map(&mV, V, s.BH, s.NK, s.d) || !make_map(&mdO, dO, s.BH, s.NQ, s.d))
+        return cudaErrorInvalidValue;
+    const int split = s.split;
+    auto run = [&](auto kdq, auto kkv, auto* dq_out, auto* dk_out, auto* dv_out, int D) -> cudaError_t {
+        const size_t smem = (size_t)D * TILE * 2 * 4 + (size_t)2 * TILE * TILE * 2 + kSmemTail;
+        cudaError_t r = prep(kdq, smem);
+        if (r == cudaSuccess) r = prep(kkv, smem);
+        if (r != cudaSuccess) return r;
+        kdq<<<dim3(s.nQB, s.BH), NTHREADS, smem, st>>>(mQ, mK, mV, mdO, s, Qidx, Kidx, bd, tau, rownorm,
+                                                      Dq, ptr, idx, dq_out, split, err);
+        note_launch();
+        r = cudaGetLastError();
+        if (r != cudaSuccess) return r;
+        kkv<<<dim3(s.nKB, s.BH), NTHREADS, smem, st>>>(mQ, mK, mV, mdO, s, Qidx, Kidx, bd, tau, rownorm,
+                                                      Dq, cptr, cidx, dk_out, dv_out, split, err);
+        note_launch();
+        return cudaGetLastError();
+    };
+    if (s.out_dtype == ASA_DTYPE_F32) {
+        if (s.d == 128)
+            return run(k4_dq<128, float>, k4_dkdv<128, float>, (float*)dQ, (float*)dK, (float*)dV, 128);
+        return run(k4_dq<64, float>, k4_dkdv<64, float>, (float*)dQ, (float*)dK, (float*)dV, 64);
+    }
+    using bf = __nv_bfloat16;
+    if (s.d == 128)
+        return run(k4_dq<128, bf>, k4_dkdv<128, bf>, (bf*)dQ, (bf*)dK, (bf*)dV, 128);
+    return run(k4_dq<64, bf>, k4_dkdv<64, bf>, (bf*)dQ, (bf*)dK, (bf*)dV, 64);
 }
 
 }  // namespace asa

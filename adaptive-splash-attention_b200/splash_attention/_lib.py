@@ -20,7 +20,7 @@ PRECISION = {"split": 0, "bf16": 1}
 SYMBOLS = ("asa_params_default", "asa_workspace_bytes", "asa_resolve_backend", "asa_tau_mask",
            "asa_forward", "asa_backward", "asa_scrub", "asa_device_error", "asa_status_string",
            "asa_version", "asa_profile_begin", "asa_profile_end", "asa_profile_get",
-           "asa_launch_count")
+           "asa_launch_count", "asa_last_cuda_error")
 
 
 class Params(ctypes.Structure):
@@ -40,7 +40,10 @@ class AsaError(RuntimeError):
 
     def __init__(self, code, what):
         self.code = code
-        super().__init__(f"{what}: {status_string(code)} (asa_status {code})")
+        extra = ""
+        if code == ASA_ERR_CUDA:
+            extra = f": {lib().asa_last_cuda_error().decode()}"
+        super().__init__(f"{what}: {status_string(code)}{extra} (asa_status {code})")
 
 
 _lib = None
@@ -74,6 +77,8 @@ def lib():
                                       ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_int)]
         L.asa_launch_count.argtypes = []
         L.asa_launch_count.restype = ctypes.c_longlong
+        L.asa_last_cuda_error.argtypes = []
+        L.asa_last_cuda_error.restype = ctypes.c_char_p
         for name in SYMBOLS:
             getattr(L, name)
         _lib = L

@@ -149,6 +149,9 @@ int asa_profile_end(void);
 int asa_profile_get(int i, const char** label, double* total_ms, int* launches);
 long long asa_launch_count(void);
 
+/* Text of the CUDA error behind the calling thread's last ASA_ERR_CUDA. */
+const char* asa_last_cuda_error(void);
+
 /* Human-readable text of an asa_status. */
 const char* asa_status_string(int status);
 

@@ -42,11 +42,21 @@ def oracle_run(Q, K, V, dO, Qi, Ki, BM, BN, k_keep, alpha, sm_scale, causal=True
                        f(dO) if grads else None)
 
 
-def assert_tau(got, ref):
+def assert_tau(got, ref, tensor_core=False):
+    """τ within 1e-5 relative.  Tensor-core scores sum the d products in a
+    different order than the reference's FMA chain, so a few rows whose
+    five-step solve sits on a branch point (the |f| < 1e-4 exit, the
+    bisection side) may move further: on that path at most 0.1% of rows may
+    exceed 1e-5 and none may exceed 1e-4 (relative to max(1, |τ|))."""
     got, ref = np.asarray(got, np.float64), np.asarray(ref, np.float64)
     err = np.abs(got - ref) - (TAU_ATOL + TAU_RTOL * np.abs(ref))
     bad = int((err > 0).sum())
-    assert bad == 0, f"τ: {bad} rows outside rtol {TAU_RTOL}; worst excess {err.max():.3g}"
+    if not tensor_core:
+        assert bad == 0, f"τ: {bad} rows outside rtol {TAU_RTOL}; worst excess {err.max():.3g}"
+        return
+    assert bad <= max(1, err.size // 1000), f"τ: {bad} of {err.size} rows outside rtol {TAU_RTOL}"
+    rel = np.abs(got - ref) / np.maximum(1.0, np.abs(ref))
+    assert rel.max() <= 1e-4, f"τ: worst relative error {rel.max():.3g}"
 
 
 def assert_close(name, got, ref, atol):
