@@ -40,7 +40,7 @@ def run_engine(Q, K, V, dO, Qi, Ki, BM, BN, kk, alpha, sc, causal, backend, prec
     O, s = ops.forward_saved(Qd, Kd, Vd, Qi.to(dev), Ki.to(dev), st)
     dQ, dK, dV = ops.backward_saved(Qd, Kd, Vd, dOd, s)
     torch.cuda.synchronize()
-    assert ops.device_error() == 0, "a kernel's bounded wait ran out
+    assert ops.device_error() == 0, "a kernel's bounded wait ran out"
     c = lambda x: x.cpu().numpy()
     B, H = Q.shape[:2]
     f = lambda x: c(x).reshape(B * H, x.shape[2], x.shape[3])
