@@ -334,6 +334,55 @@ int asa_backward(const asa_params* p, const void* Q, const void* K, const void* 
     return cuda_status(e);
 }
 
+// ---- allocation-free τ / block mask ------------------------------------------
+// Some callers cannot allocate device memory at the point where they need
+// the mask: code running inside another framework's custom allocator or
+// memory pool that forbids cudaMalloc from a plugin, or an embedded host that
+// has handed all device memory to a fixed arena.  For them
+// asa_tau_mask_noalloc() takes its scratch from this file-scope device
+// array instead of a caller workspace.  The array lives on every GPU that
+// loads the library, for the life of the process.
+static __device__ __align__(256) unsigned char g_asa_noalloc_scratch[ASA_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+void* g_noalloc_ptr[kMaxDevices];
+
+// Device address of g_asa_noalloc_scratch on the current device.  Host code
+// must not use the symbol itself (it names a host-side shadow); the address
+// comes from cudaGetSymbolAddress, looked up once per device with that
+// device current.
+int noalloc_scratch(void** out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_status(e);
+    if (dev < 0 || dev >= kMaxDevices) return ASA_ERR_UNSUPPORTED;
+    if (!g_noalloc_ptr[dev]) {
+        void* ptr = nullptr;
+        e = cudaGetSymbolAddress(&ptr, g_asa_noalloc_scratch);
+        if (e != cudaSuccess) return cuda_status(e);
+        g_noalloc_ptr[dev] = ptr;
+    }
+    *out = g_noalloc_ptr[dev];
+    return ASA_OK;
+}
+}  // namespace
+
+int asa_tau_mask_noalloc(const asa_params* p, const void* Q, const void* K, const int32_t* Qidx,
+                         const int32_t* Kidx, float* tau, uint8_t* M, int32_t* csr_ptr,
+                         int32_t* csr_idx, asa_stream_t stream) {
+    size_t need = 0;
+    int rc = asa_workspace_bytes(p, &need, nullptr);
+    if (rc) return rc;
+    if (need > ASA_NOALLOC_SCRATCH_BYTES) return ASA_ERR_WORKSPACE;
+    void* scratch = nullptr;
+    rc = noalloc_scratch(&scratch);
+    if (rc) return rc;
+    // Every call rewrites the part of the scratch it reads (the per-block
+    // index bounds) before reading it, so nothing needs clearing here.
+    return asa_tau_mask(p, Q, K, Qidx, Kidx, tau, M, csr_ptr, csr_idx, scratch,
+                        ASA_NOALLOC_SCRATCH_BYTES, stream);
+}
+
 int asa_scrub(int dtype, void* x, size_t n, void* ws, asa_stream_t stream) {
     if ((dtype != ASA_DTYPE_F32 && dtype != ASA_DTYPE_BF16) || (n && !x) || !ws)
         return ASA_ERR_INVALID;

@@ -48,7 +48,6 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, long l
     if (mbar_try(bar, parity)) return true;
     for (long long i = 0; i < spins; ++i) {
         if (mbar_try(bar, parity)) return true;
-        if (i > 64) __nanosleep(64);
         // once any wait has given up, the rest give up at once
         if ((i & 1023) == 1023 && err && *reinterpret_cast<volatile int*>(err) != 0) return false;
     }

@@ -20,7 +20,8 @@ PRECISION = {"split": 0, "bf16": 1}
 SYMBOLS = ("asa_params_default", "asa_workspace_bytes", "asa_resolve_backend", "asa_tau_mask",
            "asa_forward", "asa_backward", "asa_scrub", "asa_device_error", "asa_status_string",
            "asa_version", "asa_profile_begin", "asa_profile_end", "asa_profile_get",
-           "asa_launch_count", "asa_last_cuda_error")
+           "asa_launch_count", "asa_last_cuda_error", "asa_tau_mask_noalloc")
+NOALLOC_SCRATCH_BYTES = 1 << 20
 
 
 class Params(ctypes.Structure):
@@ -77,6 +78,7 @@ def lib():
                                       ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_int)]
         L.asa_launch_count.argtypes = []
         L.asa_launch_count.restype = ctypes.c_longlong
+        L.asa_tau_mask_noalloc.argtypes = [pp, vp, vp, vp, vp, vp, vp, vp, vp, vp]
         L.asa_last_cuda_error.argtypes = []
         L.asa_last_cuda_error.restype = ctypes.c_char_p
         for name in SYMBOLS:

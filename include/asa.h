@@ -103,6 +103,27 @@ int asa_tau_mask(const asa_params* p, const void* Q, const void* K,
                  float* tau, uint8_t* M, int32_t* csr_ptr, int32_t* csr_idx,
                  void* ws, size_t ws_bytes, asa_stream_t stream);
 
+/* asa_tau_mask without a workspace argument: the same τ, block mask and CSR,
+ * for callers that cannot allocate device memory (a plugin inside a host
+ * framework whose allocator forbids cudaMalloc, or an embedded runtime that
+ * owns all device memory up front).  No counterpart in the reference, which
+ * allocates its temporaries with torch::zeros on every call.
+ *
+ * Scratch comes from a fixed device array of ASA_NOALLOC_SCRATCH_BYTES inside
+ * the library (present on every GPU that loads it until the process exits);
+ * shapes whose scratch need (asa_workspace_bytes' fwd_bytes) exceeds it are
+ * rejected with ASA_ERR_WORKSPACE before anything is launched.  The first
+ * call on each device looks the array's address up (cudaGetSymbolAddress);
+ * make that first call before any stream capture.  Calls share the one
+ * array, so two calls that overlap on the GPU (different streams, or
+ * different host threads) race; serialise them.  Nothing is allocated: no
+ * cudaMalloc, cudaFree or allocating library call. */
+#define ASA_NOALLOC_SCRATCH_BYTES (1u << 20)
+int asa_tau_mask_noalloc(const asa_params* p, const void* Q, const void* K,
+                         const int32_t* Q_idx, const int32_t* K_idx,
+                         float* tau, uint8_t* M, int32_t* csr_ptr, int32_t* csr_idx,
+                         asa_stream_t stream);
+
 /* Full forward: τ / mask / CSR, then O = Σ p v / (Σ p + 1e-8) over the active
  * tiles (reference forward_splash :537-609 and splash_forward_sparse
  * :244-341).  O is out_dtype; O32 (optional, may be NULL or equal to O when
