@@ -102,6 +102,21 @@ struct TopK {
         }
     }
     __device__ __forceinline__ float threshold() const { return v[KM - 1]; }
+    // Insert under the total order (value desc, key index asc): used to merge
+    // two partial lists of disjoint key sets; the result is the first k of
+    // that order, exactly what sequential strict-'>' insertion in key order
+    // keeps.
+    __device__ __forceinline__ void insert_lex(float s, int idx) {
+#pragma unroll
+        for (int j = KM - 1; j >= 0; --j) {
+            const bool gt = s > v[j] || (s == v[j] && idx < i[j]);
+            const bool gt_up = (j > 0) ? (s > v[j - 1] || (s == v[j - 1] && idx < i[j - 1])) : false;
+            if (gt) {
+                v[j] = gt_up ? v[j - 1] : s;
+                i[j] = gt_up ? i[j - 1] : idx;
+            }
+        }
+    }
     __device__ __forceinline__ void insert(float s, int idx) {
 #pragma unroll
         for (int j = KM - 1; j >= 0; --j) {

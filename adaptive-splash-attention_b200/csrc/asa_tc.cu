@@ -29,6 +29,7 @@
 #include "asa_sm100.cuh"
 #include <climits>
 #include <cudaTypedefs.h>
+#include <type_traits>
 
 namespace asa {
 namespace {
@@ -38,8 +39,9 @@ using namespace sm100;
 constexpr int TILE = 128;
 constexpr int BOX = 64;                    // bf16 elements per 128-byte swizzle row
 constexpr int BOX_BYTES = TILE * 128;      // one 64-column box of 128 rows
-constexpr int NTHREADS = 192;
+constexpr int NTHREADS = 320;              // producer warp, MMA warp, two 4-warp epilogue groups
 constexpr int EPI0 = 64;                   // first epilogue thread
+constexpr int NEPI = 256;                  // epilogue threads
 
 struct Bounds {
     const int* qmin;   // [BH][nQB]
@@ -58,7 +60,7 @@ __device__ __forceinline__ uint8_t* align1024(uint8_t* p, int* err) {
 }
 
 __device__ __forceinline__ void epi_bar() {
-    asm volatile("bar.sync 1, 128;" ::: "memory");
+    asm volatile("bar.sync 1, 256;" ::: "memory");
 }
 
 __device__ __forceinline__ float neg_inf() { return __int_as_float(0xff800000); }
@@ -156,18 +158,47 @@ __device__ __forceinline__ void split_pack(const float (&x)[32], uint32_t (&hi)[
     }
 }
 
-// p = u^e for the entmax transform inside the tile loops (fp32; the result is
-// rounded to a bf16 pair afterwards, so 1-2 ulp here do not matter).
-__device__ __forceinline__ float pow_fast(float x, const PowSpec& s) {
-    switch (s.kind) {
-        case 1: return x;
-        case 2: return x * x;
-        case 3: return x * x * x;
-        case 4: { const float y = x * x; return y * y; }
-        case 5: return 1.0f;
-        case 6: return 1.0f / x;
-        default: return powf(x, s.e);
-    }
+// v[i] for a runtime i in [0, 32) without local memory: a 5-level select tree.
+__device__ __forceinline__ float pick32(const float (&v)[32], int i) {
+    float a[16], b[8], c[4], d[2];
+#pragma unroll
+    for (int k = 0; k < 16; ++k) a[k] = (i & 1) ? v[2 * k + 1] : v[2 * k];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) b[k] = (i & 2) ? a[2 * k + 1] : a[2 * k];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) c[k] = (i & 4) ? b[2 * k + 1] : b[2 * k];
+#pragma unroll
+    for (int k = 0; k < 2; ++k) d[k] = (i & 8) ? c[2 * k + 1] : c[2 * k];
+    return (i & 16) ? d[1] : d[0];
+}
+
+// x^e with the exponent class fixed at compile time (PK = PowSpec kind:
+// 1 x, 2 x^2, 3 x^3, 4 x^4, 5 one, 0 powf with runtime e).
+template <int PK>
+__device__ __forceinline__ float powk(float x, float e) {
+    if constexpr (PK == 1) return x;
+    else if constexpr (PK == 2) return x * x;
+    else if constexpr (PK == 3) return x * x * x;
+    else if constexpr (PK == 4) { const float y = x * x; return y * y; }
+    else if constexpr (PK == 5) return 1.0f;
+    else return powf(x, e);
+}
+
+// Entmax weight of one score (reference :311-316) for a known exponent class.
+template <int PK>
+__device__ __forceinline__ float entmax_pk(float u, float e) {
+    float p = u > 0.0f ? powk<PK>(fmaxf(u, ASA_EPS), e) : 0.0f;
+    if constexpr (PK == 0 || PK == 3 || PK == 4) p = isfinite(p) ? p : 0.0f;
+    return p;
+}
+
+// Score gradient (reference :481-507): g = u^{(2-α)/(α-1)} · (dP - D) / n
+// for u > EPS, else 0; non-finite -> 0.
+template <int PK>
+__device__ __forceinline__ float grad_pk(float u, float e, float dP, float Dq, float invN) {
+    if (!(u > ASA_EPS)) return 0.0f;
+    const float g = powk<PK>(fmaxf(u, ASA_EPS), e) * (dP - Dq) * invN;
+    return isfinite(g) ? g : 0.0f;
 }
 
 __device__ __forceinline__ uint32_t tmem_lane_base(uint32_t tbase, int warp) {
@@ -213,6 +244,10 @@ __global__ void tc_bounds_kernel(Shape s, const int32_t* __restrict__ Qidx,
 // ===========================================================================
 // K1: τ and block mask
 // ===========================================================================
+// The two epilogue warpgroups split every S tile by columns (warpgroup h owns
+// keys [64h, 64h+64) of each tile) and keep one partial top-k list per row;
+// warpgroup 0 merges the two lists under (score desc, key asc) -- the order
+// the reference's sequential strict-'>' insertion produces -- and solves τ.
 template <int D, int KM>
 __global__ void __launch_bounds__(NTHREADS, 1)
 k1_tau_mask(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK, Shape s,
@@ -224,7 +259,9 @@ k1_tau_mask(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
     uint8_t* base = align1024(smem_raw, err);
     uint8_t* sQ = base;
     uint8_t* sK = base + TB;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(sK + S * TB);
+    float* topv_s = reinterpret_cast<float*>(sK + S * TB);     // [128][KM] warpgroup 1's lists
+    int* topi_s = reinterpret_cast<int*>(topv_s + TILE * KM);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(topi_s + TILE * KM);
     uint64_t* q_full = bars;
     uint64_t* k_full = bars + 1;
     uint64_t* k_empty = bars + 1 + S;
@@ -243,15 +280,17 @@ k1_tau_mask(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
     if (threadIdx.x == 0) {
         mbar_init(q_full, 1);
         for (int i = 0; i < S; ++i) { mbar_init(&k_full[i], 1); mbar_init(&k_empty[i], 1); }
-        for (int i = 0; i < 2; ++i) { mbar_init(&s_full[i], 1); mbar_init(&s_free[i], 128); }
+        for (int i = 0; i < 2; ++i) { mbar_init(&s_full[i], 1); mbar_init(&s_free[i], NEPI); }
         fence_barrier_init();
     }
     if (warp == 1) { tmem_alloc(holder, 256); tmem_relinquish(); }
     if (threadIdx.x >= EPI0) {
         const int r = threadIdx.x - EPI0;
-        const int q = qb * TILE + r;
-        qidx_blk[r] = (q < s.NQ && s.causal) ? Qidx[(size_t)bh * s.NQ + q] : INT_MAX;
-        for (int i = r; i < s.nKB; i += 128) flags[i] = 0;
+        if (r < TILE) {
+            const int q = qb * TILE + r;
+            qidx_blk[r] = (q < s.NQ && s.causal) ? Qidx[(size_t)bh * s.NQ + q] : INT_MAX;
+        }
+        for (int i = r; i < s.nKB; i += NEPI) flags[i] = 0;
     }
     tc_fence_before();
     __syncthreads();
@@ -306,6 +345,7 @@ k1_tau_mask(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
     } else {
         const int row = (warp & 3) * 32 + lane;
         const int et = threadIdx.x - EPI0;
+        const int h = et / TILE;                  // column half of each tile
         const int q = qb * TILE + row;
         const bool qv = q < s.NQ;
         const int qpos = !qv ? INT_MIN : (s.causal ? Qidx[(size_t)bh * s.NQ + q] : INT_MAX);
@@ -317,7 +357,7 @@ k1_tau_mask(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
             if (!vis_any(s, bd, bh, qb, kb)) continue;
             const int b = j & 1;
             const bool all = vis_all(s, bd, bh, qb, kb);
-            {
+            if (et < TILE) {
                 const int kn = kb * TILE + et;
                 kidx_s[b * TILE + et] = kn < s.NK ? (s.causal ? Kidx_bh[kn] : INT_MIN) : INT_MAX;
             }
@@ -325,38 +365,52 @@ k1_tau_mask(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
             mbar_wait(&s_full[b], (j >> 1) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
             tc_fence_after();
 #pragma unroll 1
-            for (int c = 0; c < 4; ++c) {
+            for (int cc = 0; cc < 2; ++cc) {
+                const int c = 2 * h + cc;
                 uint32_t r[32];
                 tmem_ld32(tl + b * 128 + c * 32, r);
                 tmem_ld_wait();
                 float sv[32];
-                float mx = neg_inf();
+                uint32_t cand = 0;
+                const float thr = tk.threshold();
 #pragma unroll
                 for (int i = 0; i < 32; ++i) {
                     const int col = c * 32 + i;
                     const bool v = all || (kb * TILE + col < s.NK && kidx_s[b * TILE + col] <= qpos);
                     sv[i] = v ? clamp_score(__uint_as_float(r[i]), s.scale) : neg_inf();
-                    mx = fmaxf(mx, sv[i]);
+                    cand |= (sv[i] > thr ? 1u : 0u) << i;
                 }
-                if (mx > tk.threshold()) {
-#pragma unroll 1
-                    for (int i = 0; i < 32; ++i)
-                        if (sv[i] > tk.threshold()) tk.insert(sv[i], kb * TILE + c * 32 + i);
+                while (cand) {
+                    const int i = __ffs(cand) - 1;
+                    cand &= cand - 1;
+                    const float val = pick32(sv, i);
+                    if (val > tk.threshold()) tk.insert(val, kb * TILE + c * 32 + i);
                 }
             }
             tc_fence_before();
             mbar_arrive(&s_free[b]);
             ++j;
         }
-        if (qv) {
-            tau[(size_t)bh * s.NQ + q] = ref_tau<KM>(tk.v, s.k, s.alpha);
+        if (h == 1) {
 #pragma unroll
-            for (int i = 0; i < KM; ++i)
-                if (tk.i[i] >= 0) flags[tk.i[i] / TILE] = 1;
+            for (int i = 0; i < KM; ++i) {
+                topv_s[row * KM + i] = tk.v[i];
+                topi_s[row * KM + i] = tk.i[i];
+            }
+        }
+        epi_bar();
+        if (h == 0) {
+            for (int i = KM - s.k; i < KM; ++i) tk.insert_lex(topv_s[row * KM + i], topi_s[row * KM + i]);
+            if (qv) {
+                tau[(size_t)bh * s.NQ + q] = ref_tau<KM>(tk.v, s.k, s.alpha);
+#pragma unroll
+                for (int i = 0; i < KM; ++i)
+                    if (tk.i[i] >= 0) flags[tk.i[i] / TILE] = 1;
+            }
         }
         epi_bar();
         uint8_t* Mrow = M + ((size_t)bh * s.nQB + qb) * s.nKB;
-        for (int i = et; i < s.nKB; i += 128) Mrow[i] = flags[i];
+        for (int i = et; i < s.nKB; i += NEPI) Mrow[i] = flags[i];
     }
     tc_fence_before();
     __syncthreads();
@@ -366,10 +420,27 @@ k1_tau_mask(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
     }
 }
 
+// Store this thread's fp32 values o[0..31] (columns [32c, 32c+32) of `row`)
+// to a row-major [rows][D] output of type TO.
+template <int D, typename TO>
+__device__ __forceinline__ void store_out32(TO* dst_row, int c, const float (&o)[32]) {
+    if constexpr (sizeof(TO) == 2) {
+        uint4* dst = reinterpret_cast<uint4*>(dst_row + c * 32);
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+            dst[i] = make_uint4(pack_bf16(o[8 * i], o[8 * i + 1]), pack_bf16(o[8 * i + 2], o[8 * i + 3]),
+                                pack_bf16(o[8 * i + 4], o[8 * i + 5]), pack_bf16(o[8 * i + 6], o[8 * i + 7]));
+    } else {
+        float4* dst = reinterpret_cast<float4*>(dst_row + c * 32);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) dst[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+    }
+}
+
 // ===========================================================================
 // K3: forward over the CSR tile list
 // ===========================================================================
-template <int D, typename TO>
+template <int D, typename TO, int PINV>
 __global__ void __launch_bounds__(NTHREADS, 1)
 k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
            const __grid_constant__ CUtensorMap tmV, Shape s, const int32_t* __restrict__ Qidx,
@@ -395,7 +466,7 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
     uint64_t* p_free = bars + 6 + 2 * S;
     uint64_t* o_full = bars + 7 + 2 * S;
     uint32_t* holder = reinterpret_cast<uint32_t*>(bars + 16);
-    int* kidx_s = reinterpret_cast<int*>(holder + 4);      // [2][128]
+    int* kidx_s = reinterpret_cast<int*>(holder + 4);      // [2][128]; row sums at the end
     int* qidx_blk = kidx_s + 256;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -409,14 +480,14 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
     if (threadIdx.x == 0) {
         mbar_init(q_full, 1);
         for (int i = 0; i < S; ++i) { mbar_init(&kv_full[i], 1); mbar_init(&kv_empty[i], 1); }
-        for (int i = 0; i < 2; ++i) { mbar_init(&s_full[i], 1); mbar_init(&s_free[i], 128); }
-        mbar_init(p_full, 128);
+        for (int i = 0; i < 2; ++i) { mbar_init(&s_full[i], 1); mbar_init(&s_free[i], NEPI); }
+        mbar_init(p_full, NEPI);
         mbar_init(p_free, 1);
         mbar_init(o_full, 1);
         fence_barrier_init();
     }
     if (warp == 1) { tmem_alloc(holder, 512); tmem_relinquish(); }
-    if (threadIdx.x >= EPI0) {
+    if (threadIdx.x >= EPI0 && threadIdx.x < EPI0 + TILE) {
         const int r = threadIdx.x - EPI0;
         const int q = qb * TILE + r;
         qidx_blk[r] = (q < s.NQ && s.causal) ? Qidx[(size_t)bh * s.NQ + q] : INT_MAX;
@@ -499,6 +570,7 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
     } else {
         const int row = (warp & 3) * 32 + lane;
         const int et = threadIdx.x - EPI0;
+        const int h = et / TILE;
         const int q = qb * TILE + row;
         const bool qv = q < s.NQ;
         const size_t qrow = (size_t)bh * s.NQ + (qv ? q : 0);
@@ -506,11 +578,13 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
         const float tq = qv ? tau[qrow] : 0.0f;
         const uint32_t tl = tmem_lane_base(tbase, warp);
         float n = 0.0f;
+        int kb_next = T > 0 ? list[e0] : 0;
         for (int j = 0; j < T; ++j) {
-            const int kb = list[e0 + j];
+            const int kb = kb_next;
+            if (j + 1 < T) kb_next = list[e0 + j + 1];
             const int b = j & 1;
             const bool all = vis_all(s, bd, bh, qb, kb);
-            {
+            if (!all && et < TILE) {
                 const int kn = kb * TILE + et;
                 kidx_s[b * TILE + et] = kn < s.NK ? (s.causal ? Kidx_bh[kn] : INT_MIN) : INT_MAX;
             }
@@ -519,21 +593,28 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
             tc_fence_after();
             mbar_wait(p_free, (j & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
 #pragma unroll 1
-            for (int c = 0; c < 4; ++c) {
+            for (int cc = 0; cc < 2; ++cc) {
+                const int c = 2 * h + cc;
                 uint32_t r[32];
                 tmem_ld32(tl + b * 128 + c * 32, r);
                 tmem_ld_wait();
                 float p[32];
+                if (all) {
 #pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    const int col = c * 32 + i;
-                    const bool v = all || (kb * TILE + col < s.NK && kidx_s[b * TILE + col] <= qpos);
-                    const float sc = clamp_score(__uint_as_float(r[i]), s.scale);
-                    const float u = __fmaf_rn(s.am1, sc, -tq);
-                    float pr = (v && u > 0.0f) ? pow_fast(fmaxf(u, ASA_EPS), s.pinv) : 0.0f;
-                    if (!isfinite(pr)) pr = 0.0f;
-                    p[i] = pr;
-                    n += pr;
+                    for (int i = 0; i < 32; ++i) {
+                        const float u = __fmaf_rn(s.am1, clamp_score(__uint_as_float(r[i]), s.scale), -tq);
+                        p[i] = entmax_pk<PINV>(u, s.pinv.e);
+                        n += p[i];
+                    }
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) {
+                        const int col = c * 32 + i;
+                        const bool v = kb * TILE + col < s.NK && kidx_s[b * TILE + col] <= qpos;
+                        const float u = __fmaf_rn(s.am1, clamp_score(__uint_as_float(r[i]), s.scale), -tq);
+                        p[i] = v ? entmax_pk<PINV>(u, s.pinv.e) : 0.0f;
+                        n += p[i];
+                    }
                 }
                 uint32_t hi[16], lo[16];
                 split_pack(p, hi, lo);
@@ -545,11 +626,26 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
             fence_async_smem();
             mbar_arrive(p_full);
         }
+        // row sum = warpgroup 0's half + warpgroup 1's half
+        float* nsum = reinterpret_cast<float*>(kidx_s);
+        epi_bar();
+        if (h == 1) nsum[row] = n;
+        epi_bar();
+        if (h == 0) {
+            n = n + nsum[row];
+            if (qv) rownorm[qrow] = n;
+        }
+        epi_bar();
+        if (h == 0) nsum[row] = n;
+        epi_bar();
+        n = nsum[row];
         mbar_wait(o_full, 0, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
         tc_fence_after();
         const float inv = __fdiv_rn(1.0f, __fadd_rn(n, ASA_EPS));
+        constexpr int CPW = D / 64;     // 32-column chunks per warpgroup
 #pragma unroll 1
-        for (int c = 0; c < D / 32; ++c) {
+        for (int cc = 0; cc < CPW; ++cc) {
+            const int c = h * CPW + cc;
             uint32_t r[32];
             tmem_ld32(tl + tO + c * 32, r);
             tmem_ld_wait();
@@ -558,29 +654,11 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
 #pragma unroll
             for (int i = 0; i < 32; ++i) {
                 float v = T > 0 ? __uint_as_float(r[i]) * inv : 0.0f;
-                if (!isfinite(v)) v = 0.0f;
-                o[i] = v;
+                o[i] = isfinite(v) ? v : 0.0f;
             }
-            if (O32) {
-                float4* dst = reinterpret_cast<float4*>(O32 + qrow * D + c * 32);
-#pragma unroll
-                for (int i = 0; i < 8; ++i) dst[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
-            }
-            if constexpr (sizeof(TO) == 2) {
-                uint4* dst = reinterpret_cast<uint4*>(O + qrow * D + c * 32);
-#pragma unroll
-                for (int i = 0; i < 4; ++i)
-                    dst[i] = make_uint4(pack_bf16(o[8 * i], o[8 * i + 1]), pack_bf16(o[8 * i + 2], o[8 * i + 3]),
-                                        pack_bf16(o[8 * i + 4], o[8 * i + 5]), pack_bf16(o[8 * i + 6], o[8 * i + 7]));
-            } else {
-                if ((void*)O != (void*)O32) {
-                    float4* dst = reinterpret_cast<float4*>(O + qrow * D + c * 32);
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) dst[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
-                }
-            }
+            if (O32) store_out32<D, float>(O32 + qrow * D, c, o);
+            if (sizeof(TO) == 2 || (void*)O != (void*)O32) store_out32<D, TO>(O + qrow * D, c, o);
         }
-        if (qv) rownorm[qrow] = n;
     }
     tc_fence_before();
     __syncthreads();
@@ -591,39 +669,11 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
 }
 
 // ===========================================================================
-// K4 pre: D_q = Σ_t O_t · dO_t  (fp32 O, bf16 dO), one warp per row.
-// ===========================================================================
-template <int D>
-__global__ void k4_pre(const float* __restrict__ O32, const __nv_bfloat16* __restrict__ dO,
-                       float* __restrict__ Dq, size_t rows) {
-    const size_t r = (size_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-    const int lane = threadIdx.x & 31;
-    if (r >= rows) return;
-    float acc = 0.0f;
-#pragma unroll
-    for (int t = lane; t < D; t += 32) acc = fmaf(O32[r * D + t], __bfloat162float(dO[r * D + t]), acc);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-    if (lane == 0) Dq[r] = acc;
-}
-
-// Gradient of one score (reference :481-507) from s (clamped), dP = dO·v,
-// the row's τ, 1/n and D = O·dO:  g = u^{(2-α)/(α-1)} · (dP - D)/n for
-// u > EPS, else 0.
-__device__ __forceinline__ float score_grad(const Shape& s, float sc, float dP, float tq, float invN,
-                                            float Dq, bool vis) {
-    const float u = __fmaf_rn(s.am1, sc, -tq);
-    if (!vis || !(u > ASA_EPS)) return 0.0f;
-    const float pw = pow_fast(fmaxf(u, ASA_EPS), s.pe2);
-    float g = pw * (dP - Dq) * invN;
-    return isfinite(g) ? g : 0.0f;
-}
-
-// ===========================================================================
 // K4 dQ: query-major over the CSR list.  S = Q·K^T, dP = dO·V^T; dS in the
-// epilogue; dQ += dS·K (K tile as the MN-major B operand).
+// epilogue (warpgroup h owns key columns [64h, 64h+64)); dQ += dS·K (K tile
+// as the MN-major B operand).
 // ===========================================================================
-template <int D, typename TO>
+template <int D, typename TO, int PE2>
 __global__ void __launch_bounds__(NTHREADS, 1)
 k4_dq(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
       const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO, Shape s,
@@ -664,12 +714,12 @@ k4_dq(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < 8; ++i) mbar_init(&bars[i], 1);
-        mbar_init(sd_free, 128);
-        mbar_init(ds_full, 128);
+        mbar_init(sd_free, NEPI);
+        mbar_init(ds_full, NEPI);
         fence_barrier_init();
     }
     if (warp == 1) { tmem_alloc(holder, 512); tmem_relinquish(); }
-    if (threadIdx.x >= EPI0) {
+    if (threadIdx.x >= EPI0 && threadIdx.x < EPI0 + TILE) {
         const int r = threadIdx.x - EPI0;
         const int q = qb * TILE + r;
         qidx_blk[r] = (q < s.NQ && s.causal) ? Qidx[(size_t)bh * s.NQ + q] : INT_MAX;
@@ -743,6 +793,7 @@ k4_dq(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
     } else {
         const int row = (warp & 3) * 32 + lane;
         const int et = threadIdx.x - EPI0;
+        const int h = et / TILE;
         const int q = qb * TILE + row;
         const bool qv = q < s.NQ;
         const size_t qrow = (size_t)bh * s.NQ + (qv ? q : 0);
@@ -751,11 +802,13 @@ k4_dq(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
         const float invN = qv ? __fdiv_rn(1.0f, __fadd_rn(rownorm[qrow], ASA_EPS)) : 0.0f;
         const float Dq = qv ? Dqv[qrow] : 0.0f;
         const uint32_t tl = tmem_lane_base(tbase, warp);
+        int kb_next = T > 0 ? list[e0] : 0;
         for (int j = 0; j < T; ++j) {
-            const int kb = list[e0 + j];
+            const int kb = kb_next;
+            if (j + 1 < T) kb_next = list[e0 + j + 1];
             const int b = j & 1;
-            const bool all = vis_all(s, bd, bh, qb, kb);
-            {
+            const bool all = qv && vis_all(s, bd, bh, qb, kb);
+            if (!all && et < TILE) {
                 const int kn = kb * TILE + et;
                 kidx_s[b * TILE + et] = kn < s.NK ? (s.causal ? Kidx_bh[kn] : INT_MIN) : INT_MAX;
             }
@@ -764,7 +817,8 @@ k4_dq(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
             tc_fence_after();
             mbar_wait(ds_free, (j & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
 #pragma unroll 1
-            for (int c = 0; c < 4; ++c) {
+            for (int cc = 0; cc < 2; ++cc) {
+                const int c = 2 * h + cc;
                 uint32_t rs[32], rp[32];
                 tmem_ld32(tl + tS + c * 32, rs);
                 tmem_ld32(tl + tP + c * 32, rp);
@@ -773,9 +827,9 @@ k4_dq(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
 #pragma unroll
                 for (int i = 0; i < 32; ++i) {
                     const int col = c * 32 + i;
-                    const bool v = qv && (all || (kb * TILE + col < s.NK && kidx_s[b * TILE + col] <= qpos));
-                    g[i] = score_grad(s, clamp_score(__uint_as_float(rs[i]), s.scale),
-                                      __uint_as_float(rp[i]), tq, invN, Dq, v);
+                    const bool v = all || (qv && kb * TILE + col < s.NK && kidx_s[b * TILE + col] <= qpos);
+                    const float u = __fmaf_rn(s.am1, clamp_score(__uint_as_float(rs[i]), s.scale), -tq);
+                    g[i] = v ? grad_pk<PE2>(u, s.pe2.e, __uint_as_float(rp[i]), Dq, invN) : 0.0f;
                 }
                 uint32_t hi[16], lo[16];
                 split_pack(g, hi, lo);
@@ -789,8 +843,10 @@ k4_dq(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
         }
         mbar_wait(dq_full, 0, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
         tc_fence_after();
+        constexpr int CPW = D / 64;
 #pragma unroll 1
-        for (int c = 0; c < D / 32; ++c) {
+        for (int cc = 0; cc < CPW; ++cc) {
+            const int c = h * CPW + cc;
             uint32_t r[32];
             tmem_ld32(tl + tQ + c * 32, r);
             tmem_ld_wait();
@@ -801,17 +857,7 @@ k4_dq(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
                 float v = T > 0 ? __uint_as_float(r[i]) * s.scale : 0.0f;
                 o[i] = isfinite(v) ? v : 0.0f;
             }
-            if constexpr (sizeof(TO) == 2) {
-                uint4* dst = reinterpret_cast<uint4*>(dQ + qrow * D + c * 32);
-#pragma unroll
-                for (int i = 0; i < 4; ++i)
-                    dst[i] = make_uint4(pack_bf16(o[8 * i], o[8 * i + 1]), pack_bf16(o[8 * i + 2], o[8 * i + 3]),
-                                        pack_bf16(o[8 * i + 4], o[8 * i + 5]), pack_bf16(o[8 * i + 6], o[8 * i + 7]));
-            } else {
-                float4* dst = reinterpret_cast<float4*>(dQ + qrow * D + c * 32);
-#pragma unroll
-                for (int i = 0; i < 8; ++i) dst[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
-            }
+            store_out32<D, TO>(dQ + qrow * D, c, o);
         }
     }
     tc_fence_before();
@@ -824,10 +870,11 @@ k4_dq(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
 
 // ===========================================================================
 // K4 dK/dV: key-major over the transposed list.  S^T = K·Q^T, dP^T = V·dO^T;
-// the epilogue (thread = key row, columns = queries) writes P^T/n, then dS^T,
-// into one shared buffer; dV += (P^T/n)·dO, dK += dS^T·Q.
+// the epilogue (thread = key row; warpgroup h owns query columns
+// [64h, 64h+64)) writes P^T/n, then dS^T, into one shared buffer;
+// dV += (P^T/n)·dO, dK += dS^T·Q.
 // ===========================================================================
-template <int D, typename TO>
+template <int D, typename TO, int PINV, int PE2>
 __global__ void __launch_bounds__(NTHREADS, 1)
 k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
         const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO, Shape s,
@@ -874,9 +921,9 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < 10; ++i) mbar_init(&bars[i], 1);
-        mbar_init(sd_free, 128);
-        mbar_init(p_full, 128);
-        mbar_init(ds_full, 128);
+        mbar_init(sd_free, NEPI);
+        mbar_init(p_full, NEPI);
+        mbar_init(ds_full, NEPI);
         fence_barrier_init();
     }
     if (warp == 1) { tmem_alloc(holder, 512); tmem_relinquish(); }
@@ -979,6 +1026,7 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
     } else {
         const int row = (warp & 3) * 32 + lane;
         const int et = threadIdx.x - EPI0;
+        const int h = et / TILE;
         const int kn = kb * TILE + row;
         const bool kv = kn < s.NK;
         const size_t krow = (size_t)bh * s.NK + (kv ? kn : 0);
@@ -987,7 +1035,7 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
         for (int i = 0; i < T; ++i) {
             const int qb = list[e0 + i];
             epi_bar();   // previous pair's readers of the per-query arrays are done
-            {
+            if (et < TILE) {
                 const int q = qb * TILE + et;
                 const bool ok = q < s.NQ;
                 const size_t r = (size_t)bh * s.NQ + (ok ? q : 0);
@@ -997,13 +1045,14 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
                 qp_s[et] = ok ? (s.causal ? Qidx_bh[q] : INT_MAX) : INT_MIN;
             }
             epi_bar();
-            const bool all = vis_all(s, bd, bh, qb, kb) && (qb + 1) * TILE <= s.NQ;
+            const bool all = kv && vis_all(s, bd, bh, qb, kb) && (qb + 1) * TILE <= s.NQ;
             mbar_wait(sd_full, i & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
             tc_fence_after();
             mbar_wait(ds_free, (i & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
             // pass 1: P^T / n
 #pragma unroll 1
-            for (int c = 0; c < 4; ++c) {
+            for (int cc = 0; cc < 2; ++cc) {
+                const int c = 2 * h + cc;
                 uint32_t rs[32];
                 tmem_ld32(tl + tS + c * 32, rs);
                 tmem_ld_wait();
@@ -1011,12 +1060,9 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
 #pragma unroll
                 for (int k = 0; k < 32; ++k) {
                     const int col = c * 32 + k;
-                    const bool v = kv && (all || kpos <= qp_s[col]);
-                    const float sc = clamp_score(__uint_as_float(rs[k]), s.scale);
-                    const float u = __fmaf_rn(s.am1, sc, -tau_s[col]);
-                    float pr = (v && u > 0.0f) ? pow_fast(fmaxf(u, ASA_EPS), s.pinv) : 0.0f;
-                    pr *= inv_s[col];
-                    p[k] = isfinite(pr) ? pr : 0.0f;
+                    const bool v = all || (kv && kpos <= qp_s[col]);
+                    const float u = __fmaf_rn(s.am1, clamp_score(__uint_as_float(rs[k]), s.scale), -tau_s[col]);
+                    p[k] = v ? entmax_pk<PINV>(u, s.pinv.e) * inv_s[col] : 0.0f;
                 }
                 uint32_t hi[16], lo[16];
                 split_pack(p, hi, lo);
@@ -1028,7 +1074,8 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
             mbar_wait(p_free, i & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
             // pass 2: dS^T
 #pragma unroll 1
-            for (int c = 0; c < 4; ++c) {
+            for (int cc = 0; cc < 2; ++cc) {
+                const int c = 2 * h + cc;
                 uint32_t rs[32], rp[32];
                 tmem_ld32(tl + tS + c * 32, rs);
                 tmem_ld32(tl + tP + c * 32, rp);
@@ -1037,9 +1084,9 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
 #pragma unroll
                 for (int k = 0; k < 32; ++k) {
                     const int col = c * 32 + k;
-                    const bool v = kv && (all || kpos <= qp_s[col]);
-                    g[k] = score_grad(s, clamp_score(__uint_as_float(rs[k]), s.scale),
-                                      __uint_as_float(rp[k]), tau_s[col], inv_s[col], dq_s[col], v);
+                    const bool v = all || (kv && kpos <= qp_s[col]);
+                    const float u = __fmaf_rn(s.am1, clamp_score(__uint_as_float(rs[k]), s.scale), -tau_s[col]);
+                    g[k] = v ? grad_pk<PE2>(u, s.pe2.e, __uint_as_float(rp[k]), dq_s[col], inv_s[col]) : 0.0f;
                 }
                 uint32_t hi[16], lo[16];
                 split_pack(g, hi, lo);
@@ -1055,13 +1102,15 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
             mbar_wait(out_full, 0, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
             tc_fence_after();
         }
+        constexpr int CPW = D / 64;
 #pragma unroll 1
         for (int part = 0; part < 2; ++part) {
             TO* dst_base = part == 0 ? dV : dK;
             const float mul = part == 0 ? 1.0f : s.scale;
             const uint32_t col0 = part == 0 ? tV : tK;
 #pragma unroll 1
-            for (int c = 0; c < D / 32; ++c) {
+            for (int cc = 0; cc < CPW; ++cc) {
+                const int c = h * CPW + cc;
                 uint32_t r[32];
                 if (T > 0) {
                     tmem_ld32(tl + col0 + c * 32, r);
@@ -1074,17 +1123,7 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
                     float v = T > 0 ? __uint_as_float(r[k]) * mul : 0.0f;
                     o[k] = isfinite(v) ? v : 0.0f;
                 }
-                if constexpr (sizeof(TO) == 2) {
-                    uint4* dst = reinterpret_cast<uint4*>(dst_base + krow * D + c * 32);
-#pragma unroll
-                    for (int k = 0; k < 4; ++k)
-                        dst[k] = make_uint4(pack_bf16(o[8 * k], o[8 * k + 1]), pack_bf16(o[8 * k + 2], o[8 * k + 3]),
-                                            pack_bf16(o[8 * k + 4], o[8 * k + 5]), pack_bf16(o[8 * k + 6], o[8 * k + 7]));
-                } else {
-                    float4* dst = reinterpret_cast<float4*>(dst_base + krow * D + c * 32);
-#pragma unroll
-                    for (int k = 0; k < 8; ++k) dst[k] = make_float4(o[4 * k], o[4 * k + 1], o[4 * k + 2], o[4 * k + 3]);
-                }
+                store_out32<D, TO>(dst_base + krow * D, c, o);
             }
         }
     }
@@ -1095,6 +1134,25 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
         tmem_dealloc(tbase, 512);
     }
 }
+
+// ===========================================================================
+// K4 pre: D_q = Σ_t O_t · dO_t  (fp32 O, bf16 dO), one warp per row.
+// ===========================================================================
+template <int D>
+__global__ void k4_pre(const float* __restrict__ O32, const __nv_bfloat16* __restrict__ dO,
+                       float* __restrict__ Dq, size_t rows) {
+    const size_t r = (size_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (r >= rows) return;
+    float acc = 0.0f;
+#pragma unroll
+    for (int t = lane; t < D; t += 32) acc = fmaf(O32[r * D + t], __bfloat162float(dO[r * D + t]), acc);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (lane == 0) Dq[r] = acc;
+}
+
+
 
 // ===========================================================================
 // host side
@@ -1180,6 +1238,30 @@ size_t tc_bwd_workspace(const Shape& s) {
     return ((bounds_ints(s) * 4 + 15) & ~size_t(15)) + (size_t)s.BH * s.NQ * 4;
 }
 
+// Exponent classes the kernels are specialised for: (1/(α-1), (2-α)/(α-1))
+// kinds (2,1) for α=1.5, (1,5) for α=2, (4,3) for α=1.25; anything else runs
+// the generic powf instantiation.
+template <int PI, int PE> struct AlphaClass {
+    static constexpr int pinv = PI, pe2 = PE;
+};
+template <typename F>
+cudaError_t with_alpha(const Shape& s, F&& f) {
+    if (s.pinv.kind == 2 && s.pe2.kind == 1) return f(AlphaClass<2, 1>{});
+    if (s.pinv.kind == 1 && s.pe2.kind == 5) return f(AlphaClass<1, 5>{});
+    if (s.pinv.kind == 4 && s.pe2.kind == 3) return f(AlphaClass<4, 3>{});
+    return f(AlphaClass<0, 0>{});
+}
+template <typename F>
+cudaError_t with_dtype_d(const Shape& s, F&& f) {
+    using bf = __nv_bfloat16;
+    if (s.out_dtype == ASA_DTYPE_F32) {
+        if (s.d == 128) return f(std::integral_constant<int, 128>{}, (float*)nullptr);
+        return f(std::integral_constant<int, 64>{}, (float*)nullptr);
+    }
+    if (s.d == 128) return f(std::integral_constant<int, 128>{}, (bf*)nullptr);
+    return f(std::integral_constant<int, 64>{}, (bf*)nullptr);
+}
+
 cudaError_t tc_tau_mask(const Shape& s, const void* Q, const void* K, const int32_t* Qidx,
                         const int32_t* Kidx, float* tau, uint8_t* M, void* ws, int* err,
                         cudaStream_t st) {
@@ -1189,8 +1271,8 @@ cudaError_t tc_tau_mask(const Shape& s, const void* Q, const void* K, const int3
     if (!make_map(&mQ, Q, s.BH, s.NQ, s.d) || !make_map(&mK, K, s.BH, s.NK, s.d)) return cudaErrorInvalidValue;
     Bounds bd = bounds_at(s, ws);
     dim3 grid(s.nQB, s.BH);
-    auto go = [&](auto kern, int D) -> cudaError_t {
-        const size_t smem = (size_t)D * TILE * 2 * 5 + kSmemTail + s.nKB;
+    auto go = [&](auto kern, int D, int KM) -> cudaError_t {
+        const size_t smem = (size_t)D * TILE * 2 * 5 + (size_t)TILE * KM * 8 + kSmemTail + s.nKB;
         cudaError_t r = prep(kern, smem);
         if (r != cudaSuccess) return r;
         kern<<<grid, NTHREADS, smem, st>>>(mQ, mK, s, Qidx, Kidx, bd, tau, M, err);
@@ -1198,13 +1280,13 @@ cudaError_t tc_tau_mask(const Shape& s, const void* Q, const void* K, const int3
         return cudaGetLastError();
     };
     if (s.d == 128) {
-        if (s.k <= 8) return go(k1_tau_mask<128, 8>, 128);
-        if (s.k <= 16) return go(k1_tau_mask<128, 16>, 128);
-        return go(k1_tau_mask<128, 32>, 128);
+        if (s.k <= 8) return go(k1_tau_mask<128, 8>, 128, 8);
+        if (s.k <= 16) return go(k1_tau_mask<128, 16>, 128, 16);
+        return go(k1_tau_mask<128, 32>, 128, 32);
     }
-    if (s.k <= 8) return go(k1_tau_mask<64, 8>, 64);
-    if (s.k <= 16) return go(k1_tau_mask<64, 16>, 64);
-    return go(k1_tau_mask<64, 32>, 64);
+    if (s.k <= 8) return go(k1_tau_mask<64, 8>, 64, 8);
+    if (s.k <= 16) return go(k1_tau_mask<64, 16>, 64, 16);
+    return go(k1_tau_mask<64, 32>, 64, 32);
 }
 
 cudaError_t tc_forward(const Shape& s, const void* Q, const void* K, const void* V, const int32_t* Qidx,
@@ -1217,41 +1299,20 @@ cudaError_t tc_forward(const Shape& s, const void* Q, const void* K, const void*
     Bounds bd = bounds_at(s, ws);   // filled by tc_tau_mask
     dim3 grid(s.nQB, s.BH);
     const int split = s.split;
-    if (s.out_dtype == ASA_DTYPE_F32) {
-        if (s.d == 128) {
-            auto k = k3_forward<128, float>;
-            const size_t smem = (size_t)128 * TILE * 2 * 5 + (size_t)2 * TILE * TILE * 2 + kSmemTail;
+    return with_dtype_d(s, [&](auto dtag, auto* out) -> cudaError_t {
+        constexpr int D = decltype(dtag)::value;
+        using TO = std::remove_pointer_t<decltype(out)>;
+        return with_alpha(s, [&](auto ac) -> cudaError_t {
+            auto k = k3_forward<D, TO, decltype(ac)::pinv>;
+            const size_t smem = (size_t)D * TILE * 2 * 5 + (size_t)2 * TILE * TILE * 2 + kSmemTail;
             cudaError_t r = prep(k, smem);
             if (r != cudaSuccess) return r;
-            k<<<grid, NTHREADS, smem, st>>>(mQ, mK, mV, s, Qidx, Kidx, bd, tau, ptr, idx, (float*)O, O32,
+            k<<<grid, NTHREADS, smem, st>>>(mQ, mK, mV, s, Qidx, Kidx, bd, tau, ptr, idx, (TO*)O, O32,
                                             rownorm, split, err);
-        } else {
-            auto k = k3_forward<64, float>;
-            const size_t smem = (size_t)64 * TILE * 2 * 5 + (size_t)2 * TILE * TILE * 2 + kSmemTail;
-            cudaError_t r = prep(k, smem);
-            if (r != cudaSuccess) return r;
-            k<<<grid, NTHREADS, smem, st>>>(mQ, mK, mV, s, Qidx, Kidx, bd, tau, ptr, idx, (float*)O, O32,
-                                            rownorm, split, err);
-        }
-    } else {
-        if (s.d == 128) {
-            auto k = k3_forward<128, __nv_bfloat16>;
-            const size_t smem = (size_t)128 * TILE * 2 * 5 + (size_t)2 * TILE * TILE * 2 + kSmemTail;
-            cudaError_t r = prep(k, smem);
-            if (r != cudaSuccess) return r;
-            k<<<grid, NTHREADS, smem, st>>>(mQ, mK, mV, s, Qidx, Kidx, bd, tau, ptr, idx,
-                                            (__nv_bfloat16*)O, O32, rownorm, split, err);
-        } else {
-            auto k = k3_forward<64, __nv_bfloat16>;
-            const size_t smem = (size_t)64 * TILE * 2 * 5 + (size_t)2 * TILE * TILE * 2 + kSmemTail;
-            cudaError_t r = prep(k, smem);
-            if (r != cudaSuccess) return r;
-            k<<<grid, NTHREADS, smem, st>>>(mQ, mK, mV, s, Qidx, Kidx, bd, tau, ptr, idx,
-                                            (__nv_bfloat16*)O, O32, rownorm, split, err);
-        }
-    }
-    note_launch();
-    return cudaGetLastError();
+            note_launch();
+            return cudaGetLastError();
+        });
+    });
 }
 
 cudaError_t tc_backward(const Shape& s, const void* Q, const void* K, const void* V, const int32_t* Qidx,
@@ -1276,30 +1337,28 @@ cudaError_t tc_backward(const Shape& s, const void* Q, const void* K, const void
         !make_map(&mV, V, s.BH, s.NK, s.d) || !make_map(&mdO, dO, s.BH, s.NQ, s.d))
         return cudaErrorInvalidValue;
     const int split = s.split;
-    auto run = [&](auto kdq, auto kkv, auto* dq_out, auto* dk_out, auto* dv_out, int D) -> cudaError_t {
-        const size_t smem = (size_t)D * TILE * 2 * 4 + (size_t)2 * TILE * TILE * 2 + kSmemTail;
-        cudaError_t r = prep(kdq, smem);
-        if (r == cudaSuccess) r = prep(kkv, smem);
-        if (r != cudaSuccess) return r;
-        kdq<<<dim3(s.nQB, s.BH), NTHREADS, smem, st>>>(mQ, mK, mV, mdO, s, Qidx, Kidx, bd, tau, rownorm,
-                                                      Dq, ptr, idx, dq_out, split, err);
-        note_launch();
-        r = cudaGetLastError();
-        if (r != cudaSuccess) return r;
-        kkv<<<dim3(s.nKB, s.BH), NTHREADS, smem, st>>>(mQ, mK, mV, mdO, s, Qidx, Kidx, bd, tau, rownorm,
-                                                      Dq, cptr, cidx, dk_out, dv_out, split, err);
-        note_launch();
-        return cudaGetLastError();
-    };
-    if (s.out_dtype == ASA_DTYPE_F32) {
-        if (s.d == 128)
-            return run(k4_dq<128, float>, k4_dkdv<128, float>, (float*)dQ, (float*)dK, (float*)dV, 128);
-        return run(k4_dq<64, float>, k4_dkdv<64, float>, (float*)dQ, (float*)dK, (float*)dV, 64);
-    }
-    using bf = __nv_bfloat16;
-    if (s.d == 128)
-        return run(k4_dq<128, bf>, k4_dkdv<128, bf>, (bf*)dQ, (bf*)dK, (bf*)dV, 128);
-    return run(k4_dq<64, bf>, k4_dkdv<64, bf>, (bf*)dQ, (bf*)dK, (bf*)dV, 64);
+    return with_dtype_d(s, [&](auto dtag, auto* out) -> cudaError_t {
+        constexpr int D = decltype(dtag)::value;
+        using TO = std::remove_pointer_t<decltype(out)>;
+        return with_alpha(s, [&](auto ac) -> cudaError_t {
+            auto kdq = k4_dq<D, TO, decltype(ac)::pe2>;
+            auto kkv = k4_dkdv<D, TO, decltype(ac)::pinv, decltype(ac)::pe2>;
+            const size_t smem = (size_t)D * TILE * 2 * 4 + (size_t)2 * TILE * TILE * 2 + kSmemTail;
+            cudaError_t r = prep(kdq, smem);
+            if (r == cudaSuccess) r = prep(kkv, smem);
+            if (r != cudaSuccess) return r;
+            kdq<<<dim3(s.nQB, s.BH), NTHREADS, smem, st>>>(mQ, mK, mV, mdO, s, Qidx, Kidx, bd, tau,
+                                                          rownorm, Dq, ptr, idx, (TO*)dQ, split, err);
+            note_launch();
+            r = cudaGetLastError();
+            if (r != cudaSuccess) return r;
+            kkv<<<dim3(s.nKB, s.BH), NTHREADS, smem, st>>>(mQ, mK, mV, mdO, s, Qidx, Kidx, bd, tau,
+                                                          rownorm, Dq, cptr, cidx, (TO*)dK, (TO*)dV,
+                                                          split, err);
+            note_launch();
+            return cudaGetLastError();
+        });
+    });
 }
 
 }  // namespace asa
