@@ -32,7 +32,7 @@ cudaError_t tc_backward(const Shape& s, const void* Q, const void* K, const void
                         const float* tau, const int32_t* ptr, const int32_t* idx,
                         const int32_t* cptr, const int32_t* cidx, const float* rownorm,
                         const void* dO, void* dQ, void* dK, void* dV, void* ws, int* err,
-                        cudaStream_t st);
+                        cudaStream_t st, int stages);
 }  // namespace asa
 
 __device__ int g_asa_error;
@@ -313,10 +313,13 @@ int asa_backward(const asa_params* p, const void* Q, const void* K, const void* 
     }
     if (e != cudaSuccess) return cuda_status(e);
     if (b == ASA_BACKEND_TC) {
-        ProfScope ps("backward", st);
         if (!O32 || !rownorm) return ASA_ERR_INVALID;
-        e = asa::tc_backward(s, Q, K, V, Qidx, Kidx, O32, tau, csr_ptr, csr_idx, cptr, cidx,
-                             rownorm, dO, dQ, dK, dV, w + L.extra, error_word(), st);
+        static const char* labels[3] = {"bwd_pre", "bwd_dq", "bwd_dkdv"};
+        for (int k = 0; k < 3 && e == cudaSuccess; ++k) {
+            ProfScope ps(labels[k], st);
+            e = asa::tc_backward(s, Q, K, V, Qidx, Kidx, O32, tau, csr_ptr, csr_idx, cptr, cidx,
+                                 rownorm, dO, dQ, dK, dV, w + L.extra, error_word(), st, 1 << k);
+        }
         return cuda_status(e);
     }
     {

@@ -201,6 +201,28 @@ __device__ __forceinline__ float grad_pk(float u, float e, float dP, float Dq, f
     return isfinite(g) ? g : 0.0f;
 }
 
+// Positions of keys kn0 .. kn0+31 (INT_MAX past NK, INT_MIN when every key
+// is visible).  L1-cached loads; only partially visible tiles need them.
+__device__ __forceinline__ void load_kpos32(const int32_t* __restrict__ Kidx_bh, int kn0, int NK,
+                                            int causal, int (&kp)[32]) {
+    if (!causal) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) kp[i] = kn0 + i < NK ? INT_MIN : INT_MAX;
+        return;
+    }
+    if (kn0 + 32 <= NK && ((reinterpret_cast<uintptr_t>(Kidx_bh + kn0) & 15) == 0)) {
+        const int4* p = reinterpret_cast<const int4*>(Kidx_bh + kn0);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int4 v = __ldg(p + i);
+            kp[4 * i] = v.x; kp[4 * i + 1] = v.y; kp[4 * i + 2] = v.z; kp[4 * i + 3] = v.w;
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) kp[i] = kn0 + i < NK ? __ldg(Kidx_bh + kn0 + i) : INT_MAX;
+    }
+}
+
 __device__ __forceinline__ uint32_t tmem_lane_base(uint32_t tbase, int warp) {
     return tbase + ((uint32_t)((warp & 3) * 32) << 16);
 }
@@ -352,31 +374,37 @@ k1_tau_mask(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
         const uint32_t tl = tmem_lane_base(tbase, warp);
         TopK<KM> tk;
         tk.init(s.k);
+        const bool scale_pos = s.scale > 0.0f;
         int j = 0;
         for (int kb = 0; kb < s.nKB; ++kb) {
             if (!vis_any(s, bd, bh, qb, kb)) continue;
             const int b = j & 1;
             const bool all = vis_all(s, bd, bh, qb, kb);
-            if (et < TILE) {
-                const int kn = kb * TILE + et;
-                kidx_s[b * TILE + et] = kn < s.NK ? (s.causal ? Kidx_bh[kn] : INT_MIN) : INT_MAX;
-            }
-            epi_bar();
             mbar_wait(&s_full[b], (j >> 1) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
             tc_fence_after();
 #pragma unroll 1
             for (int cc = 0; cc < 2; ++cc) {
                 const int c = 2 * h + cc;
+                const int kn0 = kb * TILE + c * 32;
                 uint32_t r[32];
                 tmem_ld32(tl + b * 128 + c * 32, r);
                 tmem_ld_wait();
+                if (all && scale_pos) {
+                    // clamp(x·scale) is monotone in x: if the chunk's largest raw
+                    // score cannot enter the list, none of its scores can
+                    float m = __uint_as_float(r[0]);
+#pragma unroll
+                    for (int i = 1; i < 32; ++i) m = fmaxf(m, __uint_as_float(r[i]));
+                    if (!(clamp_score(m, s.scale) > tk.threshold())) continue;
+                }
+                int kp[32];
+                if (!all) load_kpos32(Kidx_bh, kn0, s.NK, s.causal, kp);
                 float sv[32];
                 uint32_t cand = 0;
                 const float thr = tk.threshold();
 #pragma unroll
                 for (int i = 0; i < 32; ++i) {
-                    const int col = c * 32 + i;
-                    const bool v = all || (kb * TILE + col < s.NK && kidx_s[b * TILE + col] <= qpos);
+                    const bool v = all || kp[i] <= qpos;
                     sv[i] = v ? clamp_score(__uint_as_float(r[i]), s.scale) : neg_inf();
                     cand |= (sv[i] > thr ? 1u : 0u) << i;
                 }
@@ -384,7 +412,7 @@ k1_tau_mask(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
                     const int i = __ffs(cand) - 1;
                     cand &= cand - 1;
                     const float val = pick32(sv, i);
-                    if (val > tk.threshold()) tk.insert(val, kb * TILE + c * 32 + i);
+                    if (val > tk.threshold()) tk.insert(val, kn0 + i);
                 }
             }
             tc_fence_before();
@@ -584,11 +612,6 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
             if (j + 1 < T) kb_next = list[e0 + j + 1];
             const int b = j & 1;
             const bool all = vis_all(s, bd, bh, qb, kb);
-            if (!all && et < TILE) {
-                const int kn = kb * TILE + et;
-                kidx_s[b * TILE + et] = kn < s.NK ? (s.causal ? Kidx_bh[kn] : INT_MIN) : INT_MAX;
-            }
-            epi_bar();
             mbar_wait(&s_full[b], (j >> 1) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
             tc_fence_after();
             mbar_wait(p_free, (j & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
@@ -607,10 +630,11 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
                         n += p[i];
                     }
                 } else {
+                    int kp[32];
+                    load_kpos32(Kidx_bh, kb * TILE + c * 32, s.NK, s.causal, kp);
 #pragma unroll
                     for (int i = 0; i < 32; ++i) {
-                        const int col = c * 32 + i;
-                        const bool v = kb * TILE + col < s.NK && kidx_s[b * TILE + col] <= qpos;
+                        const bool v = kp[i] <= qpos;
                         const float u = __fmaf_rn(s.am1, clamp_score(__uint_as_float(r[i]), s.scale), -tq);
                         p[i] = v ? entmax_pk<PINV>(u, s.pinv.e) : 0.0f;
                         n += p[i];
@@ -678,7 +702,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 k4_dq(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
       const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO, Shape s,
       const int32_t* __restrict__ Qidx, const int32_t* __restrict__ Kidx, Bounds bd,
-      const float* __restrict__ tau, const float* __restrict__ rownorm, const float* __restrict__ Dqv,
+      const float* __restrict__ tau, const float* __restrict__ invNv, const float* __restrict__ Dqv,
       const int32_t* __restrict__ ptr, const int32_t* __restrict__ idx, TO* __restrict__ dQ, int split,
       int* err) {
     constexpr int TB = D * TILE * 2;
@@ -799,7 +823,7 @@ k4_dq(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
         const size_t qrow = (size_t)bh * s.NQ + (qv ? q : 0);
         const int qpos = !qv ? INT_MIN : (s.causal ? Qidx[qrow] : INT_MAX);
         const float tq = qv ? tau[qrow] : 0.0f;
-        const float invN = qv ? __fdiv_rn(1.0f, __fadd_rn(rownorm[qrow], ASA_EPS)) : 0.0f;
+        const float invN = qv ? invNv[qrow] : 0.0f;
         const float Dq = qv ? Dqv[qrow] : 0.0f;
         const uint32_t tl = tmem_lane_base(tbase, warp);
         int kb_next = T > 0 ? list[e0] : 0;
@@ -808,11 +832,6 @@ k4_dq(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
             if (j + 1 < T) kb_next = list[e0 + j + 1];
             const int b = j & 1;
             const bool all = qv && vis_all(s, bd, bh, qb, kb);
-            if (!all && et < TILE) {
-                const int kn = kb * TILE + et;
-                kidx_s[b * TILE + et] = kn < s.NK ? (s.causal ? Kidx_bh[kn] : INT_MIN) : INT_MAX;
-            }
-            epi_bar();
             mbar_wait(sd_full, j & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
             tc_fence_after();
             mbar_wait(ds_free, (j & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
@@ -823,11 +842,12 @@ k4_dq(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
                 tmem_ld32(tl + tS + c * 32, rs);
                 tmem_ld32(tl + tP + c * 32, rp);
                 tmem_ld_wait();
+                int kp[32];
+                if (!all) load_kpos32(Kidx_bh, kb * TILE + c * 32, s.NK, s.causal, kp);
                 float g[32];
 #pragma unroll
                 for (int i = 0; i < 32; ++i) {
-                    const int col = c * 32 + i;
-                    const bool v = all || (qv && kb * TILE + col < s.NK && kidx_s[b * TILE + col] <= qpos);
+                    const bool v = all || (qv && kp[i] <= qpos);
                     const float u = __fmaf_rn(s.am1, clamp_score(__uint_as_float(rs[i]), s.scale), -tq);
                     g[i] = v ? grad_pk<PE2>(u, s.pe2.e, __uint_as_float(rp[i]), Dq, invN) : 0.0f;
                 }
@@ -879,7 +899,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
         const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO, Shape s,
         const int32_t* __restrict__ Qidx, const int32_t* __restrict__ Kidx, Bounds bd,
-        const float* __restrict__ tau, const float* __restrict__ rownorm, const float* __restrict__ Dqv,
+        const float* __restrict__ tau, const float* __restrict__ invNv, const float* __restrict__ Dqv,
         const int32_t* __restrict__ cptr, const int32_t* __restrict__ cidx, TO* __restrict__ dK,
         TO* __restrict__ dV, int split, int* err) {
     constexpr int TB = D * TILE * 2;
@@ -904,11 +924,9 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
     uint64_t* ds_free = bars + 8;
     uint64_t* out_full = bars + 9;
     uint32_t* holder = reinterpret_cast<uint32_t*>(bars + 16);
-    float* tau_s = reinterpret_cast<float*>(holder + 4);   // [128] per query of the current block
-    float* inv_s = tau_s + TILE;
-    float* dq_s = inv_s + TILE;
-    int* qp_s = reinterpret_cast<int*>(dq_s + TILE);
-    int* qidx_blk = qp_s + TILE;                           // [128] for the tile-load fix
+    // per query of the current (and next) block: {τ, 1/n, D, position}
+    float4* qinfo = reinterpret_cast<float4*>(holder + 4);   // [2][128]
+    int* qidx_blk = reinterpret_cast<int*>(qinfo + 2 * TILE); // [128] for the tile-load fix
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int bh = blockIdx.y;
@@ -1032,19 +1050,30 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
         const size_t krow = (size_t)bh * s.NK + (kv ? kn : 0);
         const int kpos = !kv ? INT_MAX : (s.causal ? Kidx_bh[kn] : INT_MIN);
         const uint32_t tl = tmem_lane_base(tbase, warp);
+        // Query-block metadata of pair i lives in qinfo[i & 1]; it is fetched
+        // one pair ahead so its global loads overlap the previous pair.
+        auto fetch = [&](int i, float4& out) {
+            const int qb = list[e0 + i];
+            const int q = qb * TILE + et;
+            const bool ok = q < s.NQ;
+            const size_t r = (size_t)bh * s.NQ + (ok ? q : 0);
+            out = make_float4(ok ? tau[r] : 0.0f, ok ? invNv[r] : 0.0f, ok ? Dqv[r] : 0.0f,
+                              __int_as_float(ok ? (s.causal ? Qidx_bh[q] : INT_MAX) : INT_MIN));
+        };
+        if (T > 0 && et < TILE) {
+            float4 v;
+            fetch(0, v);
+            qinfo[et] = v;
+        }
         for (int i = 0; i < T; ++i) {
             const int qb = list[e0 + i];
-            epi_bar();   // previous pair's readers of the per-query arrays are done
-            if (et < TILE) {
-                const int q = qb * TILE + et;
-                const bool ok = q < s.NQ;
-                const size_t r = (size_t)bh * s.NQ + (ok ? q : 0);
-                tau_s[et] = ok ? tau[r] : 0.0f;
-                inv_s[et] = ok ? __fdiv_rn(1.0f, __fadd_rn(rownorm[r], ASA_EPS)) : 0.0f;
-                dq_s[et] = ok ? Dqv[r] : 0.0f;
-                qp_s[et] = ok ? (s.causal ? Qidx_bh[q] : INT_MAX) : INT_MIN;
+            epi_bar();   // qinfo[i&1] written; every reader of qinfo[(i+1)&1] (pair i-1) done
+            if (i + 1 < T && et < TILE) {
+                float4 v;
+                fetch(i + 1, v);
+                qinfo[((i + 1) & 1) * TILE + et] = v;
             }
-            epi_bar();
+            const float4* qi = qinfo + (i & 1) * TILE;
             const bool all = kv && vis_all(s, bd, bh, qb, kb) && (qb + 1) * TILE <= s.NQ;
             mbar_wait(sd_full, i & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
             tc_fence_after();
@@ -1059,10 +1088,10 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
                 float p[32];
 #pragma unroll
                 for (int k = 0; k < 32; ++k) {
-                    const int col = c * 32 + k;
-                    const bool v = all || (kv && kpos <= qp_s[col]);
-                    const float u = __fmaf_rn(s.am1, clamp_score(__uint_as_float(rs[k]), s.scale), -tau_s[col]);
-                    p[k] = v ? entmax_pk<PINV>(u, s.pinv.e) * inv_s[col] : 0.0f;
+                    const float4 m = qi[c * 32 + k];
+                    const bool v = all || (kv && kpos <= __float_as_int(m.w));
+                    const float u = __fmaf_rn(s.am1, clamp_score(__uint_as_float(rs[k]), s.scale), -m.x);
+                    p[k] = v ? entmax_pk<PINV>(u, s.pinv.e) * m.y : 0.0f;
                 }
                 uint32_t hi[16], lo[16];
                 split_pack(p, hi, lo);
@@ -1083,10 +1112,10 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
                 float g[32];
 #pragma unroll
                 for (int k = 0; k < 32; ++k) {
-                    const int col = c * 32 + k;
-                    const bool v = all || (kv && kpos <= qp_s[col]);
-                    const float u = __fmaf_rn(s.am1, clamp_score(__uint_as_float(rs[k]), s.scale), -tau_s[col]);
-                    g[k] = v ? grad_pk<PE2>(u, s.pe2.e, __uint_as_float(rp[k]), dq_s[col], inv_s[col]) : 0.0f;
+                    const float4 m = qi[c * 32 + k];
+                    const bool v = all || (kv && kpos <= __float_as_int(m.w));
+                    const float u = __fmaf_rn(s.am1, clamp_score(__uint_as_float(rs[k]), s.scale), -m.x);
+                    g[k] = v ? grad_pk<PE2>(u, s.pe2.e, __uint_as_float(rp[k]), m.z, m.y) : 0.0f;
                 }
                 uint32_t hi[16], lo[16];
                 split_pack(g, hi, lo);
@@ -1140,7 +1169,8 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
 // ===========================================================================
 template <int D>
 __global__ void k4_pre(const float* __restrict__ O32, const __nv_bfloat16* __restrict__ dO,
-                       float* __restrict__ Dq, size_t rows) {
+                       const float* __restrict__ rownorm, float* __restrict__ Dq,
+                       float* __restrict__ invN, size_t rows) {
     const size_t r = (size_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     if (r >= rows) return;
@@ -1149,7 +1179,10 @@ __global__ void k4_pre(const float* __restrict__ O32, const __nv_bfloat16* __res
     for (int t = lane; t < D; t += 32) acc = fmaf(O32[r * D + t], __bfloat162float(dO[r * D + t]), acc);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-    if (lane == 0) Dq[r] = acc;
+    if (lane == 0) {
+        Dq[r] = acc;
+        invN[r] = __fdiv_rn(1.0f, __fadd_rn(rownorm[r], ASA_EPS));   // reference :435
+    }
 }
 
 
@@ -1214,6 +1247,7 @@ cudaError_t prep(F* f, size_t smem) {
 }
 
 constexpr size_t kSmemTail = 16 * 8 + 16 + 5 * 128 * 4;  // barriers, TMEM holder, per-row arrays
+constexpr size_t kSmemTailBwd = 16 * 8 + 16 + 2 * 128 * 16 + 128 * 4;  // + per-query float4 x2
 
 bool is_sm100() {
     static int cached = -1;
@@ -1235,7 +1269,7 @@ bool tc_supported(const Shape& s) {
 
 size_t tc_fwd_workspace(const Shape& s) { return bounds_ints(s) * 4; }
 size_t tc_bwd_workspace(const Shape& s) {
-    return ((bounds_ints(s) * 4 + 15) & ~size_t(15)) + (size_t)s.BH * s.NQ * 4;
+    return ((bounds_ints(s) * 4 + 15) & ~size_t(15)) + (size_t)2 * s.BH * s.NQ * 4;
 }
 
 // Exponent classes the kernels are specialised for: (1/(α-1), (2-α)/(α-1))
@@ -1319,19 +1353,24 @@ cudaError_t tc_backward(const Shape& s, const void* Q, const void* K, const void
                         const int32_t* Kidx, const float* O32, const float* tau, const int32_t* ptr,
                         const int32_t* idx, const int32_t* cptr, const int32_t* cidx,
                         const float* rownorm, const void* dO, void* dQ, void* dK, void* dV, void* ws,
-                        int* err, cudaStream_t st) {
-    cudaError_t e = launch_bounds(s, Qidx, Kidx, ws, st);
-    if (e != cudaSuccess) return e;
+                        int* err, cudaStream_t st, int stages) {
     Bounds bd = bounds_at(s, ws);
     float* Dq = (float*)((char*)ws + ((bounds_ints(s) * 4 + 15) & ~size_t(15)));
     const size_t rows = (size_t)s.BH * s.NQ;
+    float* invNv = Dq + rows;
+    cudaError_t e = cudaSuccess;
+    if (stages & 1) {
+    e = launch_bounds(s, Qidx, Kidx, ws, st);
+    if (e != cudaSuccess) return e;
     if (s.d == 128)
-        k4_pre<128><<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(O32, (const __nv_bfloat16*)dO, Dq, rows);
+        k4_pre<128><<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(O32, (const __nv_bfloat16*)dO, rownorm, Dq, invNv, rows);
     else
-        k4_pre<64><<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(O32, (const __nv_bfloat16*)dO, Dq, rows);
+        k4_pre<64><<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(O32, (const __nv_bfloat16*)dO, rownorm, Dq, invNv, rows);
     note_launch();
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
+    }
+    if (!(stages & 6)) return cudaSuccess;
     CUtensorMap mQ, mK, mV, mdO;
     if (!make_map(&mQ, Q, s.BH, s.NQ, s.d) || !make_map(&mK, K, s.BH, s.NK, s.d) ||
         !make_map(&mV, V, s.BH, s.NK, s.d) || !make_map(&mdO, dO, s.BH, s.NQ, s.d))
@@ -1343,17 +1382,20 @@ cudaError_t tc_backward(const Shape& s, const void* Q, const void* K, const void
         return with_alpha(s, [&](auto ac) -> cudaError_t {
             auto kdq = k4_dq<D, TO, decltype(ac)::pe2>;
             auto kkv = k4_dkdv<D, TO, decltype(ac)::pinv, decltype(ac)::pe2>;
-            const size_t smem = (size_t)D * TILE * 2 * 4 + (size_t)2 * TILE * TILE * 2 + kSmemTail;
+            const size_t smem = (size_t)D * TILE * 2 * 4 + (size_t)2 * TILE * TILE * 2 + kSmemTailBwd;
             cudaError_t r = prep(kdq, smem);
             if (r == cudaSuccess) r = prep(kkv, smem);
             if (r != cudaSuccess) return r;
-            kdq<<<dim3(s.nQB, s.BH), NTHREADS, smem, st>>>(mQ, mK, mV, mdO, s, Qidx, Kidx, bd, tau,
-                                                          rownorm, Dq, ptr, idx, (TO*)dQ, split, err);
-            note_launch();
-            r = cudaGetLastError();
-            if (r != cudaSuccess) return r;
+            if (stages & 2) {
+                kdq<<<dim3(s.nQB, s.BH), NTHREADS, smem, st>>>(mQ, mK, mV, mdO, s, Qidx, Kidx, bd, tau,
+                                                              invNv, Dq, ptr, idx, (TO*)dQ, split, err);
+                note_launch();
+                r = cudaGetLastError();
+                if (r != cudaSuccess) return r;
+            }
+            if (!(stages & 4)) return cudaSuccess;
             kkv<<<dim3(s.nKB, s.BH), NTHREADS, smem, st>>>(mQ, mK, mV, mdO, s, Qidx, Kidx, bd, tau,
-                                                          rownorm, Dq, cptr, cidx, (TO*)dK, (TO*)dV,
+                                                          invNv, Dq, cptr, cidx, (TO*)dK, (TO*)dV,
                                                           split, err);
             note_launch();
             return cudaGetLastError();
