@@ -570,12 +570,15 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
             }
             __syncwarp();
         };
+        int kbn = T > 0 ? list[e0] : 0;
         for (int j = 0; j < T; ++j) {
-            const int kb = list[e0 + j];
+            const int kb = kbn;
+            const bool fix = needs_fix(s, bd, bh, qb, kb);
+            if (j + 1 < T) kbn = list[e0 + j + 1];
             const int st = j % S, b = j & 1;
             uint8_t* kt = sKV + st * 2 * TB;
             mbar_wait(&kv_full[st], (j / S) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
-            if (needs_fix(s, bd, bh, qb, kb)) {
+            if (fix) {
                 fix_tile<D>(kt, qidx_blk, qmin_blk, Kidx_bh, kb, s.NK, lane);
                 fix_tile<D>(kt + TB, qidx_blk, qmin_blk, Kidx_bh, kb, s.NK, lane);
                 fence_async_smem();
@@ -606,16 +609,21 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
         const float tq = qv ? tau[qrow] : 0.0f;
         const uint32_t tl = tmem_lane_base(tbase, warp);
         float n = 0.0f;
-        int kb_next = T > 0 ? list[e0] : 0;
+        // tile metadata two tiles ahead: kb from the list, then its visibility
+        int kb0 = T > 0 ? list[e0] : 0;
+        int kb1 = T > 1 ? list[e0 + 1] : 0;
+        bool all0 = T > 0 && vis_all(s, bd, bh, qb, kb0);
         for (int j = 0; j < T; ++j) {
-            const int kb = kb_next;
-            if (j + 1 < T) kb_next = list[e0 + j + 1];
+            const int kb = kb0;
+            const bool all = all0;
+            const int kb2 = j + 2 < T ? list[e0 + j + 2] : 0;
+            const bool all1 = j + 1 < T && vis_all(s, bd, bh, qb, kb1);
+            kb0 = kb1; all0 = all1; kb1 = kb2;
             const int b = j & 1;
-            const bool all = vis_all(s, bd, bh, qb, kb);
             mbar_wait(&s_full[b], (j >> 1) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
             tc_fence_after();
-            mbar_wait(p_free, (j & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
-#pragma unroll 1
+            uint32_t hi[2][16], lo[2][16];
+#pragma unroll
             for (int cc = 0; cc < 2; ++cc) {
                 const int c = 2 * h + cc;
                 uint32_t r[32];
@@ -640,13 +648,18 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
                         n += p[i];
                     }
                 }
-                uint32_t hi[16], lo[16];
-                split_pack(p, hi, lo);
-                store_row_chunk(sPh, row, c, hi);
-                if (split) store_row_chunk(sPl, row, c, lo);
+                split_pack(p, hi[cc], lo[cc]);
             }
+            // S is consumed: let the MMA warp reuse the buffer, then wait for
+            // the previous P·V before overwriting P
             tc_fence_before();
             mbar_arrive(&s_free[b]);
+            mbar_wait(p_free, (j & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+#pragma unroll
+            for (int cc = 0; cc < 2; ++cc) {
+                store_row_chunk(sPh, row, 2 * h + cc, hi[cc]);
+                if (split) store_row_chunk(sPl, row, 2 * h + cc, lo[cc]);
+            }
             fence_async_smem();
             mbar_arrive(p_full);
         }
@@ -776,10 +789,13 @@ k4_dq(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
         constexpr uint32_t idS = idesc_bf16(128, 128, 0, 0);
         constexpr uint32_t idQ = idesc_bf16(128, D, 0, 1);
         if (T > 0) mbar_wait(q_full, 0, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+        int kbn = T > 0 ? list[e0] : 0;
         for (int j = 0; j < T; ++j) {
-            const int kb = list[e0 + j];
+            const int kb = kbn;
+            const bool fix = needs_fix(s, bd, bh, qb, kb);
+            if (j + 1 < T) kbn = list[e0 + j + 1];
             mbar_wait(kv_full, j & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
-            if (needs_fix(s, bd, bh, qb, kb)) {
+            if (fix) {
                 fix_tile<D>(sK, qidx_blk, qmin_blk, Kidx_bh, kb, s.NK, lane);
                 fix_tile<D>(sV, qidx_blk, qmin_blk, Kidx_bh, kb, s.NK, lane);
                 fence_async_smem();
@@ -826,16 +842,19 @@ k4_dq(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
         const float invN = qv ? invNv[qrow] : 0.0f;
         const float Dq = qv ? Dqv[qrow] : 0.0f;
         const uint32_t tl = tmem_lane_base(tbase, warp);
-        int kb_next = T > 0 ? list[e0] : 0;
+        int kb0 = T > 0 ? list[e0] : 0;
+        int kb1 = T > 1 ? list[e0 + 1] : 0;
+        bool all0 = T > 0 && vis_all(s, bd, bh, qb, kb0);
         for (int j = 0; j < T; ++j) {
-            const int kb = kb_next;
-            if (j + 1 < T) kb_next = list[e0 + j + 1];
-            const int b = j & 1;
-            const bool all = qv && vis_all(s, bd, bh, qb, kb);
+            const int kb = kb0;
+            const bool all = qv && all0;
+            const int kb2 = j + 2 < T ? list[e0 + j + 2] : 0;
+            const bool all1 = j + 1 < T && vis_all(s, bd, bh, qb, kb1);
+            kb0 = kb1; all0 = all1; kb1 = kb2;
             mbar_wait(sd_full, j & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
             tc_fence_after();
-            mbar_wait(ds_free, (j & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
-#pragma unroll 1
+            uint32_t hi[2][16], lo[2][16];
+#pragma unroll
             for (int cc = 0; cc < 2; ++cc) {
                 const int c = 2 * h + cc;
                 uint32_t rs[32], rp[32];
@@ -851,13 +870,16 @@ k4_dq(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
                     const float u = __fmaf_rn(s.am1, clamp_score(__uint_as_float(rs[i]), s.scale), -tq);
                     g[i] = v ? grad_pk<PE2>(u, s.pe2.e, __uint_as_float(rp[i]), Dq, invN) : 0.0f;
                 }
-                uint32_t hi[16], lo[16];
-                split_pack(g, hi, lo);
-                store_row_chunk(sDh, row, c, hi);
-                if (split) store_row_chunk(sDl, row, c, lo);
+                split_pack(g, hi[cc], lo[cc]);
             }
             tc_fence_before();
             mbar_arrive(sd_free);
+            mbar_wait(ds_free, (j & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+#pragma unroll
+            for (int cc = 0; cc < 2; ++cc) {
+                store_row_chunk(sDh, row, 2 * h + cc, hi[cc]);
+                if (split) store_row_chunk(sDl, row, 2 * h + cc, lo[cc]);
+            }
             fence_async_smem();
             mbar_arrive(ds_full);
         }
@@ -1077,9 +1099,9 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
             const bool all = kv && vis_all(s, bd, bh, qb, kb) && (qb + 1) * TILE <= s.NQ;
             mbar_wait(sd_full, i & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
             tc_fence_after();
-            mbar_wait(ds_free, (i & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
-            // pass 1: P^T / n
-#pragma unroll 1
+            // pass 1: P^T / n (computed, then stored once the buffer is free)
+            uint32_t hi[2][16], lo[2][16];
+#pragma unroll
             for (int cc = 0; cc < 2; ++cc) {
                 const int c = 2 * h + cc;
                 uint32_t rs[32];
@@ -1093,16 +1115,18 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
                     const float u = __fmaf_rn(s.am1, clamp_score(__uint_as_float(rs[k]), s.scale), -m.x);
                     p[k] = v ? entmax_pk<PINV>(u, s.pinv.e) * m.y : 0.0f;
                 }
-                uint32_t hi[16], lo[16];
-                split_pack(p, hi, lo);
-                store_row_chunk(sBh, row, c, hi);
-                if (split) store_row_chunk(sBl, row, c, lo);
+                split_pack(p, hi[cc], lo[cc]);
+            }
+            mbar_wait(ds_free, (i & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+#pragma unroll
+            for (int cc = 0; cc < 2; ++cc) {
+                store_row_chunk(sBh, row, 2 * h + cc, hi[cc]);
+                if (split) store_row_chunk(sBl, row, 2 * h + cc, lo[cc]);
             }
             fence_async_smem();
             mbar_arrive(p_full);
-            mbar_wait(p_free, i & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
             // pass 2: dS^T
-#pragma unroll 1
+#pragma unroll
             for (int cc = 0; cc < 2; ++cc) {
                 const int c = 2 * h + cc;
                 uint32_t rs[32], rp[32];
@@ -1117,13 +1141,16 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
                     const float u = __fmaf_rn(s.am1, clamp_score(__uint_as_float(rs[k]), s.scale), -m.x);
                     g[k] = v ? grad_pk<PE2>(u, s.pe2.e, __uint_as_float(rp[k]), m.z, m.y) : 0.0f;
                 }
-                uint32_t hi[16], lo[16];
-                split_pack(g, hi, lo);
-                store_row_chunk(sBh, row, c, hi);
-                if (split) store_row_chunk(sBl, row, c, lo);
+                split_pack(g, hi[cc], lo[cc]);
             }
             tc_fence_before();
             mbar_arrive(sd_free);
+            mbar_wait(p_free, i & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+#pragma unroll
+            for (int cc = 0; cc < 2; ++cc) {
+                store_row_chunk(sBh, row, 2 * h + cc, hi[cc]);
+                if (split) store_row_chunk(sBl, row, 2 * h + cc, lo[cc]);
+            }
             fence_async_smem();
             mbar_arrive(ds_full);
         }
