@@ -468,6 +468,10 @@ __device__ __forceinline__ void store_out32(TO* dst_row, int c, const float (&o)
 // ===========================================================================
 // K3: forward over the CSR tile list
 // ===========================================================================
+// Shared memory holds Q and three stages each of K and V (K is released as
+// soon as S = Q·K^T completes, V after P·V).  TMEM: S double buffer
+// (columns 0-255), O (256-383), P as bf16 hi/lo pairs (384-447, 448-511)
+// read by the tensor cores as the A operand of O += P·V.
 template <int D, typename TO, int PINV>
 __global__ void __launch_bounds__(NTHREADS, 1)
 k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -475,27 +479,27 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
            const int32_t* __restrict__ Kidx, Bounds bd, const float* __restrict__ tau,
            const int32_t* __restrict__ ptr, const int32_t* __restrict__ idx, TO* __restrict__ O,
            float* __restrict__ O32, float* __restrict__ rownorm, int split, int* err) {
-    constexpr int S = 2;
+    constexpr int S = 3;
     constexpr int TB = D * TILE * 2;
-    constexpr int PB = TILE * TILE * 2;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* base = align1024(smem_raw, err);
     uint8_t* sQ = base;
-    uint8_t* sKV = base + TB;                 // S stages of [K | V]
-    uint8_t* sPh = sKV + S * 2 * TB;
-    uint8_t* sPl = sPh + PB;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(sPl + PB);
+    uint8_t* sK = base + TB;                  // S stages
+    uint8_t* sV = sK + S * TB;                // S stages
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sV + S * TB);
     uint64_t* q_full = bars;
-    uint64_t* kv_full = bars + 1;
-    uint64_t* kv_empty = bars + 1 + S;
-    uint64_t* s_full = bars + 1 + 2 * S;
-    uint64_t* s_free = bars + 3 + 2 * S;
-    uint64_t* p_full = bars + 5 + 2 * S;
-    uint64_t* p_free = bars + 6 + 2 * S;
-    uint64_t* o_full = bars + 7 + 2 * S;
-    uint32_t* holder = reinterpret_cast<uint32_t*>(bars + 16);
-    int* kidx_s = reinterpret_cast<int*>(holder + 4);      // [2][128]; row sums at the end
-    int* qidx_blk = kidx_s + 256;
+    uint64_t* k_full = bars + 1;
+    uint64_t* k_empty = k_full + S;
+    uint64_t* v_full = k_empty + S;
+    uint64_t* v_empty = v_full + S;
+    uint64_t* s_full = v_empty + S;           // [2]
+    uint64_t* s_free = s_full + 2;            // [2]
+    uint64_t* p_full = s_free + 2;
+    uint64_t* p_free = p_full + 1;
+    uint64_t* o_full = p_free + 1;
+    uint32_t* holder = reinterpret_cast<uint32_t*>(bars + 24);
+    float* nsum = reinterpret_cast<float*>(holder + 4);     // [128]
+    int* qidx_blk = reinterpret_cast<int*>(nsum + TILE);    // [128]
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int bh = blockIdx.y;
@@ -507,7 +511,10 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
 
     if (threadIdx.x == 0) {
         mbar_init(q_full, 1);
-        for (int i = 0; i < S; ++i) { mbar_init(&kv_full[i], 1); mbar_init(&kv_empty[i], 1); }
+        for (int i = 0; i < S; ++i) {
+            mbar_init(&k_full[i], 1); mbar_init(&k_empty[i], 1);
+            mbar_init(&v_full[i], 1); mbar_init(&v_empty[i], 1);
+        }
         for (int i = 0; i < 2; ++i) { mbar_init(&s_full[i], 1); mbar_init(&s_free[i], NEPI); }
         mbar_init(p_full, NEPI);
         mbar_init(p_free, 1);
@@ -524,7 +531,7 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
     __syncthreads();
     tc_fence_after();
     const uint32_t tbase = *holder;
-    const uint32_t tO = 256;
+    constexpr uint32_t tO = 256, tPh = 384, tPl = 448;
     const int qmin_blk = s.causal ? bd.qmin[bh * s.nQB + qb] : INT_MIN;
 
     if (warp == 0) {
@@ -538,49 +545,55 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
             for (int j = 0; j < T; ++j) {
                 const int kb = list[e0 + j];
                 const int st = j % S;
-                mbar_wait(&kv_empty[st], ((j / S) & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
-                mbar_expect_tx(&kv_full[st], 2 * TB);
-                uint8_t* kt = sKV + st * 2 * TB;
-                for (int bx = 0; bx < D / BOX; ++bx) {
-                    tma_load_3d(kt + bx * BOX_BYTES, &tmK, &kv_full[st], bx * BOX, kb * TILE, bh);
-                    tma_load_3d(kt + TB + bx * BOX_BYTES, &tmV, &kv_full[st], bx * BOX, kb * TILE, bh);
-                }
+                const uint32_t par = ((j / S) & 1) ^ 1;
+                mbar_wait(&k_empty[st], par, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+                mbar_expect_tx(&k_full[st], TB);
+                for (int bx = 0; bx < D / BOX; ++bx)
+                    tma_load_3d(sK + st * TB + bx * BOX_BYTES, &tmK, &k_full[st], bx * BOX, kb * TILE, bh);
+                mbar_wait(&v_empty[st], par, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+                mbar_expect_tx(&v_full[st], TB);
+                for (int bx = 0; bx < D / BOX; ++bx)
+                    tma_load_3d(sV + st * TB + bx * BOX_BYTES, &tmV, &v_full[st], bx * BOX, kb * TILE, bh);
             }
         }
     } else if (warp == 1) {
         constexpr uint32_t idS = idesc_bf16(128, 128, 0, 0);
         constexpr uint32_t idPV = idesc_bf16(128, D, 0, 1);
         if (T > 0) mbar_wait(q_full, 0, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
-        auto do_pv = [&](int i) {
+        auto do_pv = [&](int i, bool fixed) {
             const int st = i % S;
-            const uint8_t* vt = sKV + st * 2 * TB + TB;
+            const uint8_t* vt = sV + st * TB;
+            if (!fixed) mbar_wait(&v_full[st], (i / S) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
             mbar_wait(p_full, i & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
             tc_fence_after();
             if (lane == 0) {
 #pragma unroll
                 for (int kk = 0; kk < TILE / 16; ++kk)
-                    mma_bf16_ss(tbase + tO, kdesc(sPh, kk), mndesc(vt, kk), idPV, (i > 0 || kk > 0));
+                    mma_bf16_ts(tbase + tO, tbase + tPh + kk * 8, mndesc(vt, kk), idPV, (i > 0 || kk > 0));
                 if (split) {
 #pragma unroll
                     for (int kk = 0; kk < TILE / 16; ++kk)
-                        mma_bf16_ss(tbase + tO, kdesc(sPl, kk), mndesc(vt, kk), idPV, 1);
+                        mma_bf16_ts(tbase + tO, tbase + tPl + kk * 8, mndesc(vt, kk), idPV, 1);
                 }
                 mma_commit(p_free);
-                mma_commit(&kv_empty[st]);
+                mma_commit(&v_empty[st]);
             }
             __syncwarp();
         };
         int kbn = T > 0 ? list[e0] : 0;
+        bool prev_fixed = false;
         for (int j = 0; j < T; ++j) {
             const int kb = kbn;
             const bool fix = needs_fix(s, bd, bh, qb, kb);
             if (j + 1 < T) kbn = list[e0 + j + 1];
             const int st = j % S, b = j & 1;
-            uint8_t* kt = sKV + st * 2 * TB;
-            mbar_wait(&kv_full[st], (j / S) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+            uint8_t* kt = sK + st * TB;
+            mbar_wait(&k_full[st], (j / S) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
             if (fix) {
+                // the zeroing touches V as well: wait for it here
+                mbar_wait(&v_full[st], (j / S) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
                 fix_tile<D>(kt, qidx_blk, qmin_blk, Kidx_bh, kb, s.NK, lane);
-                fix_tile<D>(kt + TB, qidx_blk, qmin_blk, Kidx_bh, kb, s.NK, lane);
+                fix_tile<D>(sV + st * TB, qidx_blk, qmin_blk, Kidx_bh, kb, s.NK, lane);
                 fence_async_smem();
             }
             __syncwarp();
@@ -591,11 +604,13 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
                 for (int kk = 0; kk < D / 16; ++kk)
                     mma_bf16_ss(tbase + b * 128, kdesc(sQ, kk), kdesc(kt, kk), idS, kk > 0);
                 mma_commit(&s_full[b]);
+                mma_commit(&k_empty[st]);
             }
             __syncwarp();
-            if (j > 0) do_pv(j - 1);
+            if (j > 0) do_pv(j - 1, prev_fixed);
+            prev_fixed = fix;
         }
-        if (T > 0) do_pv(T - 1);
+        if (T > 0) do_pv(T - 1, prev_fixed);
         if (lane == 0) mma_commit(o_full);
         __syncwarp();
     } else {
@@ -650,22 +665,23 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
                 }
                 split_pack(p, hi[cc], lo[cc]);
             }
-            // S is consumed: let the MMA warp reuse the buffer, then wait for
-            // the previous P·V before overwriting P
+            // S is consumed: the MMA warp may refill this buffer; P's columns
+            // are rewritten once the previous P·V has read them
             tc_fence_before();
             mbar_arrive(&s_free[b]);
             mbar_wait(p_free, (j & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+            tc_fence_after();
 #pragma unroll
             for (int cc = 0; cc < 2; ++cc) {
-                store_row_chunk(sPh, row, 2 * h + cc, hi[cc]);
-                if (split) store_row_chunk(sPl, row, 2 * h + cc, lo[cc]);
+                const int c = 2 * h + cc;
+                tmem_st16(tl + tPh + c * 16, hi[cc]);
+                if (split) tmem_st16(tl + tPl + c * 16, lo[cc]);
             }
-            fence_async_smem();
+            tmem_st_wait();
+            tc_fence_before();
             mbar_arrive(p_full);
         }
         // row sum = warpgroup 0's half + warpgroup 1's half
-        float* nsum = reinterpret_cast<float*>(kidx_s);
-        epi_bar();
         if (h == 1) nsum[row] = n;
         epi_bar();
         if (h == 0) {
@@ -706,9 +722,12 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
 }
 
 // ===========================================================================
-// K4 dQ: query-major over the CSR list.  S = Q·K^T, dP = dO·V^T; dS in the
-// epilogue (warpgroup h owns key columns [64h, 64h+64)); dQ += dS·K (K tile
-// as the MN-major B operand).
+// K4 dQ: query-major over the CSR list.  S = Q·K^T, dP = dO·V^T into TMEM;
+// the epilogue (warpgroup h owns key columns [64h, 64h+64)) writes dS as a
+// bf16 hi/lo pair into TMEM; dQ += dS·K with dS as the TMEM A operand and
+// the K tile as the MN-major B operand.  TMEM: S 0-127, dP 128-255,
+// dQ 256-383, dS hi 384-447, dS lo 448-511.  K and V have two stages each;
+// V is released after dP, K after dQ.
 // ===========================================================================
 template <int D, typename TO, int PE2>
 __global__ void __launch_bounds__(NTHREADS, 1)
@@ -718,28 +737,27 @@ k4_dq(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
       const float* __restrict__ tau, const float* __restrict__ invNv, const float* __restrict__ Dqv,
       const int32_t* __restrict__ ptr, const int32_t* __restrict__ idx, TO* __restrict__ dQ, int split,
       int* err) {
+    constexpr int S = 2;
     constexpr int TB = D * TILE * 2;
-    constexpr int PB = TILE * TILE * 2;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* base = align1024(smem_raw, err);
     uint8_t* sQ = base;
     uint8_t* sdO = base + TB;
-    uint8_t* sK = base + 2 * TB;
-    uint8_t* sV = base + 3 * TB;
-    uint8_t* sDh = base + 4 * TB;
-    uint8_t* sDl = sDh + PB;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(sDl + PB);
+    uint8_t* sK = base + 2 * TB;              // S stages
+    uint8_t* sV = sK + S * TB;                // S stages
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sV + S * TB);
     uint64_t* q_full = bars;
-    uint64_t* kv_full = bars + 1;
-    uint64_t* kv_empty = bars + 2;
-    uint64_t* sd_full = bars + 3;
-    uint64_t* sd_free = bars + 4;
-    uint64_t* ds_full = bars + 5;
-    uint64_t* ds_free = bars + 6;
-    uint64_t* dq_full = bars + 7;
-    uint32_t* holder = reinterpret_cast<uint32_t*>(bars + 16);
-    int* kidx_s = reinterpret_cast<int*>(holder + 4);     // [2][128]
-    int* qidx_blk = kidx_s + 256;
+    uint64_t* k_full = bars + 1;
+    uint64_t* k_empty = k_full + S;
+    uint64_t* v_full = k_empty + S;
+    uint64_t* v_empty = v_full + S;
+    uint64_t* sd_full = v_empty + S;
+    uint64_t* sd_free = sd_full + 1;
+    uint64_t* ds_full = sd_free + 1;
+    uint64_t* ds_free = ds_full + 1;
+    uint64_t* dq_full = ds_free + 1;
+    uint32_t* holder = reinterpret_cast<uint32_t*>(bars + 24);
+    int* qidx_blk = reinterpret_cast<int*>(holder + 4);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int bh = blockIdx.y;
@@ -750,9 +768,16 @@ k4_dq(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
     const int T = ptr[(size_t)bh * (s.nQB + 1) + qb + 1] - e0;
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < 8; ++i) mbar_init(&bars[i], 1);
+        mbar_init(q_full, 1);
+        for (int i = 0; i < S; ++i) {
+            mbar_init(&k_full[i], 1); mbar_init(&k_empty[i], 1);
+            mbar_init(&v_full[i], 1); mbar_init(&v_empty[i], 1);
+        }
+        mbar_init(sd_full, 1);
         mbar_init(sd_free, NEPI);
         mbar_init(ds_full, NEPI);
+        mbar_init(ds_free, 1);
+        mbar_init(dq_full, 1);
         fence_barrier_init();
     }
     if (warp == 1) { tmem_alloc(holder, 512); tmem_relinquish(); }
@@ -765,7 +790,7 @@ k4_dq(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
     __syncthreads();
     tc_fence_after();
     const uint32_t tbase = *holder;
-    const uint32_t tS = 0, tP = 128, tQ = 256;
+    constexpr uint32_t tS = 0, tP = 128, tQ = 256, tDh = 384, tDl = 448;
     const int qmin_blk = s.causal ? bd.qmin[bh * s.nQB + qb] : INT_MIN;
 
     if (warp == 0) {
@@ -777,27 +802,54 @@ k4_dq(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
             }
             for (int j = 0; j < T; ++j) {
                 const int kb = list[e0 + j];
-                mbar_wait(kv_empty, (j & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
-                mbar_expect_tx(kv_full, 2 * TB);
-                for (int bx = 0; bx < D / BOX; ++bx) {
-                    tma_load_3d(sK + bx * BOX_BYTES, &tmK, kv_full, bx * BOX, kb * TILE, bh);
-                    tma_load_3d(sV + bx * BOX_BYTES, &tmV, kv_full, bx * BOX, kb * TILE, bh);
-                }
+                const int st = j % S;
+                const uint32_t par = ((j / S) & 1) ^ 1;
+                mbar_wait(&k_empty[st], par, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+                mbar_expect_tx(&k_full[st], TB);
+                for (int bx = 0; bx < D / BOX; ++bx)
+                    tma_load_3d(sK + st * TB + bx * BOX_BYTES, &tmK, &k_full[st], bx * BOX, kb * TILE, bh);
+                mbar_wait(&v_empty[st], par, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+                mbar_expect_tx(&v_full[st], TB);
+                for (int bx = 0; bx < D / BOX; ++bx)
+                    tma_load_3d(sV + st * TB + bx * BOX_BYTES, &tmV, &v_full[st], bx * BOX, kb * TILE, bh);
             }
         }
     } else if (warp == 1) {
         constexpr uint32_t idS = idesc_bf16(128, 128, 0, 0);
         constexpr uint32_t idQ = idesc_bf16(128, D, 0, 1);
         if (T > 0) mbar_wait(q_full, 0, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+        auto do_dq = [&](int i) {
+            const int st = i % S;
+            const uint8_t* kt = sK + st * TB;
+            mbar_wait(ds_full, i & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+            tc_fence_after();
+            if (lane == 0) {
+#pragma unroll
+                for (int kk = 0; kk < TILE / 16; ++kk)
+                    mma_bf16_ts(tbase + tQ, tbase + tDh + kk * 8, mndesc(kt, kk), idQ, (i > 0 || kk > 0));
+                if (split) {
+#pragma unroll
+                    for (int kk = 0; kk < TILE / 16; ++kk)
+                        mma_bf16_ts(tbase + tQ, tbase + tDl + kk * 8, mndesc(kt, kk), idQ, 1);
+                }
+                mma_commit(ds_free);
+                mma_commit(&k_empty[st]);
+            }
+            __syncwarp();
+        };
         int kbn = T > 0 ? list[e0] : 0;
         for (int j = 0; j < T; ++j) {
             const int kb = kbn;
             const bool fix = needs_fix(s, bd, bh, qb, kb);
             if (j + 1 < T) kbn = list[e0 + j + 1];
-            mbar_wait(kv_full, j & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+            const int st = j % S;
+            uint8_t* kt = sK + st * TB;
+            uint8_t* vt = sV + st * TB;
+            mbar_wait(&k_full[st], (j / S) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+            mbar_wait(&v_full[st], (j / S) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
             if (fix) {
-                fix_tile<D>(sK, qidx_blk, qmin_blk, Kidx_bh, kb, s.NK, lane);
-                fix_tile<D>(sV, qidx_blk, qmin_blk, Kidx_bh, kb, s.NK, lane);
+                fix_tile<D>(kt, qidx_blk, qmin_blk, Kidx_bh, kb, s.NK, lane);
+                fix_tile<D>(vt, qidx_blk, qmin_blk, Kidx_bh, kb, s.NK, lane);
                 fence_async_smem();
             }
             __syncwarp();
@@ -806,28 +858,16 @@ k4_dq(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
             if (lane == 0) {
 #pragma unroll
                 for (int kk = 0; kk < D / 16; ++kk) {
-                    mma_bf16_ss(tbase + tS, kdesc(sQ, kk), kdesc(sK, kk), idS, kk > 0);
-                    mma_bf16_ss(tbase + tP, kdesc(sdO, kk), kdesc(sV, kk), idS, kk > 0);
+                    mma_bf16_ss(tbase + tS, kdesc(sQ, kk), kdesc(kt, kk), idS, kk > 0);
+                    mma_bf16_ss(tbase + tP, kdesc(sdO, kk), kdesc(vt, kk), idS, kk > 0);
                 }
                 mma_commit(sd_full);
+                mma_commit(&v_empty[st]);
             }
             __syncwarp();
-            mbar_wait(ds_full, j & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
-            tc_fence_after();
-            if (lane == 0) {
-#pragma unroll
-                for (int kk = 0; kk < TILE / 16; ++kk)
-                    mma_bf16_ss(tbase + tQ, kdesc(sDh, kk), mndesc(sK, kk), idQ, (j > 0 || kk > 0));
-                if (split) {
-#pragma unroll
-                    for (int kk = 0; kk < TILE / 16; ++kk)
-                        mma_bf16_ss(tbase + tQ, kdesc(sDl, kk), mndesc(sK, kk), idQ, 1);
-                }
-                mma_commit(ds_free);
-                mma_commit(kv_empty);
-            }
-            __syncwarp();
+            if (j > 0) do_dq(j - 1);
         }
+        if (T > 0) do_dq(T - 1);
         if (lane == 0) mma_commit(dq_full);
         __syncwarp();
     } else {
@@ -875,12 +915,15 @@ k4_dq(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
             tc_fence_before();
             mbar_arrive(sd_free);
             mbar_wait(ds_free, (j & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+            tc_fence_after();
 #pragma unroll
             for (int cc = 0; cc < 2; ++cc) {
-                store_row_chunk(sDh, row, 2 * h + cc, hi[cc]);
-                if (split) store_row_chunk(sDl, row, 2 * h + cc, lo[cc]);
+                const int c = 2 * h + cc;
+                tmem_st16(tl + tDh + c * 16, hi[cc]);
+                if (split) tmem_st16(tl + tDl + c * 16, lo[cc]);
             }
-            fence_async_smem();
+            tmem_st_wait();
+            tc_fence_before();
             mbar_arrive(ds_full);
         }
         mbar_wait(dq_full, 0, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
@@ -1365,7 +1408,7 @@ cudaError_t tc_forward(const Shape& s, const void* Q, const void* K, const void*
         using TO = std::remove_pointer_t<decltype(out)>;
         return with_alpha(s, [&](auto ac) -> cudaError_t {
             auto k = k3_forward<D, TO, decltype(ac)::pinv>;
-            const size_t smem = (size_t)D * TILE * 2 * 5 + (size_t)2 * TILE * TILE * 2 + kSmemTail;
+            const size_t smem = (size_t)D * TILE * 2 * 7 + kSmemTail;
             cudaError_t r = prep(k, smem);
             if (r != cudaSuccess) return r;
             k<<<grid, NTHREADS, smem, st>>>(mQ, mK, mV, s, Qidx, Kidx, bd, tau, ptr, idx, (TO*)O, O32,
