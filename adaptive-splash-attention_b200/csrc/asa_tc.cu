@@ -80,6 +80,58 @@ __device__ __forceinline__ bool needs_fix(const Shape& s, const Bounds& b, int b
     return b.kmax[bh * s.nKB + kb] > b.qmin[bh * s.nQB + qb];
 }
 
+// ---- per-CTA tile schedule ----------------------------------------------------
+// Each CTA stages its tile sequence in shared memory once, so no role chases
+// a global list -> bounds dependency per tile: entry = block index (low 24
+// bits) | SCHED_ALL (every pair of the tile visible) | SCHED_FIX (the
+// reference's tile-load zeroing can apply).
+constexpr uint32_t SCHED_IDX = (1u << 24) - 1, SCHED_ALL = 1u << 30, SCHED_FIX = 1u << 31;
+
+__device__ __forceinline__ uint32_t sched_entry(const Shape& s, const Bounds& bd, int bh, int qb, int kb,
+                                                int idx) {
+    uint32_t e = (uint32_t)idx;
+    if (vis_all(s, bd, bh, qb, kb) && (qb + 1) * TILE <= s.NQ) e |= SCHED_ALL;
+    if (needs_fix(s, bd, bh, qb, kb)) e |= SCHED_FIX;
+    return e;
+}
+
+// Schedule from a CSR (query-major: fixed qb, list of kb) or transposed
+// (key-major: fixed kb, list of qb) tile list; run by the epilogue threads.
+__device__ __forceinline__ void sched_from_list(uint32_t* sched, const int32_t* __restrict__ list, int T,
+                                                const Shape& s, const Bounds& bd, int bh, int fixed,
+                                                bool key_major, int et) {
+    for (int t = et; t < T; t += NEPI) {
+        const int other = list[t];
+        sched[t] = key_major ? sched_entry(s, bd, bh, other, fixed, other)
+                             : sched_entry(s, bd, bh, fixed, other, other);
+    }
+}
+
+// Schedule of every key block with a visible pair for query block qb (the
+// τ / mask pass), compacted in ascending order.  Returns the count; run by
+// the 256 epilogue threads (warp_cnt: 8 ints of shared memory).
+__device__ int sched_visible(uint32_t* sched, int* warp_cnt, const Shape& s, const Bounds& bd, int bh,
+                             int qb, int et) {
+    const int w = et >> 5, lane = et & 31;
+    int total = 0;
+    for (int base = 0; base < s.nKB; base += NEPI) {
+        const int kb = base + et;
+        const bool v = kb < s.nKB && vis_any(s, bd, bh, qb, kb);
+        const uint32_t bal = __ballot_sync(0xffffffffu, v);
+        if (lane == 0) warp_cnt[w] = __popc(bal);
+        epi_bar();
+        int before = 0, all = 0;
+        for (int i = 0; i < NEPI / 32; ++i) {
+            before += i < w ? warp_cnt[i] : 0;
+            all += warp_cnt[i];
+        }
+        if (v) sched[total + before + __popc(bal & ((1u << lane) - 1))] = sched_entry(s, bd, bh, qb, kb, kb);
+        total += all;
+        epi_bar();
+    }
+    return total;
+}
+
 // ---- the reference's tile-load zeroing on a swizzled 128-row tile ------------
 // Element (row r, dim t) of key kb*128+r is zeroed for query block qb when the
 // reference thread that stages it (query qb*128 + ((r*d + t) % 128)) cannot
@@ -96,12 +148,13 @@ __device__ void fix_tile(uint8_t* tile, const int* qidx_blk, int qmin_blk,
 #pragma unroll 1
         for (int ch = 0; ch < D / 8; ++ch) {
             const int t0 = ch * 8;
-            uint32_t keep = 0;
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-                const int off = (r * D + t0 + e) & (TILE - 1);
-                keep |= (kpos <= qidx_blk[off] ? 1u : 0u) << e;
-            }
+            // the 8 staging queries of this 16-byte chunk are consecutive
+            const int4* qp = reinterpret_cast<const int4*>(qidx_blk + ((r * D + t0) & (TILE - 1)));
+            const int4 qa = qp[0], qc = qp[1];
+            const uint32_t keep = (kpos <= qa.x ? 1u : 0u) | (kpos <= qa.y ? 2u : 0u) |
+                                  (kpos <= qa.z ? 4u : 0u) | (kpos <= qa.w ? 8u : 0u) |
+                                  (kpos <= qc.x ? 16u : 0u) | (kpos <= qc.y ? 32u : 0u) |
+                                  (kpos <= qc.z ? 64u : 0u) | (kpos <= qc.w ? 128u : 0u);
             if (keep == 0xffu) continue;
             const int box = t0 / BOX;
             const int phys = ((t0 % BOX) / 8) ^ (r & 7);
@@ -266,10 +319,16 @@ __global__ void tc_bounds_kernel(Shape s, const int32_t* __restrict__ Qidx,
 // ===========================================================================
 // K1: τ and block mask
 // ===========================================================================
-// The two epilogue warpgroups split every S tile by columns (warpgroup h owns
-// keys [64h, 64h+64) of each tile) and keep one partial top-k list per row;
-// warpgroup 0 merges the two lists under (score desc, key asc) -- the order
-// the reference's sequential strict-'>' insertion produces -- and solves τ.
+// Two passes over the row's visible tiles (S = Q·K^T recomputed in TMEM for
+// each).  Pass A keeps, per thread, the k largest 32-column chunk maxima;
+// the k-th of them, t0, is a lower bound for the row half's k-th largest
+// score because those maxima are k distinct scores.  Pass B streams the
+// scores in key order and inserts only those >= t0 with the reference's
+// strict '>' rule, which yields exactly the list full insertion would.
+// The two epilogue warpgroups split every tile by columns (warpgroup h owns
+// keys [64h, 64h+64)) and keep one partial list per row; warpgroup 0 merges
+// them under (score desc, key asc) -- the order sequential insertion
+// produces -- and solves τ.
 template <int D, int KM>
 __global__ void __launch_bounds__(NTHREADS, 1)
 k1_tau_mask(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK, Shape s,
@@ -290,9 +349,10 @@ k1_tau_mask(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
     uint64_t* s_full = bars + 1 + 2 * S;
     uint64_t* s_free = bars + 3 + 2 * S;
     uint32_t* holder = reinterpret_cast<uint32_t*>(bars + 16);
-    int* kidx_s = reinterpret_cast<int*>(holder + 4);      // [2][128]
-    int* qidx_blk = kidx_s + 256;                            // [128]
-    uint8_t* flags = reinterpret_cast<uint8_t*>(qidx_blk + TILE);
+    int* qidx_blk = reinterpret_cast<int*>(holder + 4);      // [128]
+    int* misc = qidx_blk + TILE;                             // [8] warp counts, [8] tile count
+    uint32_t* sched = reinterpret_cast<uint32_t*>(misc + 16);   // [nKB]
+    uint8_t* flags = reinterpret_cast<uint8_t*>(sched + s.nKB);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int bh = blockIdx.y;
@@ -313,41 +373,43 @@ k1_tau_mask(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
             qidx_blk[r] = (q < s.NQ && s.causal) ? Qidx[(size_t)bh * s.NQ + q] : INT_MAX;
         }
         for (int i = r; i < s.nKB; i += NEPI) flags[i] = 0;
+        const int n = sched_visible(sched, misc, s, bd, bh, qb, r);
+        if (r == 0) misc[8] = n;
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tbase = *holder;
     const int qmin_blk = s.causal ? bd.qmin[bh * s.nQB + qb] : INT_MIN;
+    // visible tiles, visited twice in ascending key-block order
+    const int T = misc[8];
 
     if (warp == 0) {
-        if (lane == 0) {
+        if (lane == 0 && T > 0) {
             tma_prefetch_desc(&tmQ);
             tma_prefetch_desc(&tmK);
             mbar_expect_tx(q_full, TB);
             for (int bx = 0; bx < D / BOX; ++bx)
                 tma_load_3d(sQ + bx * BOX_BYTES, &tmQ, q_full, bx * BOX, qb * TILE, bh);
-            int j = 0;
-            for (int kb = 0; kb < s.nKB; ++kb) {
-                if (!vis_any(s, bd, bh, qb, kb)) continue;
+            for (int j = 0; j < 2 * T; ++j) {
+                const int kb = (int)(sched[j < T ? j : j - T] & SCHED_IDX);
                 const int st = j % S;
                 mbar_wait(&k_empty[st], ((j / S) & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
                 mbar_expect_tx(&k_full[st], TB);
                 for (int bx = 0; bx < D / BOX; ++bx)
                     tma_load_3d(sK + st * TB + bx * BOX_BYTES, &tmK, &k_full[st], bx * BOX, kb * TILE, bh);
-                ++j;
             }
         }
     } else if (warp == 1) {
         constexpr uint32_t idesc = idesc_bf16(128, 128, 0, 0);
-        mbar_wait(q_full, 0, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
-        int j = 0;
-        for (int kb = 0; kb < s.nKB; ++kb) {
-            if (!vis_any(s, bd, bh, qb, kb)) continue;
+        if (T > 0) mbar_wait(q_full, 0, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+        for (int j = 0; j < 2 * T; ++j) {
+            const uint32_t e = sched[j < T ? j : j - T];
+            const int kb = (int)(e & SCHED_IDX);
             const int st = j % S, b = j & 1;
             uint8_t* kt = sK + st * TB;
             mbar_wait(&k_full[st], (j / S) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
-            if (needs_fix(s, bd, bh, qb, kb)) {
+            if (e & SCHED_FIX) {
                 fix_tile<D>(kt, qidx_blk, qmin_blk, Kidx_bh, kb, s.NK, lane);
                 fence_async_smem();
             }
@@ -362,7 +424,6 @@ k1_tau_mask(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
                 mma_commit(&k_empty[st]);
             }
             __syncwarp();
-            ++j;
         }
     } else {
         const int row = (warp & 3) * 32 + lane;
@@ -372,41 +433,64 @@ k1_tau_mask(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
         const bool qv = q < s.NQ;
         const int qpos = !qv ? INT_MIN : (s.causal ? Qidx[(size_t)bh * s.NQ + q] : INT_MAX);
         const uint32_t tl = tmem_lane_base(tbase, warp);
+        const bool scale_pos = s.scale > 0.0f;
         TopK<KM> tk;
         tk.init(s.k);
-        const bool scale_pos = s.scale > 0.0f;
-        int j = 0;
-        for (int kb = 0; kb < s.nKB; ++kb) {
-            if (!vis_any(s, bd, bh, qb, kb)) continue;
+        float t0 = neg_inf();
+        for (int j = 0; j < 2 * T; ++j) {
+            const bool passB = j >= T;
+            if (j == T) {
+                t0 = tk.threshold();          // k-th largest chunk maximum (or the sentinel)
+                tk.init(s.k);
+            }
+            const uint32_t e = sched[passB ? j - T : j];
+            const int kb = (int)(e & SCHED_IDX);
             const int b = j & 1;
-            const bool all = vis_all(s, bd, bh, qb, kb);
+            const bool all = (e & SCHED_ALL) != 0;
             mbar_wait(&s_full[b], (j >> 1) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
             tc_fence_after();
-#pragma unroll 1
+            uint32_t r2[2][32];
+            tmem_ld32(tl + b * 128 + (2 * h) * 32, r2[0]);
+            tmem_ld32(tl + b * 128 + (2 * h + 1) * 32, r2[1]);
+            tmem_ld_wait();
+            tc_fence_before();
+            mbar_arrive(&s_free[b]);          // S is in registers: release the buffer
+#pragma unroll
             for (int cc = 0; cc < 2; ++cc) {
                 const int c = 2 * h + cc;
                 const int kn0 = kb * TILE + c * 32;
-                uint32_t r[32];
-                tmem_ld32(tl + b * 128 + c * 32, r);
-                tmem_ld_wait();
-                if (all && scale_pos) {
-                    // clamp(x·scale) is monotone in x: if the chunk's largest raw
-                    // score cannot enter the list, none of its scores can
-                    float m = __uint_as_float(r[0]);
+                const uint32_t (&r)[32] = r2[cc];
+                float mraw = __uint_as_float(r[0]);
 #pragma unroll
-                    for (int i = 1; i < 32; ++i) m = fmaxf(m, __uint_as_float(r[i]));
-                    if (!(clamp_score(m, s.scale) > tk.threshold())) continue;
+                for (int i = 1; i < 32; ++i) mraw = fmaxf(mraw, __uint_as_float(r[i]));
+                const bool fast = all && scale_pos;
+                if (!passB) {
+                    // pass A: this chunk's largest visible score
+                    float m;
+                    if (fast) {
+                        m = clamp_score(mraw, s.scale);    // clamp(x·scale) is monotone in x
+                    } else {
+                        int kp[32];
+                        load_kpos32(Kidx_bh, kn0, s.NK, s.causal, kp);
+                        m = neg_inf();
+#pragma unroll
+                        for (int i = 0; i < 32; ++i)
+                            if (all || kp[i] <= qpos) m = fmaxf(m, clamp_score(__uint_as_float(r[i]), s.scale));
+                    }
+                    if (m > tk.threshold()) tk.insert(m, 0);
+                    continue;
                 }
+                const float lim = fmaxf(tk.threshold(), t0);
+                if (fast && !(clamp_score(mraw, s.scale) >= lim)) continue;
                 int kp[32];
                 if (!all) load_kpos32(Kidx_bh, kn0, s.NK, s.causal, kp);
                 float sv[32];
                 uint32_t cand = 0;
-                const float thr = tk.threshold();
 #pragma unroll
                 for (int i = 0; i < 32; ++i) {
                     const bool v = all || kp[i] <= qpos;
                     sv[i] = v ? clamp_score(__uint_as_float(r[i]), s.scale) : neg_inf();
-                    cand |= (sv[i] > thr ? 1u : 0u) << i;
+                    cand |= (sv[i] >= t0 && sv[i] > tk.threshold() ? 1u : 0u) << i;
                 }
                 while (cand) {
                     const int i = __ffs(cand) - 1;
@@ -415,9 +499,6 @@ k1_tau_mask(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
                     if (val > tk.threshold()) tk.insert(val, kn0 + i);
                 }
             }
-            tc_fence_before();
-            mbar_arrive(&s_free[b]);
-            ++j;
         }
         if (h == 1) {
 #pragma unroll
@@ -479,20 +560,21 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
            const int32_t* __restrict__ Kidx, Bounds bd, const float* __restrict__ tau,
            const int32_t* __restrict__ ptr, const int32_t* __restrict__ idx, TO* __restrict__ O,
            float* __restrict__ O32, float* __restrict__ rownorm, int split, int* err) {
-    constexpr int S = 3;
+    constexpr int S = 3;                      // K stages
+    constexpr int SV = 2;                     // V stages
     constexpr int TB = D * TILE * 2;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* base = align1024(smem_raw, err);
     uint8_t* sQ = base;
     uint8_t* sK = base + TB;                  // S stages
-    uint8_t* sV = sK + S * TB;                // S stages
-    uint64_t* bars = reinterpret_cast<uint64_t*>(sV + S * TB);
+    uint8_t* sV = sK + S * TB;                // SV stages
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sV + SV * TB);
     uint64_t* q_full = bars;
     uint64_t* k_full = bars + 1;
     uint64_t* k_empty = k_full + S;
     uint64_t* v_full = k_empty + S;
-    uint64_t* v_empty = v_full + S;
-    uint64_t* s_full = v_empty + S;           // [2]
+    uint64_t* v_empty = v_full + SV;
+    uint64_t* s_full = v_empty + SV;          // [2]
     uint64_t* s_free = s_full + 2;            // [2]
     uint64_t* p_full = s_free + 2;
     uint64_t* p_free = p_full + 1;
@@ -500,6 +582,7 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
     uint32_t* holder = reinterpret_cast<uint32_t*>(bars + 24);
     float* nsum = reinterpret_cast<float*>(holder + 4);     // [128]
     int* qidx_blk = reinterpret_cast<int*>(nsum + TILE);    // [128]
+    uint32_t* sched = reinterpret_cast<uint32_t*>(qidx_blk + TILE);   // [T]
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int bh = blockIdx.y;
@@ -511,10 +594,8 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
 
     if (threadIdx.x == 0) {
         mbar_init(q_full, 1);
-        for (int i = 0; i < S; ++i) {
-            mbar_init(&k_full[i], 1); mbar_init(&k_empty[i], 1);
-            mbar_init(&v_full[i], 1); mbar_init(&v_empty[i], 1);
-        }
+        for (int i = 0; i < S; ++i) { mbar_init(&k_full[i], 1); mbar_init(&k_empty[i], 1); }
+        for (int i = 0; i < SV; ++i) { mbar_init(&v_full[i], 1); mbar_init(&v_empty[i], 1); }
         for (int i = 0; i < 2; ++i) { mbar_init(&s_full[i], 1); mbar_init(&s_free[i], NEPI); }
         mbar_init(p_full, NEPI);
         mbar_init(p_free, 1);
@@ -522,10 +603,11 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
         fence_barrier_init();
     }
     if (warp == 1) { tmem_alloc(holder, 512); tmem_relinquish(); }
-    if (threadIdx.x >= EPI0 && threadIdx.x < EPI0 + TILE) {
+    if (threadIdx.x >= EPI0) {
         const int r = threadIdx.x - EPI0;
         const int q = qb * TILE + r;
-        qidx_blk[r] = (q < s.NQ && s.causal) ? Qidx[(size_t)bh * s.NQ + q] : INT_MAX;
+        if (r < TILE) qidx_blk[r] = (q < s.NQ && s.causal) ? Qidx[(size_t)bh * s.NQ + q] : INT_MAX;
+        sched_from_list(sched, list + e0, T, s, bd, bh, qb, false, r);
     }
     tc_fence_before();
     __syncthreads();
@@ -543,27 +625,26 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
             for (int bx = 0; bx < D / BOX; ++bx)
                 tma_load_3d(sQ + bx * BOX_BYTES, &tmQ, q_full, bx * BOX, qb * TILE, bh);
             for (int j = 0; j < T; ++j) {
-                const int kb = list[e0 + j];
-                const int st = j % S;
-                const uint32_t par = ((j / S) & 1) ^ 1;
-                mbar_wait(&k_empty[st], par, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+                const int kb = (int)(sched[j] & SCHED_IDX);
+                const int st = j % S, sv = j % SV;
+                mbar_wait(&k_empty[st], ((j / S) & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
                 mbar_expect_tx(&k_full[st], TB);
                 for (int bx = 0; bx < D / BOX; ++bx)
                     tma_load_3d(sK + st * TB + bx * BOX_BYTES, &tmK, &k_full[st], bx * BOX, kb * TILE, bh);
-                mbar_wait(&v_empty[st], par, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
-                mbar_expect_tx(&v_full[st], TB);
+                mbar_wait(&v_empty[sv], ((j / SV) & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+                mbar_expect_tx(&v_full[sv], TB);
                 for (int bx = 0; bx < D / BOX; ++bx)
-                    tma_load_3d(sV + st * TB + bx * BOX_BYTES, &tmV, &v_full[st], bx * BOX, kb * TILE, bh);
+                    tma_load_3d(sV + sv * TB + bx * BOX_BYTES, &tmV, &v_full[sv], bx * BOX, kb * TILE, bh);
             }
         }
     } else if (warp == 1) {
         constexpr uint32_t idS = idesc_bf16(128, 128, 0, 0);
         constexpr uint32_t idPV = idesc_bf16(128, D, 0, 1);
         if (T > 0) mbar_wait(q_full, 0, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
-        auto do_pv = [&](int i, bool fixed) {
-            const int st = i % S;
+        auto do_pv = [&](int i) {
+            const int st = i % SV;
             const uint8_t* vt = sV + st * TB;
-            if (!fixed) mbar_wait(&v_full[st], (i / S) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+            mbar_wait(&v_full[st], (i / SV) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
             mbar_wait(p_full, i & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
             tc_fence_after();
             if (lane == 0) {
@@ -580,20 +661,18 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
             }
             __syncwarp();
         };
-        int kbn = T > 0 ? list[e0] : 0;
-        bool prev_fixed = false;
         for (int j = 0; j < T; ++j) {
-            const int kb = kbn;
-            const bool fix = needs_fix(s, bd, bh, qb, kb);
-            if (j + 1 < T) kbn = list[e0 + j + 1];
+            const uint32_t e = sched[j];
+            const int kb = (int)(e & SCHED_IDX);
+            const bool fix = (e & SCHED_FIX) != 0;
             const int st = j % S, b = j & 1;
             uint8_t* kt = sK + st * TB;
             mbar_wait(&k_full[st], (j / S) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
             if (fix) {
                 // the zeroing touches V as well: wait for it here
-                mbar_wait(&v_full[st], (j / S) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+                mbar_wait(&v_full[j % SV], (j / SV) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
                 fix_tile<D>(kt, qidx_blk, qmin_blk, Kidx_bh, kb, s.NK, lane);
-                fix_tile<D>(sV + st * TB, qidx_blk, qmin_blk, Kidx_bh, kb, s.NK, lane);
+                fix_tile<D>(sV + (j % SV) * TB, qidx_blk, qmin_blk, Kidx_bh, kb, s.NK, lane);
                 fence_async_smem();
             }
             __syncwarp();
@@ -607,10 +686,9 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
                 mma_commit(&k_empty[st]);
             }
             __syncwarp();
-            if (j > 0) do_pv(j - 1, prev_fixed);
-            prev_fixed = fix;
+            if (j > 0) do_pv(j - 1);
         }
-        if (T > 0) do_pv(T - 1, prev_fixed);
+        if (T > 0) do_pv(T - 1);
         if (lane == 0) mma_commit(o_full);
         __syncwarp();
     } else {
@@ -624,16 +702,10 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
         const float tq = qv ? tau[qrow] : 0.0f;
         const uint32_t tl = tmem_lane_base(tbase, warp);
         float n = 0.0f;
-        // tile metadata two tiles ahead: kb from the list, then its visibility
-        int kb0 = T > 0 ? list[e0] : 0;
-        int kb1 = T > 1 ? list[e0 + 1] : 0;
-        bool all0 = T > 0 && vis_all(s, bd, bh, qb, kb0);
         for (int j = 0; j < T; ++j) {
-            const int kb = kb0;
-            const bool all = all0;
-            const int kb2 = j + 2 < T ? list[e0 + j + 2] : 0;
-            const bool all1 = j + 1 < T && vis_all(s, bd, bh, qb, kb1);
-            kb0 = kb1; all0 = all1; kb1 = kb2;
+            const uint32_t e = sched[j];
+            const int kb = (int)(e & SCHED_IDX);
+            const bool all = (e & SCHED_ALL) != 0;
             const int b = j & 1;
             mbar_wait(&s_full[b], (j >> 1) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
             tc_fence_after();
@@ -758,6 +830,7 @@ k4_dq(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
     uint64_t* dq_full = ds_free + 1;
     uint32_t* holder = reinterpret_cast<uint32_t*>(bars + 24);
     int* qidx_blk = reinterpret_cast<int*>(holder + 4);
+    uint32_t* sched = reinterpret_cast<uint32_t*>(qidx_blk + TILE);   // [T]
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int bh = blockIdx.y;
@@ -781,10 +854,11 @@ k4_dq(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
         fence_barrier_init();
     }
     if (warp == 1) { tmem_alloc(holder, 512); tmem_relinquish(); }
-    if (threadIdx.x >= EPI0 && threadIdx.x < EPI0 + TILE) {
+    if (threadIdx.x >= EPI0) {
         const int r = threadIdx.x - EPI0;
         const int q = qb * TILE + r;
-        qidx_blk[r] = (q < s.NQ && s.causal) ? Qidx[(size_t)bh * s.NQ + q] : INT_MAX;
+        if (r < TILE) qidx_blk[r] = (q < s.NQ && s.causal) ? Qidx[(size_t)bh * s.NQ + q] : INT_MAX;
+        sched_from_list(sched, list + e0, T, s, bd, bh, qb, false, r);
     }
     tc_fence_before();
     __syncthreads();
@@ -801,7 +875,7 @@ k4_dq(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
                 tma_load_3d(sdO + bx * BOX_BYTES, &tmdO, q_full, bx * BOX, qb * TILE, bh);
             }
             for (int j = 0; j < T; ++j) {
-                const int kb = list[e0 + j];
+                const int kb = (int)(sched[j] & SCHED_IDX);
                 const int st = j % S;
                 const uint32_t par = ((j / S) & 1) ^ 1;
                 mbar_wait(&k_empty[st], par, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
@@ -837,11 +911,10 @@ k4_dq(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
             }
             __syncwarp();
         };
-        int kbn = T > 0 ? list[e0] : 0;
         for (int j = 0; j < T; ++j) {
-            const int kb = kbn;
-            const bool fix = needs_fix(s, bd, bh, qb, kb);
-            if (j + 1 < T) kbn = list[e0 + j + 1];
+            const uint32_t e = sched[j];
+            const int kb = (int)(e & SCHED_IDX);
+            const bool fix = (e & SCHED_FIX) != 0;
             const int st = j % S;
             uint8_t* kt = sK + st * TB;
             uint8_t* vt = sV + st * TB;
@@ -882,15 +955,10 @@ k4_dq(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
         const float invN = qv ? invNv[qrow] : 0.0f;
         const float Dq = qv ? Dqv[qrow] : 0.0f;
         const uint32_t tl = tmem_lane_base(tbase, warp);
-        int kb0 = T > 0 ? list[e0] : 0;
-        int kb1 = T > 1 ? list[e0 + 1] : 0;
-        bool all0 = T > 0 && vis_all(s, bd, bh, qb, kb0);
         for (int j = 0; j < T; ++j) {
-            const int kb = kb0;
-            const bool all = qv && all0;
-            const int kb2 = j + 2 < T ? list[e0 + j + 2] : 0;
-            const bool all1 = j + 1 < T && vis_all(s, bd, bh, qb, kb1);
-            kb0 = kb1; all0 = all1; kb1 = kb2;
+            const uint32_t e = sched[j];
+            const int kb = (int)(e & SCHED_IDX);
+            const bool all = qv && (e & SCHED_ALL) != 0;
             mbar_wait(sd_full, j & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
             tc_fence_after();
             uint32_t hi[2][16], lo[2][16];
@@ -992,6 +1060,7 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
     // per query of the current (and next) block: {τ, 1/n, D, position}
     float4* qinfo = reinterpret_cast<float4*>(holder + 4);   // [2][128]
     int* qidx_blk = reinterpret_cast<int*>(qinfo + 2 * TILE); // [128] for the tile-load fix
+    uint32_t* sched = reinterpret_cast<uint32_t*>(qidx_blk + TILE);   // [T]
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int bh = blockIdx.y;
@@ -1010,6 +1079,7 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
         fence_barrier_init();
     }
     if (warp == 1) { tmem_alloc(holder, 512); tmem_relinquish(); }
+    if (threadIdx.x >= EPI0) sched_from_list(sched, list + e0, T, s, bd, bh, kb, true, threadIdx.x - EPI0);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -1019,7 +1089,7 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
     if (warp == 0) {
         if (lane == 0 && T > 0) {
             for (int i = 0; i < T; ++i) {
-                const int qb = list[e0 + i];
+                const int qb = (int)(sched[i] & SCHED_IDX);
                 mbar_wait(q_empty, (i & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
                 mbar_expect_tx(q_full, 2 * TB);
                 for (int bx = 0; bx < D / BOX; ++bx) {
@@ -1034,8 +1104,9 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
         int loads = 0;
         bool dirty = true;   // K/V not loaded yet
         for (int i = 0; i < T; ++i) {
-            const int qb = list[e0 + i];
-            const bool fix = needs_fix(s, bd, bh, qb, kb);
+            const uint32_t e = sched[i];
+            const int qb = (int)(e & SCHED_IDX);
+            const bool fix = (e & SCHED_FIX) != 0;
             if (dirty || fix) {
                 // (re)load pristine K/V once the previous pair's S/dP MMAs are done
                 if (i > 0) mbar_wait(sd_full, (i - 1) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
@@ -1118,7 +1189,7 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
         // Query-block metadata of pair i lives in qinfo[i & 1]; it is fetched
         // one pair ahead so its global loads overlap the previous pair.
         auto fetch = [&](int i, float4& out) {
-            const int qb = list[e0 + i];
+            const int qb = (int)(sched[i] & SCHED_IDX);
             const int q = qb * TILE + et;
             const bool ok = q < s.NQ;
             const size_t r = (size_t)bh * s.NQ + (ok ? q : 0);
@@ -1131,7 +1202,7 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
             qinfo[et] = v;
         }
         for (int i = 0; i < T; ++i) {
-            const int qb = list[e0 + i];
+            const uint32_t e = sched[i];
             epi_bar();   // qinfo[i&1] written; every reader of qinfo[(i+1)&1] (pair i-1) done
             if (i + 1 < T && et < TILE) {
                 float4 v;
@@ -1139,7 +1210,7 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
                 qinfo[((i + 1) & 1) * TILE + et] = v;
             }
             const float4* qi = qinfo + (i & 1) * TILE;
-            const bool all = kv && vis_all(s, bd, bh, qb, kb) && (qb + 1) * TILE <= s.NQ;
+            const bool all = kv && (e & SCHED_ALL) != 0;
             mbar_wait(sd_full, i & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
             tc_fence_after();
             // pass 1: P^T / n (computed, then stored once the buffer is free)
@@ -1376,7 +1447,7 @@ cudaError_t tc_tau_mask(const Shape& s, const void* Q, const void* K, const int3
     Bounds bd = bounds_at(s, ws);
     dim3 grid(s.nQB, s.BH);
     auto go = [&](auto kern, int D, int KM) -> cudaError_t {
-        const size_t smem = (size_t)D * TILE * 2 * 5 + (size_t)TILE * KM * 8 + kSmemTail + s.nKB;
+        const size_t smem = (size_t)D * TILE * 2 * 5 + (size_t)TILE * KM * 8 + kSmemTail + (size_t)s.nKB * 5 + 64;
         cudaError_t r = prep(kern, smem);
         if (r != cudaSuccess) return r;
         kern<<<grid, NTHREADS, smem, st>>>(mQ, mK, s, Qidx, Kidx, bd, tau, M, err);
@@ -1408,7 +1479,7 @@ cudaError_t tc_forward(const Shape& s, const void* Q, const void* K, const void*
         using TO = std::remove_pointer_t<decltype(out)>;
         return with_alpha(s, [&](auto ac) -> cudaError_t {
             auto k = k3_forward<D, TO, decltype(ac)::pinv>;
-            const size_t smem = (size_t)D * TILE * 2 * 7 + kSmemTail;
+            const size_t smem = (size_t)D * TILE * 2 * 6 + kSmemTail + (size_t)s.nKB * 4;
             cudaError_t r = prep(k, smem);
             if (r != cudaSuccess) return r;
             k<<<grid, NTHREADS, smem, st>>>(mQ, mK, mV, s, Qidx, Kidx, bd, tau, ptr, idx, (TO*)O, O32,
@@ -1452,7 +1523,8 @@ cudaError_t tc_backward(const Shape& s, const void* Q, const void* K, const void
         return with_alpha(s, [&](auto ac) -> cudaError_t {
             auto kdq = k4_dq<D, TO, decltype(ac)::pe2>;
             auto kkv = k4_dkdv<D, TO, decltype(ac)::pinv, decltype(ac)::pe2>;
-            const size_t smem = (size_t)D * TILE * 2 * 4 + (size_t)2 * TILE * TILE * 2 + kSmemTailBwd;
+            const size_t smem = (size_t)D * TILE * 2 * 4 + (size_t)2 * TILE * TILE * 2 + kSmemTailBwd +
+                                (size_t)(s.nKB > s.nQB ? s.nKB : s.nQB) * 4;
             cudaError_t r = prep(kdq, smem);
             if (r == cudaSuccess) r = prep(kkv, smem);
             if (r != cudaSuccess) return r;
