@@ -65,6 +65,15 @@ __device__ __forceinline__ void epi_bar() {
 
 __device__ __forceinline__ float neg_inf() { return __int_as_float(0xff800000); }
 
+// One arrival per epilogue warp (barriers are initialised with EPI_WARPS):
+// the warp's prior writes and tcgen05 fences are ordered before lane 0's
+// arrive by __syncwarp.
+constexpr int EPI_WARPS = 8;
+__device__ __forceinline__ void epi_arrive(uint64_t* bar) {
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0) sm100::mbar_arrive(bar);
+}
+
 // ---- tile classification (identical in every role) --------------------------
 __device__ __forceinline__ bool vis_any(const Shape& s, const Bounds& b, int bh, int qb, int kb) {
     if (!s.causal) return true;
@@ -329,12 +338,14 @@ __global__ void tc_bounds_kernel(Shape s, const int32_t* __restrict__ Qidx,
 // keys [64h, 64h+64)) and keep one partial list per row; warpgroup 0 merges
 // them under (score desc, key asc) -- the order sequential insertion
 // produces -- and solves τ.
-template <int D, int KM>
+template <int D, int KM, bool TWO_PASS>
 __global__ void __launch_bounds__(NTHREADS, 1)
 k1_tau_mask(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK, Shape s,
             const int32_t* __restrict__ Qidx, const int32_t* __restrict__ Kidx, Bounds bd,
             float* __restrict__ tau, uint8_t* __restrict__ M, int* err) {
-    constexpr int S = 4;
+    constexpr int S = 4;                      // K stages
+    constexpr int NB = 4;                     // S buffers in TMEM (128 columns each)
+    constexpr int NPASS = TWO_PASS ? 2 : 1;
     constexpr int TB = D * TILE * 2;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* base = align1024(smem_raw, err);
@@ -346,9 +357,9 @@ k1_tau_mask(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
     uint64_t* q_full = bars;
     uint64_t* k_full = bars + 1;
     uint64_t* k_empty = bars + 1 + S;
-    uint64_t* s_full = bars + 1 + 2 * S;
-    uint64_t* s_free = bars + 3 + 2 * S;
-    uint32_t* holder = reinterpret_cast<uint32_t*>(bars + 16);
+    uint64_t* s_full = bars + 1 + 2 * S;      // [NB]
+    uint64_t* s_free = s_full + NB;           // [NB]
+    uint32_t* holder = reinterpret_cast<uint32_t*>(bars + 24);
     int* qidx_blk = reinterpret_cast<int*>(holder + 4);      // [128]
     int* misc = qidx_blk + TILE;                             // [8] warp counts, [8] tile count
     uint32_t* sched = reinterpret_cast<uint32_t*>(misc + 16);   // [nKB]
@@ -362,10 +373,15 @@ k1_tau_mask(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
     if (threadIdx.x == 0) {
         mbar_init(q_full, 1);
         for (int i = 0; i < S; ++i) { mbar_init(&k_full[i], 1); mbar_init(&k_empty[i], 1); }
-        for (int i = 0; i < 2; ++i) { mbar_init(&s_full[i], 1); mbar_init(&s_free[i], NEPI); }
+        for (int i = 0; i < NB; ++i) { mbar_init(&s_full[i], 1); mbar_init(&s_free[i], EPI_WARPS); }
         fence_barrier_init();
     }
-    if (warp == 1) { tmem_alloc(holder, 256); tmem_relinquish(); }
+#ifdef ASA_EXP_K1_NOTHING
+    if (true) return;
+#endif
+#ifndef ASA_EXP_K1_NOTMEM
+    if (warp == 1) { tmem_alloc(holder, 512); tmem_relinquish(); }
+#endif
     if (threadIdx.x >= EPI0) {
         const int r = threadIdx.x - EPI0;
         if (r < TILE) {
@@ -373,8 +389,12 @@ k1_tau_mask(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
             qidx_blk[r] = (q < s.NQ && s.causal) ? Qidx[(size_t)bh * s.NQ + q] : INT_MAX;
         }
         for (int i = r; i < s.nKB; i += NEPI) flags[i] = 0;
+#ifdef ASA_EXP_K1_NOSCHED
+        if (r == 0) misc[8] = qb + 1;
+#else
         const int n = sched_visible(sched, misc, s, bd, bh, qb, r);
         if (r == 0) misc[8] = n;
+#endif
     }
     tc_fence_before();
     __syncthreads();
@@ -382,7 +402,21 @@ k1_tau_mask(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
     const uint32_t tbase = *holder;
     const int qmin_blk = s.causal ? bd.qmin[bh * s.nQB + qb] : INT_MIN;
     // visible tiles, visited twice in ascending key-block order
+#ifdef ASA_EXP_K1_EMPTY
+    if (true) {
+        tc_fence_before();
+        __syncthreads();
+#ifndef ASA_EXP_K1_NOTMEM
+        if (warp == 1) { tc_fence_after(); tmem_dealloc(tbase, 512); }
+#endif
+        return;
+    }
+#endif
+#ifdef ASA_EXP_K1_T1
+    const int T = misc[8] > 0 ? 1 : 0;
+#else
     const int T = misc[8];
+#endif
 
     if (warp == 0) {
         if (lane == 0 && T > 0) {
@@ -391,9 +425,12 @@ k1_tau_mask(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
             mbar_expect_tx(q_full, TB);
             for (int bx = 0; bx < D / BOX; ++bx)
                 tma_load_3d(sQ + bx * BOX_BYTES, &tmQ, q_full, bx * BOX, qb * TILE, bh);
-            for (int j = 0; j < 2 * T; ++j) {
+            for (int j = 0; j < NPASS * T; ++j) {
                 const int kb = (int)(sched[j < T ? j : j - T] & SCHED_IDX);
                 const int st = j % S;
+#ifdef ASA_EXP_K1_NOTMA
+                if (j >= S) break;
+#endif
                 mbar_wait(&k_empty[st], ((j / S) & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
                 mbar_expect_tx(&k_full[st], TB);
                 for (int bx = 0; bx < D / BOX; ++bx)
@@ -403,23 +440,32 @@ k1_tau_mask(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
     } else if (warp == 1) {
         constexpr uint32_t idesc = idesc_bf16(128, 128, 0, 0);
         if (T > 0) mbar_wait(q_full, 0, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
-        for (int j = 0; j < 2 * T; ++j) {
+        for (int j = 0; j < NPASS * T; ++j) {
             const uint32_t e = sched[j < T ? j : j - T];
             const int kb = (int)(e & SCHED_IDX);
-            const int st = j % S, b = j & 1;
+            const int st = j % S, b = j % NB;
             uint8_t* kt = sK + st * TB;
+#ifdef ASA_EXP_K1_NOTMA
+            if (j < S)
+#endif
             mbar_wait(&k_full[st], (j / S) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+#ifdef ASA_EXP_K1_NOFIX
+            if (false) {
+#else
             if (e & SCHED_FIX) {
+#endif
                 fix_tile<D>(kt, qidx_blk, qmin_blk, Kidx_bh, kb, s.NK, lane);
                 fence_async_smem();
             }
             __syncwarp();
-            mbar_wait(&s_free[b], ((j >> 1) & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+            mbar_wait(&s_free[b], ((j / NB) & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
             tc_fence_after();
             if (lane == 0) {
+#ifndef ASA_EXP_K1_NOMMA
 #pragma unroll
                 for (int kk = 0; kk < D / 16; ++kk)
                     mma_bf16_ss(tbase + b * 128, kdesc(sQ, kk), kdesc(kt, kk), idesc, kk > 0);
+#endif
                 mma_commit(&s_full[b]);
                 mma_commit(&k_empty[st]);
             }
@@ -437,24 +483,28 @@ k1_tau_mask(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
         TopK<KM> tk;
         tk.init(s.k);
         float t0 = neg_inf();
-        for (int j = 0; j < 2 * T; ++j) {
-            const bool passB = j >= T;
-            if (j == T) {
+        for (int j = 0; j < NPASS * T; ++j) {
+            const bool passB = !TWO_PASS || j >= T;
+            if (TWO_PASS && j == T) {
                 t0 = tk.threshold();          // k-th largest chunk maximum (or the sentinel)
                 tk.init(s.k);
             }
-            const uint32_t e = sched[passB ? j - T : j];
+            const uint32_t e = sched[j < T ? j : j - T];
             const int kb = (int)(e & SCHED_IDX);
-            const int b = j & 1;
+            const int b = j % NB;
             const bool all = (e & SCHED_ALL) != 0;
-            mbar_wait(&s_full[b], (j >> 1) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+            mbar_wait(&s_full[b], (j / NB) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
             tc_fence_after();
             uint32_t r2[2][32];
             tmem_ld32(tl + b * 128 + (2 * h) * 32, r2[0]);
             tmem_ld32(tl + b * 128 + (2 * h + 1) * 32, r2[1]);
             tmem_ld_wait();
             tc_fence_before();
-            mbar_arrive(&s_free[b]);          // S is in registers: release the buffer
+            epi_arrive(&s_free[b]);          // S is in registers: release the buffer
+#ifdef ASA_EXP_K1_NOEPI
+            if (r2[0][0] == 0x7fffffffu && r2[1][3] == 0x7fffffffu) tk.insert(1.0f, j);
+            continue;
+#endif
 #pragma unroll
             for (int cc = 0; cc < 2; ++cc) {
                 const int c = 2 * h + cc;
@@ -525,7 +575,7 @@ k1_tau_mask(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tbase, 256);
+        tmem_dealloc(tbase, 512);
     }
 }
 
@@ -596,8 +646,8 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
         mbar_init(q_full, 1);
         for (int i = 0; i < S; ++i) { mbar_init(&k_full[i], 1); mbar_init(&k_empty[i], 1); }
         for (int i = 0; i < SV; ++i) { mbar_init(&v_full[i], 1); mbar_init(&v_empty[i], 1); }
-        for (int i = 0; i < 2; ++i) { mbar_init(&s_full[i], 1); mbar_init(&s_free[i], NEPI); }
-        mbar_init(p_full, NEPI);
+        for (int i = 0; i < 2; ++i) { mbar_init(&s_full[i], 1); mbar_init(&s_free[i], EPI_WARPS); }
+        mbar_init(p_full, EPI_WARPS);
         mbar_init(p_free, 1);
         mbar_init(o_full, 1);
         fence_barrier_init();
@@ -740,7 +790,7 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
             // S is consumed: the MMA warp may refill this buffer; P's columns
             // are rewritten once the previous P·V has read them
             tc_fence_before();
-            mbar_arrive(&s_free[b]);
+            epi_arrive(&s_free[b]);
             mbar_wait(p_free, (j & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
             tc_fence_after();
 #pragma unroll
@@ -751,7 +801,7 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
             }
             tmem_st_wait();
             tc_fence_before();
-            mbar_arrive(p_full);
+            epi_arrive(p_full);
         }
         // row sum = warpgroup 0's half + warpgroup 1's half
         if (h == 1) nsum[row] = n;
@@ -847,8 +897,8 @@ k4_dq(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
             mbar_init(&v_full[i], 1); mbar_init(&v_empty[i], 1);
         }
         mbar_init(sd_full, 1);
-        mbar_init(sd_free, NEPI);
-        mbar_init(ds_full, NEPI);
+        mbar_init(sd_free, EPI_WARPS);
+        mbar_init(ds_full, EPI_WARPS);
         mbar_init(ds_free, 1);
         mbar_init(dq_full, 1);
         fence_barrier_init();
@@ -981,7 +1031,7 @@ k4_dq(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
                 split_pack(g, hi[cc], lo[cc]);
             }
             tc_fence_before();
-            mbar_arrive(sd_free);
+            epi_arrive(sd_free);
             mbar_wait(ds_free, (j & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
             tc_fence_after();
 #pragma unroll
@@ -992,7 +1042,7 @@ k4_dq(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
             }
             tmem_st_wait();
             tc_fence_before();
-            mbar_arrive(ds_full);
+            epi_arrive(ds_full);
         }
         mbar_wait(dq_full, 0, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
         tc_fence_after();
@@ -1073,9 +1123,9 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < 10; ++i) mbar_init(&bars[i], 1);
-        mbar_init(sd_free, NEPI);
-        mbar_init(p_full, NEPI);
-        mbar_init(ds_full, NEPI);
+        mbar_init(sd_free, EPI_WARPS);
+        mbar_init(p_full, EPI_WARPS);
+        mbar_init(ds_full, EPI_WARPS);
         fence_barrier_init();
     }
     if (warp == 1) { tmem_alloc(holder, 512); tmem_relinquish(); }
@@ -1238,7 +1288,7 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
                 if (split) store_row_chunk(sBl, row, 2 * h + cc, lo[cc]);
             }
             fence_async_smem();
-            mbar_arrive(p_full);
+            epi_arrive(p_full);
             // pass 2: dS^T
 #pragma unroll
             for (int cc = 0; cc < 2; ++cc) {
@@ -1258,7 +1308,7 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
                 split_pack(g, hi[cc], lo[cc]);
             }
             tc_fence_before();
-            mbar_arrive(sd_free);
+            epi_arrive(sd_free);
             mbar_wait(p_free, i & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
 #pragma unroll
             for (int cc = 0; cc < 2; ++cc) {
@@ -1266,7 +1316,7 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
                 if (split) store_row_chunk(sBl, row, 2 * h + cc, lo[cc]);
             }
             fence_async_smem();
-            mbar_arrive(ds_full);
+            epi_arrive(ds_full);
         }
         if (T > 0) {
             mbar_wait(out_full, 0, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
@@ -1454,14 +1504,19 @@ cudaError_t tc_tau_mask(const Shape& s, const void* Q, const void* K, const int3
         note_launch();
         return cudaGetLastError();
     };
+#ifdef ASA_K1_TWO_PASS
+    constexpr bool TP = true;
+#else
+    constexpr bool TP = false;
+#endif
     if (s.d == 128) {
-        if (s.k <= 8) return go(k1_tau_mask<128, 8>, 128, 8);
-        if (s.k <= 16) return go(k1_tau_mask<128, 16>, 128, 16);
-        return go(k1_tau_mask<128, 32>, 128, 32);
+        if (s.k <= 8) return go(k1_tau_mask<128, 8, TP>, 128, 8);
+        if (s.k <= 16) return go(k1_tau_mask<128, 16, TP>, 128, 16);
+        return go(k1_tau_mask<128, 32, TP>, 128, 32);
     }
-    if (s.k <= 8) return go(k1_tau_mask<64, 8>, 64, 8);
-    if (s.k <= 16) return go(k1_tau_mask<64, 16>, 64, 16);
-    return go(k1_tau_mask<64, 32>, 64, 32);
+    if (s.k <= 8) return go(k1_tau_mask<64, 8, TP>, 64, 8);
+    if (s.k <= 16) return go(k1_tau_mask<64, 16, TP>, 64, 16);
+    return go(k1_tau_mask<64, 32, TP>, 64, 32);
 }
 
 cudaError_t tc_forward(const Shape& s, const void* Q, const void* K, const void* V, const int32_t* Qidx,
