@@ -1072,11 +1072,21 @@ k4_dq(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
 }
 
 // ===========================================================================
-// K4 dK/dV: key-major over the transposed list.  S^T = K·Q^T, dP^T = V·dO^T;
-// the epilogue (thread = key row; warpgroup h owns query columns
-// [64h, 64h+64)) writes P^T/n, then dS^T, into one shared buffer;
-// dV += (P^T/n)·dO, dK += dS^T·Q.
+// K4 dK/dV: key-major over the transposed list.  S^T = K·Q^T and
+// dP^T = V·dO^T land in TMEM columns 0-127 and 128-255; the epilogue
+// (thread = key row; warpgroup h owns query chunks 2h, 2h+1 of 32) reads a
+// chunk of both, and writes P^T/n and dS^T back over that chunk's own
+// columns as bf16 hi/lo pairs (S^T chunk c -> P hi | P lo, dP^T chunk c ->
+// dS hi | dS lo), so no warp overwrites data another warp still reads.
+// Then dV += (P^T/n)·dO and dK += dS^T·Q with the pairs as TMEM A operands
+// (dV 256-383, dK 384-511).  Q and dO have two stages.
 // ===========================================================================
+// TMEM column of k-step kk (16 queries) of the hi (or lo) half inside a
+// 128-column region laid out as above.
+__device__ __forceinline__ uint32_t pair_col(int kk, bool lo) {
+    return (uint32_t)((kk >> 1) * 32 + (lo ? 16 : 0) + (kk & 1) * 8);
+}
+
 template <int D, typename TO, int PINV, int PE2>
 __global__ void __launch_bounds__(NTHREADS, 1)
 k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -1085,27 +1095,22 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
         const float* __restrict__ tau, const float* __restrict__ invNv, const float* __restrict__ Dqv,
         const int32_t* __restrict__ cptr, const int32_t* __restrict__ cidx, TO* __restrict__ dK,
         TO* __restrict__ dV, int split, int* err) {
+    constexpr int SQ = 2;                     // Q / dO stages
     constexpr int TB = D * TILE * 2;
-    constexpr int PB = TILE * TILE * 2;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* base = align1024(smem_raw, err);
     uint8_t* sK = base;
     uint8_t* sV = base + TB;
-    uint8_t* sQ = base + 2 * TB;
-    uint8_t* sdO = base + 3 * TB;
-    uint8_t* sBh = base + 4 * TB;
-    uint8_t* sBl = sBh + PB;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(sBl + PB);
+    uint8_t* sQ = base + 2 * TB;              // SQ stages
+    uint8_t* sdO = sQ + SQ * TB;              // SQ stages
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sdO + SQ * TB);
     uint64_t* kv_full = bars;
-    uint64_t* q_full = bars + 1;
-    uint64_t* q_empty = bars + 2;
-    uint64_t* sd_full = bars + 3;
-    uint64_t* sd_free = bars + 4;
-    uint64_t* p_full = bars + 5;
-    uint64_t* p_free = bars + 6;
-    uint64_t* ds_full = bars + 7;
-    uint64_t* ds_free = bars + 8;
-    uint64_t* out_full = bars + 9;
+    uint64_t* q_full = bars + 1;              // [SQ]
+    uint64_t* q_empty = q_full + SQ;          // [SQ]
+    uint64_t* sd_full = q_empty + SQ;
+    uint64_t* pd_full = sd_full + 1;
+    uint64_t* pd_free = pd_full + 1;
+    uint64_t* out_full = pd_free + 1;
     uint32_t* holder = reinterpret_cast<uint32_t*>(bars + 16);
     // per query of the current (and next) block: {τ, 1/n, D, position}
     float4* qinfo = reinterpret_cast<float4*>(holder + 4);   // [2][128]
@@ -1122,10 +1127,12 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
     const int T = cptr[(size_t)bh * (s.nKB + 1) + kb + 1] - e0;
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < 10; ++i) mbar_init(&bars[i], 1);
-        mbar_init(sd_free, EPI_WARPS);
-        mbar_init(p_full, EPI_WARPS);
-        mbar_init(ds_full, EPI_WARPS);
+        mbar_init(kv_full, 1);
+        for (int i = 0; i < SQ; ++i) { mbar_init(&q_full[i], 1); mbar_init(&q_empty[i], 1); }
+        mbar_init(sd_full, 1);
+        mbar_init(pd_full, EPI_WARPS);
+        mbar_init(pd_free, 1);
+        mbar_init(out_full, 1);
         fence_barrier_init();
     }
     if (warp == 1) { tmem_alloc(holder, 512); tmem_relinquish(); }
@@ -1134,17 +1141,18 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
     __syncthreads();
     tc_fence_after();
     const uint32_t tbase = *holder;
-    const uint32_t tS = 0, tP = 128, tV = 256, tK = 256 + D;
+    constexpr uint32_t tS = 0, tP = 128, tV = 256, tK = 256 + D;
 
     if (warp == 0) {
         if (lane == 0 && T > 0) {
             for (int i = 0; i < T; ++i) {
                 const int qb = (int)(sched[i] & SCHED_IDX);
-                mbar_wait(q_empty, (i & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
-                mbar_expect_tx(q_full, 2 * TB);
+                const int st = i % SQ;
+                mbar_wait(&q_empty[st], ((i / SQ) & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+                mbar_expect_tx(&q_full[st], 2 * TB);
                 for (int bx = 0; bx < D / BOX; ++bx) {
-                    tma_load_3d(sQ + bx * BOX_BYTES, &tmQ, q_full, bx * BOX, qb * TILE, bh);
-                    tma_load_3d(sdO + bx * BOX_BYTES, &tmdO, q_full, bx * BOX, qb * TILE, bh);
+                    tma_load_3d(sQ + st * TB + bx * BOX_BYTES, &tmQ, &q_full[st], bx * BOX, qb * TILE, bh);
+                    tma_load_3d(sdO + st * TB + bx * BOX_BYTES, &tmdO, &q_full[st], bx * BOX, qb * TILE, bh);
                 }
             }
         }
@@ -1157,6 +1165,7 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
             const uint32_t e = sched[i];
             const int qb = (int)(e & SCHED_IDX);
             const bool fix = (e & SCHED_FIX) != 0;
+            const int st = i % SQ;
             if (dirty || fix) {
                 // (re)load pristine K/V once the previous pair's S/dP MMAs are done
                 if (i > 0) mbar_wait(sd_full, (i - 1) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
@@ -1183,45 +1192,37 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
                 dirty = fix;
             }
             __syncwarp();
-            mbar_wait(q_full, i & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
-            mbar_wait(sd_free, (i & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+            mbar_wait(&q_full[st], (i / SQ) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+            mbar_wait(pd_free, (i & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
             tc_fence_after();
+            const uint8_t* qt = sQ + st * TB;
+            const uint8_t* ot = sdO + st * TB;
             if (lane == 0) {
 #pragma unroll
                 for (int kk = 0; kk < D / 16; ++kk) {
-                    mma_bf16_ss(tbase + tS, kdesc(sK, kk), kdesc(sQ, kk), idS, kk > 0);
-                    mma_bf16_ss(tbase + tP, kdesc(sV, kk), kdesc(sdO, kk), idS, kk > 0);
+                    mma_bf16_ss(tbase + tS, kdesc(sK, kk), kdesc(qt, kk), idS, kk > 0);
+                    mma_bf16_ss(tbase + tP, kdesc(sV, kk), kdesc(ot, kk), idS, kk > 0);
                 }
                 mma_commit(sd_full);
             }
             __syncwarp();
-            mbar_wait(p_full, i & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+            mbar_wait(pd_full, i & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
             tc_fence_after();
             if (lane == 0) {
 #pragma unroll
-                for (int kk = 0; kk < TILE / 16; ++kk)
-                    mma_bf16_ss(tbase + tV, kdesc(sBh, kk), mndesc(sdO, kk), idO, (i > 0 || kk > 0));
+                for (int kk = 0; kk < TILE / 16; ++kk) {
+                    mma_bf16_ts(tbase + tV, tbase + tS + pair_col(kk, false), mndesc(ot, kk), idO, (i > 0 || kk > 0));
+                    mma_bf16_ts(tbase + tK, tbase + tP + pair_col(kk, false), mndesc(qt, kk), idO, (i > 0 || kk > 0));
+                }
                 if (split) {
 #pragma unroll
-                    for (int kk = 0; kk < TILE / 16; ++kk)
-                        mma_bf16_ss(tbase + tV, kdesc(sBl, kk), mndesc(sdO, kk), idO, 1);
+                    for (int kk = 0; kk < TILE / 16; ++kk) {
+                        mma_bf16_ts(tbase + tV, tbase + tS + pair_col(kk, true), mndesc(ot, kk), idO, 1);
+                        mma_bf16_ts(tbase + tK, tbase + tP + pair_col(kk, true), mndesc(qt, kk), idO, 1);
+                    }
                 }
-                mma_commit(p_free);
-            }
-            __syncwarp();
-            mbar_wait(ds_full, i & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
-            tc_fence_after();
-            if (lane == 0) {
-#pragma unroll
-                for (int kk = 0; kk < TILE / 16; ++kk)
-                    mma_bf16_ss(tbase + tK, kdesc(sBh, kk), mndesc(sQ, kk), idO, (i > 0 || kk > 0));
-                if (split) {
-#pragma unroll
-                    for (int kk = 0; kk < TILE / 16; ++kk)
-                        mma_bf16_ss(tbase + tK, kdesc(sBl, kk), mndesc(sQ, kk), idO, 1);
-                }
-                mma_commit(ds_free);
-                mma_commit(q_empty);
+                mma_commit(pd_free);
+                mma_commit(&q_empty[st]);
             }
             __syncwarp();
         }
@@ -1263,60 +1264,33 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
             const bool all = kv && (e & SCHED_ALL) != 0;
             mbar_wait(sd_full, i & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
             tc_fence_after();
-            // pass 1: P^T / n (computed, then stored once the buffer is free)
-            uint32_t hi[2][16], lo[2][16];
-#pragma unroll
-            for (int cc = 0; cc < 2; ++cc) {
-                const int c = 2 * h + cc;
-                uint32_t rs[32];
-                tmem_ld32(tl + tS + c * 32, rs);
-                tmem_ld_wait();
-                float p[32];
-#pragma unroll
-                for (int k = 0; k < 32; ++k) {
-                    const float4 m = qi[c * 32 + k];
-                    const bool v = all || (kv && kpos <= __float_as_int(m.w));
-                    const float u = __fmaf_rn(s.am1, clamp_score(__uint_as_float(rs[k]), s.scale), -m.x);
-                    p[k] = v ? entmax_pk<PINV>(u, s.pinv.e) * m.y : 0.0f;
-                }
-                split_pack(p, hi[cc], lo[cc]);
-            }
-            mbar_wait(ds_free, (i & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
-#pragma unroll
-            for (int cc = 0; cc < 2; ++cc) {
-                store_row_chunk(sBh, row, 2 * h + cc, hi[cc]);
-                if (split) store_row_chunk(sBl, row, 2 * h + cc, lo[cc]);
-            }
-            fence_async_smem();
-            epi_arrive(p_full);
-            // pass 2: dS^T
-#pragma unroll
+#pragma unroll 1
             for (int cc = 0; cc < 2; ++cc) {
                 const int c = 2 * h + cc;
                 uint32_t rs[32], rp[32];
                 tmem_ld32(tl + tS + c * 32, rs);
                 tmem_ld32(tl + tP + c * 32, rp);
                 tmem_ld_wait();
-                float g[32];
+                float p[32], g[32];
 #pragma unroll
                 for (int k = 0; k < 32; ++k) {
                     const float4 m = qi[c * 32 + k];
                     const bool v = all || (kv && kpos <= __float_as_int(m.w));
                     const float u = __fmaf_rn(s.am1, clamp_score(__uint_as_float(rs[k]), s.scale), -m.x);
+                    p[k] = v ? entmax_pk<PINV>(u, s.pinv.e) * m.y : 0.0f;
                     g[k] = v ? grad_pk<PE2>(u, s.pe2.e, __uint_as_float(rp[k]), m.z, m.y) : 0.0f;
                 }
-                split_pack(g, hi[cc], lo[cc]);
+                uint32_t hi[16], lo[16];
+                split_pack(p, hi, lo);
+                tmem_st16(tl + tS + c * 32, hi);
+                if (split) tmem_st16(tl + tS + c * 32 + 16, lo);
+                split_pack(g, hi, lo);
+                tmem_st16(tl + tP + c * 32, hi);
+                if (split) tmem_st16(tl + tP + c * 32 + 16, lo);
             }
+            tmem_st_wait();
             tc_fence_before();
-            epi_arrive(sd_free);
-            mbar_wait(p_free, i & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
-#pragma unroll
-            for (int cc = 0; cc < 2; ++cc) {
-                store_row_chunk(sBh, row, 2 * h + cc, hi[cc]);
-                if (split) store_row_chunk(sBl, row, 2 * h + cc, lo[cc]);
-            }
-            fence_async_smem();
-            epi_arrive(ds_full);
+            epi_arrive(pd_full);
         }
         if (T > 0) {
             mbar_wait(out_full, 0, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
@@ -1356,7 +1330,7 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
 }
 
 // ===========================================================================
-// K4 pre: D_q = Σ_t O_t · dO_t  (fp32 O, bf16 dO), one warp per row.
+// K4 pre: D_q = Σ_t O_t · dO_t (fp32 O, bf16 dO) and 1/(n+EPS), one warp per row.
 // ===========================================================================
 template <int D>
 __global__ void k4_pre(const float* __restrict__ O32, const __nv_bfloat16* __restrict__ dO,
@@ -1375,8 +1349,6 @@ __global__ void k4_pre(const float* __restrict__ O32, const __nv_bfloat16* __res
         invN[r] = __fdiv_rn(1.0f, __fadd_rn(rownorm[r], ASA_EPS));   // reference :435
     }
 }
-
-
 
 // ===========================================================================
 // host side
@@ -1578,7 +1550,7 @@ cudaError_t tc_backward(const Shape& s, const void* Q, const void* K, const void
         return with_alpha(s, [&](auto ac) -> cudaError_t {
             auto kdq = k4_dq<D, TO, decltype(ac)::pe2>;
             auto kkv = k4_dkdv<D, TO, decltype(ac)::pinv, decltype(ac)::pe2>;
-            const size_t smem = (size_t)D * TILE * 2 * 4 + (size_t)2 * TILE * TILE * 2 + kSmemTailBwd +
+            const size_t smem = (size_t)D * TILE * 2 * 6 + kSmemTailBwd +
                                 (size_t)(s.nKB > s.nQB ? s.nKB : s.nQB) * 4;
             cudaError_t r = prep(kdq, smem);
             if (r == cudaSuccess) r = prep(kkv, smem);
