@@ -39,9 +39,14 @@ using namespace sm100;
 constexpr int TILE = 128;
 constexpr int BOX = 64;                    // bf16 elements per 128-byte swizzle row
 constexpr int BOX_BYTES = TILE * 128;      // one 64-column box of 128 rows
-constexpr int NTHREADS = 320;              // producer warp, MMA warp, two 4-warp epilogue groups
+#ifndef ASA_NWG
+#define ASA_NWG 2
+#endif
+constexpr int NWG = ASA_NWG;               // epilogue warpgroups (each owns 128/NWG columns of a tile)
+constexpr int CPT = 4 / NWG;               // 32-column chunks per epilogue thread per tile
+constexpr int NEPI = 128 * NWG;            // epilogue threads
+constexpr int NTHREADS = 64 + NEPI;        // + producer warp + MMA warp
 constexpr int EPI0 = 64;                   // first epilogue thread
-constexpr int NEPI = 256;                  // epilogue threads
 
 struct Bounds {
     const int* qmin;   // [BH][nQB]
@@ -60,7 +65,7 @@ __device__ __forceinline__ uint8_t* align1024(uint8_t* p, int* err) {
 }
 
 __device__ __forceinline__ void epi_bar() {
-    asm volatile("bar.sync 1, 256;" ::: "memory");
+    asm volatile("bar.sync 1, %0;" ::"n"(NEPI) : "memory");
 }
 
 __device__ __forceinline__ float neg_inf() { return __int_as_float(0xff800000); }
@@ -68,7 +73,7 @@ __device__ __forceinline__ float neg_inf() { return __int_as_float(0xff800000); 
 // One arrival per epilogue warp (barriers are initialised with EPI_WARPS):
 // the warp's prior writes and tcgen05 fences are ordered before lane 0's
 // arrive by __syncwarp.
-constexpr int EPI_WARPS = 8;
+constexpr int EPI_WARPS = NEPI / 32;
 __device__ __forceinline__ void epi_arrive(uint64_t* bar) {
     __syncwarp();
     if ((threadIdx.x & 31) == 0) sm100::mbar_arrive(bar);
@@ -88,6 +93,13 @@ __device__ __forceinline__ bool needs_fix(const Shape& s, const Bounds& b, int b
     if (!s.ref_load) return false;
     return b.kmax[bh * s.nKB + kb] > b.qmin[bh * s.nQB + qb];
 }
+
+#ifdef ASA_EXP_TRACE
+__device__ unsigned long long g_trace[8][64][8];
+#define TRACE(role, j, ev) do { if (blockIdx.x == 0 && blockIdx.y == 0 && (j) < 64) g_trace[role][j][ev] = clock64(); } while (0)
+#else
+#define TRACE(role, j, ev) do {} while (0)
+#endif
 
 // ---- per-CTA tile schedule ----------------------------------------------------
 // Each CTA stages its tile sequence in shared memory once, so no role chases
@@ -495,19 +507,15 @@ k1_tau_mask(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
             const bool all = (e & SCHED_ALL) != 0;
             mbar_wait(&s_full[b], (j / NB) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
             tc_fence_after();
-            uint32_t r2[2][32];
-            tmem_ld32(tl + b * 128 + (2 * h) * 32, r2[0]);
-            tmem_ld32(tl + b * 128 + (2 * h + 1) * 32, r2[1]);
+            uint32_t r2[CPT][32];
+#pragma unroll
+            for (int cc = 0; cc < CPT; ++cc) tmem_ld32(tl + b * 128 + (h * CPT + cc) * 32, r2[cc]);
             tmem_ld_wait();
             tc_fence_before();
             epi_arrive(&s_free[b]);          // S is in registers: release the buffer
-#ifdef ASA_EXP_K1_NOEPI
-            if (r2[0][0] == 0x7fffffffu && r2[1][3] == 0x7fffffffu) tk.insert(1.0f, j);
-            continue;
-#endif
 #pragma unroll
-            for (int cc = 0; cc < 2; ++cc) {
-                const int c = 2 * h + cc;
+            for (int cc = 0; cc < CPT; ++cc) {
+                const int c = h * CPT + cc;
                 const int kn0 = kb * TILE + c * 32;
                 const uint32_t (&r)[32] = r2[cc];
                 float mraw = __uint_as_float(r[0]);
@@ -550,16 +558,21 @@ k1_tau_mask(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
                 }
             }
         }
-        if (h == 1) {
+        // warpgroup 0 merges the other groups' lists one at a time
+        for (int g = 1; g < NWG; ++g) {
+            if (h == g) {
 #pragma unroll
-            for (int i = 0; i < KM; ++i) {
-                topv_s[row * KM + i] = tk.v[i];
-                topi_s[row * KM + i] = tk.i[i];
+                for (int i = 0; i < KM; ++i) {
+                    topv_s[row * KM + i] = tk.v[i];
+                    topi_s[row * KM + i] = tk.i[i];
+                }
             }
+            epi_bar();
+            if (h == 0)
+                for (int i = KM - s.k; i < KM; ++i) tk.insert_lex(topv_s[row * KM + i], topi_s[row * KM + i]);
+            epi_bar();
         }
-        epi_bar();
         if (h == 0) {
-            for (int i = KM - s.k; i < KM; ++i) tk.insert_lex(topv_s[row * KM + i], topi_s[row * KM + i]);
             if (qv) {
                 tau[(size_t)bh * s.NQ + q] = ref_tau<KM>(tk.v, s.k, s.alpha);
 #pragma unroll
@@ -630,8 +643,8 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
     uint64_t* p_free = p_full + 1;
     uint64_t* o_full = p_free + 1;
     uint32_t* holder = reinterpret_cast<uint32_t*>(bars + 24);
-    float* nsum = reinterpret_cast<float*>(holder + 4);     // [128]
-    int* qidx_blk = reinterpret_cast<int*>(nsum + TILE);    // [128]
+    float* nsum = reinterpret_cast<float*>(holder + 4);     // [NWG][128]
+    int* qidx_blk = reinterpret_cast<int*>(nsum + NWG * TILE);    // [128]
     uint32_t* sched = reinterpret_cast<uint32_t*>(qidx_blk + TILE);   // [T]
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -676,12 +689,21 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
                 tma_load_3d(sQ + bx * BOX_BYTES, &tmQ, q_full, bx * BOX, qb * TILE, bh);
             for (int j = 0; j < T; ++j) {
                 const int kb = (int)(sched[j] & SCHED_IDX);
-                const int st = j % S, sv = j % SV;
+                const int st = j % S;
                 mbar_wait(&k_empty[st], ((j / S) & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+                TRACE(0, j, 0);
                 mbar_expect_tx(&k_full[st], TB);
                 for (int bx = 0; bx < D / BOX; ++bx)
                     tma_load_3d(sK + st * TB + bx * BOX_BYTES, &tmK, &k_full[st], bx * BOX, kb * TILE, bh);
+            }
+        } else if (lane == 1 && T > 0) {
+            // V runs on its own thread: its ring (freed after P·V) must not
+            // hold back the K ring (freed after S)
+            for (int j = 0; j < T; ++j) {
+                const int kb = (int)(sched[j] & SCHED_IDX);
+                const int sv = j % SV;
                 mbar_wait(&v_empty[sv], ((j / SV) & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+                TRACE(0, j, 1);
                 mbar_expect_tx(&v_full[sv], TB);
                 for (int bx = 0; bx < D / BOX; ++bx)
                     tma_load_3d(sV + sv * TB + bx * BOX_BYTES, &tmV, &v_full[sv], bx * BOX, kb * TILE, bh);
@@ -696,8 +718,10 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
             const uint8_t* vt = sV + st * TB;
             mbar_wait(&v_full[st], (i / SV) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
             mbar_wait(p_full, i & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+            if (lane == 0) TRACE(1, i, 2);
             tc_fence_after();
             if (lane == 0) {
+#ifndef ASA_EXP_F_NOPV
 #pragma unroll
                 for (int kk = 0; kk < TILE / 16; ++kk)
                     mma_bf16_ts(tbase + tO, tbase + tPh + kk * 8, mndesc(vt, kk), idPV, (i > 0 || kk > 0));
@@ -706,6 +730,7 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
                     for (int kk = 0; kk < TILE / 16; ++kk)
                         mma_bf16_ts(tbase + tO, tbase + tPl + kk * 8, mndesc(vt, kk), idPV, 1);
                 }
+#endif
                 mma_commit(p_free);
                 mma_commit(&v_empty[st]);
             }
@@ -718,6 +743,7 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
             const int st = j % S, b = j & 1;
             uint8_t* kt = sK + st * TB;
             mbar_wait(&k_full[st], (j / S) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+            if (lane == 0) TRACE(1, j, 0);
             if (fix) {
                 // the zeroing touches V as well: wait for it here
                 mbar_wait(&v_full[j % SV], (j / SV) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
@@ -727,11 +753,14 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
             }
             __syncwarp();
             mbar_wait(&s_free[b], ((j >> 1) & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+            if (lane == 0) TRACE(1, j, 1);
             tc_fence_after();
             if (lane == 0) {
+#ifndef ASA_EXP_F_NOS
 #pragma unroll
                 for (int kk = 0; kk < D / 16; ++kk)
                     mma_bf16_ss(tbase + b * 128, kdesc(sQ, kk), kdesc(kt, kk), idS, kk > 0);
+#endif
                 mma_commit(&s_full[b]);
                 mma_commit(&k_empty[st]);
             }
@@ -758,14 +787,19 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
             const bool all = (e & SCHED_ALL) != 0;
             const int b = j & 1;
             mbar_wait(&s_full[b], (j >> 1) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+            if (et == 0) TRACE(2, j, 0);
             tc_fence_after();
-            uint32_t hi[2][16], lo[2][16];
+            uint32_t hi[CPT][16], lo[CPT][16];
 #pragma unroll
-            for (int cc = 0; cc < 2; ++cc) {
-                const int c = 2 * h + cc;
+            for (int cc = 0; cc < CPT; ++cc) {
+                const int c = h * CPT + cc;
                 uint32_t r[32];
                 tmem_ld32(tl + b * 128 + c * 32, r);
                 tmem_ld_wait();
+#ifdef ASA_EXP_F_NOEPI
+                for (int i = 0; i < 16; ++i) { hi[cc][i] = r[i]; lo[cc][i] = r[16 + i]; }
+                continue;
+#endif
                 float p[32];
                 if (all) {
 #pragma unroll
@@ -789,38 +823,38 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
             }
             // S is consumed: the MMA warp may refill this buffer; P's columns
             // are rewritten once the previous P·V has read them
+            if (et == 0) TRACE(2, j, 1);
             tc_fence_before();
             epi_arrive(&s_free[b]);
             mbar_wait(p_free, (j & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+            if (et == 0) TRACE(2, j, 2);
             tc_fence_after();
 #pragma unroll
-            for (int cc = 0; cc < 2; ++cc) {
-                const int c = 2 * h + cc;
+            for (int cc = 0; cc < CPT; ++cc) {
+                const int c = h * CPT + cc;
                 tmem_st16(tl + tPh + c * 16, hi[cc]);
                 if (split) tmem_st16(tl + tPl + c * 16, lo[cc]);
             }
             tmem_st_wait();
+            if (et == 0) TRACE(2, j, 3);
             tc_fence_before();
             epi_arrive(p_full);
         }
-        // row sum = warpgroup 0's half + warpgroup 1's half
-        if (h == 1) nsum[row] = n;
+        // row sum: the warpgroups' partial sums added in group order
+        nsum[h * TILE + row] = n;
         epi_bar();
         if (h == 0) {
-            n = n + nsum[row];
+            for (int g = 1; g < NWG; ++g) n += nsum[g * TILE + row];
             if (qv) rownorm[qrow] = n;
+            nsum[row] = n;
         }
-        epi_bar();
-        if (h == 0) nsum[row] = n;
         epi_bar();
         n = nsum[row];
         mbar_wait(o_full, 0, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
         tc_fence_after();
         const float inv = __fdiv_rn(1.0f, __fadd_rn(n, ASA_EPS));
-        constexpr int CPW = D / 64;     // 32-column chunks per warpgroup
 #pragma unroll 1
-        for (int cc = 0; cc < CPW; ++cc) {
-            const int c = h * CPW + cc;
+        for (int c = h; c < D / 32; c += NWG) {
             uint32_t r[32];
             tmem_ld32(tl + tO + c * 32, r);
             tmem_ld_wait();
@@ -927,12 +961,17 @@ k4_dq(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
             for (int j = 0; j < T; ++j) {
                 const int kb = (int)(sched[j] & SCHED_IDX);
                 const int st = j % S;
-                const uint32_t par = ((j / S) & 1) ^ 1;
-                mbar_wait(&k_empty[st], par, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+                mbar_wait(&k_empty[st], ((j / S) & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
                 mbar_expect_tx(&k_full[st], TB);
                 for (int bx = 0; bx < D / BOX; ++bx)
                     tma_load_3d(sK + st * TB + bx * BOX_BYTES, &tmK, &k_full[st], bx * BOX, kb * TILE, bh);
-                mbar_wait(&v_empty[st], par, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+            }
+        } else if (lane == 1 && T > 0) {
+            // V (freed after dP) on its own thread, ahead of K (freed after dQ)
+            for (int j = 0; j < T; ++j) {
+                const int kb = (int)(sched[j] & SCHED_IDX);
+                const int st = j % S;
+                mbar_wait(&v_empty[st], ((j / S) & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
                 mbar_expect_tx(&v_full[st], TB);
                 for (int bx = 0; bx < D / BOX; ++bx)
                     tma_load_3d(sV + st * TB + bx * BOX_BYTES, &tmV, &v_full[st], bx * BOX, kb * TILE, bh);
@@ -1011,10 +1050,10 @@ k4_dq(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
             const bool all = qv && (e & SCHED_ALL) != 0;
             mbar_wait(sd_full, j & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
             tc_fence_after();
-            uint32_t hi[2][16], lo[2][16];
+            uint32_t hi[CPT][16], lo[CPT][16];
 #pragma unroll
-            for (int cc = 0; cc < 2; ++cc) {
-                const int c = 2 * h + cc;
+            for (int cc = 0; cc < CPT; ++cc) {
+                const int c = h * CPT + cc;
                 uint32_t rs[32], rp[32];
                 tmem_ld32(tl + tS + c * 32, rs);
                 tmem_ld32(tl + tP + c * 32, rp);
@@ -1035,8 +1074,8 @@ k4_dq(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
             mbar_wait(ds_free, (j & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
             tc_fence_after();
 #pragma unroll
-            for (int cc = 0; cc < 2; ++cc) {
-                const int c = 2 * h + cc;
+            for (int cc = 0; cc < CPT; ++cc) {
+                const int c = h * CPT + cc;
                 tmem_st16(tl + tDh + c * 16, hi[cc]);
                 if (split) tmem_st16(tl + tDl + c * 16, lo[cc]);
             }
@@ -1046,10 +1085,8 @@ k4_dq(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
         }
         mbar_wait(dq_full, 0, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
         tc_fence_after();
-        constexpr int CPW = D / 64;
 #pragma unroll 1
-        for (int cc = 0; cc < CPW; ++cc) {
-            const int c = h * CPW + cc;
+        for (int c = h; c < D / 32; c += NWG) {
             uint32_t r[32];
             tmem_ld32(tl + tQ + c * 32, r);
             tmem_ld_wait();
@@ -1074,17 +1111,17 @@ k4_dq(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
 // ===========================================================================
 // K4 dK/dV: key-major over the transposed list.  S^T = K·Q^T and
 // dP^T = V·dO^T land in TMEM columns 0-127 and 128-255; the epilogue
-// (thread = key row; warpgroup h owns query chunks 2h, 2h+1 of 32) reads a
-// chunk of both, and writes P^T/n and dS^T back over that chunk's own
-// columns as bf16 hi/lo pairs (S^T chunk c -> P hi | P lo, dP^T chunk c ->
-// dS hi | dS lo), so no warp overwrites data another warp still reads.
+// (thread = key row; warpgroup h owns queries [32h, 32h+32)) reads 16
+// queries of both at a time and writes P^T/n and dS^T back over those same
+// 16 columns as bf16 hi/lo pairs (8 columns each), so no thread overwrites
+// data another still reads.
 // Then dV += (P^T/n)·dO and dK += dS^T·Q with the pairs as TMEM A operands
 // (dV 256-383, dK 384-511).  Q and dO have two stages.
 // ===========================================================================
-// TMEM column of k-step kk (16 queries) of the hi (or lo) half inside a
-// 128-column region laid out as above.
+// TMEM column of k-step kk (queries 16kk .. 16kk+15) of the hi (or lo)
+// half: each 16-query group's 16 fp32 columns become 8 hi + 8 lo columns.
 __device__ __forceinline__ uint32_t pair_col(int kk, bool lo) {
-    return (uint32_t)((kk >> 1) * 32 + (lo ? 16 : 0) + (kk & 1) * 8);
+    return (uint32_t)(kk * 16 + (lo ? 8 : 0));
 }
 
 template <int D, typename TO, int PINV, int PE2>
@@ -1265,28 +1302,35 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
             mbar_wait(sd_full, i & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
             tc_fence_after();
 #pragma unroll 1
-            for (int cc = 0; cc < 2; ++cc) {
-                const int c = 2 * h + cc;
-                uint32_t rs[32], rp[32];
-                tmem_ld32(tl + tS + c * 32, rs);
-                tmem_ld32(tl + tP + c * 32, rp);
+            for (int gq = h * 2 * CPT; gq < (h + 1) * 2 * CPT; ++gq) {     // 16-query groups
+                uint32_t rs[16], rp[16];
+                tmem_ld16(tl + tS + gq * 16, rs);
+                tmem_ld16(tl + tP + gq * 16, rp);
                 tmem_ld_wait();
-                float p[32], g[32];
+                uint32_t ph[8], pl[8], gh[8], gl[8];
 #pragma unroll
-                for (int k = 0; k < 32; ++k) {
-                    const float4 m = qi[c * 32 + k];
-                    const bool v = all || (kv && kpos <= __float_as_int(m.w));
-                    const float u = __fmaf_rn(s.am1, clamp_score(__uint_as_float(rs[k]), s.scale), -m.x);
-                    p[k] = v ? entmax_pk<PINV>(u, s.pinv.e) * m.y : 0.0f;
-                    g[k] = v ? grad_pk<PE2>(u, s.pe2.e, __uint_as_float(rp[k]), m.z, m.y) : 0.0f;
+                for (int k = 0; k < 16; k += 2) {
+                    float pv[2], gv[2];
+#pragma unroll
+                    for (int t = 0; t < 2; ++t) {
+                        const float4 m = qi[gq * 16 + k + t];
+                        const bool v = all || (kv && kpos <= __float_as_int(m.w));
+                        const float u = __fmaf_rn(s.am1, clamp_score(__uint_as_float(rs[k + t]), s.scale), -m.x);
+                        pv[t] = v ? entmax_pk<PINV>(u, s.pinv.e) * m.y : 0.0f;
+                        gv[t] = v ? grad_pk<PE2>(u, s.pe2.e, __uint_as_float(rp[k + t]), m.z, m.y) : 0.0f;
+                    }
+                    const __nv_bfloat162 a = __floats2bfloat162_rn(pv[0], pv[1]);
+                    const __nv_bfloat162 c2 = __floats2bfloat162_rn(gv[0], gv[1]);
+                    const float2 af = __bfloat1622float2(a), cf = __bfloat1622float2(c2);
+                    ph[k >> 1] = *reinterpret_cast<const uint32_t*>(&a);
+                    gh[k >> 1] = *reinterpret_cast<const uint32_t*>(&c2);
+                    pl[k >> 1] = pack_bf16(pv[0] - af.x, pv[1] - af.y);
+                    gl[k >> 1] = pack_bf16(gv[0] - cf.x, gv[1] - cf.y);
                 }
-                uint32_t hi[16], lo[16];
-                split_pack(p, hi, lo);
-                tmem_st16(tl + tS + c * 32, hi);
-                if (split) tmem_st16(tl + tS + c * 32 + 16, lo);
-                split_pack(g, hi, lo);
-                tmem_st16(tl + tP + c * 32, hi);
-                if (split) tmem_st16(tl + tP + c * 32 + 16, lo);
+                tmem_st8(tl + tS + gq * 16, ph);
+                if (split) tmem_st8(tl + tS + gq * 16 + 8, pl);
+                tmem_st8(tl + tP + gq * 16, gh);
+                if (split) tmem_st8(tl + tP + gq * 16 + 8, gl);
             }
             tmem_st_wait();
             tc_fence_before();
@@ -1296,15 +1340,13 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
             mbar_wait(out_full, 0, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
             tc_fence_after();
         }
-        constexpr int CPW = D / 64;
 #pragma unroll 1
         for (int part = 0; part < 2; ++part) {
             TO* dst_base = part == 0 ? dV : dK;
             const float mul = part == 0 ? 1.0f : s.scale;
             const uint32_t col0 = part == 0 ? tV : tK;
 #pragma unroll 1
-            for (int cc = 0; cc < CPW; ++cc) {
-                const int c = h * CPW + cc;
+            for (int c = h; c < D / 32; c += NWG) {
                 uint32_t r[32];
                 if (T > 0) {
                     tmem_ld32(tl + col0 + c * 32, r);
@@ -1409,7 +1451,7 @@ cudaError_t prep(F* f, size_t smem) {
     return cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
 }
 
-constexpr size_t kSmemTail = 16 * 8 + 16 + 5 * 128 * 4;  // barriers, TMEM holder, per-row arrays
+constexpr size_t kSmemTail = 24 * 8 + 16 + (NWG + 1) * 128 * 4 + 64;  // barriers, TMEM holder, per-row arrays
 constexpr size_t kSmemTailBwd = 16 * 8 + 16 + 2 * 128 * 16 + 128 * 4;  // + per-query float4 x2
 
 bool is_sm100() {
@@ -1573,3 +1615,14 @@ cudaError_t tc_backward(const Shape& s, const void* Q, const void* K, const void
 }
 
 }  // namespace asa
+
+#ifdef ASA_EXP_TRACE
+namespace asa {
+void* exp_trace_ptr_impl();
+}
+extern "C" void* asa_exp_trace_ptr() {
+    void* p = nullptr;
+    cudaGetSymbolAddress(&p, asa::g_trace);
+    return p;
+}
+#endif
