@@ -612,10 +612,13 @@ __device__ __forceinline__ void store_out32(TO* dst_row, int c, const float (&o)
 // ===========================================================================
 // K3: forward over the CSR tile list
 // ===========================================================================
-// Shared memory holds Q and three stages each of K and V (K is released as
-// soon as S = Q·K^T completes, V after P·V).  TMEM: S double buffer
-// (columns 0-255), O (256-383), P as bf16 hi/lo pairs (384-447, 448-511)
-// read by the tensor cores as the A operand of O += P·V.
+// Shared memory: Q, three K stages (released once S = Q·K^T completes) and
+// two V stages (released after P·V), loaded by separate producer threads.
+// TMEM: three S buffers (columns 0-383) and O (384-511).  The epilogue
+// writes P back over its own S columns as bf16 hi/lo pairs (each 16-key
+// group: 8 hi columns then 8 lo columns), which the tensor cores read as the
+// A operand of O += P·V; a buffer is reused once that P·V completes.  The MMA
+// warp issues S two tiles ahead of the P·V it waits for.
 template <int D, typename TO, int PINV>
 __global__ void __launch_bounds__(NTHREADS, 1)
 k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -625,6 +628,7 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
            float* __restrict__ O32, float* __restrict__ rownorm, int split, int* err) {
     constexpr int S = 3;                      // K stages
     constexpr int SV = 2;                     // V stages
+    constexpr int NB = 3;                     // S / P buffers in TMEM
     constexpr int TB = D * TILE * 2;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* base = align1024(smem_raw, err);
@@ -637,11 +641,10 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
     uint64_t* k_empty = k_full + S;
     uint64_t* v_full = k_empty + S;
     uint64_t* v_empty = v_full + SV;
-    uint64_t* s_full = v_empty + SV;          // [2]
-    uint64_t* s_free = s_full + 2;            // [2]
-    uint64_t* p_full = s_free + 2;
-    uint64_t* p_free = p_full + 1;
-    uint64_t* o_full = p_free + 1;
+    uint64_t* s_full = v_empty + SV;          // [NB]
+    uint64_t* s_free = s_full + NB;           // [NB]
+    uint64_t* p_full = s_free + NB;           // [NB]
+    uint64_t* o_full = p_full + NB;
     uint32_t* holder = reinterpret_cast<uint32_t*>(bars + 24);
     float* nsum = reinterpret_cast<float*>(holder + 4);     // [NWG][128]
     int* qidx_blk = reinterpret_cast<int*>(nsum + NWG * TILE);    // [128]
@@ -659,9 +662,9 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
         mbar_init(q_full, 1);
         for (int i = 0; i < S; ++i) { mbar_init(&k_full[i], 1); mbar_init(&k_empty[i], 1); }
         for (int i = 0; i < SV; ++i) { mbar_init(&v_full[i], 1); mbar_init(&v_empty[i], 1); }
-        for (int i = 0; i < 2; ++i) { mbar_init(&s_full[i], 1); mbar_init(&s_free[i], EPI_WARPS); }
-        mbar_init(p_full, EPI_WARPS);
-        mbar_init(p_free, 1);
+        for (int i = 0; i < NB; ++i) {
+            mbar_init(&s_full[i], 1); mbar_init(&s_free[i], 1); mbar_init(&p_full[i], EPI_WARPS);
+        }
         mbar_init(o_full, 1);
         fence_barrier_init();
     }
@@ -676,7 +679,7 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
     __syncthreads();
     tc_fence_after();
     const uint32_t tbase = *holder;
-    constexpr uint32_t tO = 256, tPh = 384, tPl = 448;
+    constexpr uint32_t tO = 384;
     const int qmin_blk = s.causal ? bd.qmin[bh * s.nQB + qb] : INT_MIN;
 
     if (warp == 0) {
@@ -713,46 +716,19 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
         constexpr uint32_t idS = idesc_bf16(128, 128, 0, 0);
         constexpr uint32_t idPV = idesc_bf16(128, D, 0, 1);
         if (T > 0) mbar_wait(q_full, 0, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
-        auto do_pv = [&](int i) {
-            const int st = i % SV;
-            const uint8_t* vt = sV + st * TB;
-            mbar_wait(&v_full[st], (i / SV) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
-            mbar_wait(p_full, i & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
-            if (lane == 0) TRACE(1, i, 2);
-            tc_fence_after();
-            if (lane == 0) {
-#ifndef ASA_EXP_F_NOPV
-#pragma unroll
-                for (int kk = 0; kk < TILE / 16; ++kk)
-                    mma_bf16_ts(tbase + tO, tbase + tPh + kk * 8, mndesc(vt, kk), idPV, (i > 0 || kk > 0));
-                if (split) {
-#pragma unroll
-                    for (int kk = 0; kk < TILE / 16; ++kk)
-                        mma_bf16_ts(tbase + tO, tbase + tPl + kk * 8, mndesc(vt, kk), idPV, 1);
-                }
-#endif
-                mma_commit(p_free);
-                mma_commit(&v_empty[st]);
-            }
-            __syncwarp();
-        };
-        for (int j = 0; j < T; ++j) {
+        auto issue_s = [&](int j) {
             const uint32_t e = sched[j];
             const int kb = (int)(e & SCHED_IDX);
-            const bool fix = (e & SCHED_FIX) != 0;
-            const int st = j % S, b = j & 1;
+            const int st = j % S, b = j % NB;
             uint8_t* kt = sK + st * TB;
             mbar_wait(&k_full[st], (j / S) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
             if (lane == 0) TRACE(1, j, 0);
-            if (fix) {
-                // the zeroing touches V as well: wait for it here
-                mbar_wait(&v_full[j % SV], (j / SV) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+            if (e & SCHED_FIX) {   // V is fixed before its P·V
                 fix_tile<D>(kt, qidx_blk, qmin_blk, Kidx_bh, kb, s.NK, lane);
-                fix_tile<D>(sV + (j % SV) * TB, qidx_blk, qmin_blk, Kidx_bh, kb, s.NK, lane);
                 fence_async_smem();
             }
             __syncwarp();
-            mbar_wait(&s_free[b], ((j >> 1) & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+            mbar_wait(&s_free[b], ((j / NB) & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
             if (lane == 0) TRACE(1, j, 1);
             tc_fence_after();
             if (lane == 0) {
@@ -764,10 +740,42 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
                 mma_commit(&s_full[b]);
                 mma_commit(&k_empty[st]);
             }
+            if (lane == 0) TRACE(1, j, 3);
             __syncwarp();
-            if (j > 0) do_pv(j - 1);
+        };
+        if (T > 0) issue_s(0);
+        if (T > 1) issue_s(1);
+        for (int j = 0; j < T; ++j) {
+            if (j + 2 < T) issue_s(j + 2);
+            const int b = j % NB, sv = j % SV;
+            const uint8_t* vt = sV + sv * TB;
+            mbar_wait(&v_full[sv], (j / SV) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+            if (sched[j] & SCHED_FIX) {
+                fix_tile<D>(sV + sv * TB, qidx_blk, qmin_blk, Kidx_bh, (int)(sched[j] & SCHED_IDX), s.NK, lane);
+                fence_async_smem();
+            }
+            __syncwarp();
+            mbar_wait(&p_full[b], (j / NB) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+            if (lane == 0) TRACE(1, j, 2);
+            tc_fence_after();
+            if (lane == 0) {
+                const uint32_t pb = tbase + b * 128;
+#ifndef ASA_EXP_F_NOPV
+#pragma unroll
+                for (int kk = 0; kk < TILE / 16; ++kk)
+                    mma_bf16_ts(tbase + tO, pb + kk * 16, mndesc(vt, kk), idPV, (j > 0 || kk > 0));
+                if (split) {
+#pragma unroll
+                    for (int kk = 0; kk < TILE / 16; ++kk)
+                        mma_bf16_ts(tbase + tO, pb + kk * 16 + 8, mndesc(vt, kk), idPV, 1);
+                }
+#endif
+                mma_commit(&s_free[b]);
+                mma_commit(&v_empty[sv]);
+            }
+            if (lane == 0) TRACE(1, j, 4);
+            __syncwarp();
         }
-        if (T > 0) do_pv(T - 1);
         if (lane == 0) mma_commit(o_full);
         __syncwarp();
     } else {
@@ -785,21 +793,16 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
             const uint32_t e = sched[j];
             const int kb = (int)(e & SCHED_IDX);
             const bool all = (e & SCHED_ALL) != 0;
-            const int b = j & 1;
-            mbar_wait(&s_full[b], (j >> 1) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+            const int b = j % NB;
+            mbar_wait(&s_full[b], (j / NB) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
             if (et == 0) TRACE(2, j, 0);
             tc_fence_after();
-            uint32_t hi[CPT][16], lo[CPT][16];
 #pragma unroll
             for (int cc = 0; cc < CPT; ++cc) {
                 const int c = h * CPT + cc;
                 uint32_t r[32];
                 tmem_ld32(tl + b * 128 + c * 32, r);
                 tmem_ld_wait();
-#ifdef ASA_EXP_F_NOEPI
-                for (int i = 0; i < 16; ++i) { hi[cc][i] = r[i]; lo[cc][i] = r[16 + i]; }
-                continue;
-#endif
                 float p[32];
                 if (all) {
 #pragma unroll
@@ -819,26 +822,27 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
                         n += p[i];
                     }
                 }
-                split_pack(p, hi[cc], lo[cc]);
-            }
-            // S is consumed: the MMA warp may refill this buffer; P's columns
-            // are rewritten once the previous P·V has read them
-            if (et == 0) TRACE(2, j, 1);
-            tc_fence_before();
-            epi_arrive(&s_free[b]);
-            mbar_wait(p_free, (j & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
-            if (et == 0) TRACE(2, j, 2);
-            tc_fence_after();
+                // two 16-key groups: hi then lo columns over the group's own S columns
 #pragma unroll
-            for (int cc = 0; cc < CPT; ++cc) {
-                const int c = h * CPT + cc;
-                tmem_st16(tl + tPh + c * 16, hi[cc]);
-                if (split) tmem_st16(tl + tPl + c * 16, lo[cc]);
+                for (int g = 0; g < 2; ++g) {
+                    uint32_t hi[8], lo[8];
+#pragma unroll
+                    for (int m = 0; m < 8; ++m) {
+                        const float x0 = p[16 * g + 2 * m], x1 = p[16 * g + 2 * m + 1];
+                        const __nv_bfloat162 hh = __floats2bfloat162_rn(x0, x1);
+                        const float2 hf = __bfloat1622float2(hh);
+                        hi[m] = *reinterpret_cast<const uint32_t*>(&hh);
+                        lo[m] = pack_bf16(x0 - hf.x, x1 - hf.y);
+                    }
+                    tmem_st8(tl + b * 128 + c * 32 + g * 16, hi);
+                    if (split) tmem_st8(tl + b * 128 + c * 32 + g * 16 + 8, lo);
+                }
             }
+            if (et == 0) TRACE(2, j, 1);
             tmem_st_wait();
             if (et == 0) TRACE(2, j, 3);
             tc_fence_before();
-            epi_arrive(p_full);
+            epi_arrive(&p_full[b]);
         }
         // row sum: the warpgroups' partial sums added in group order
         nsum[h * TILE + row] = n;
