@@ -100,6 +100,16 @@ __device__ unsigned long long g_trace[8][64][8];
 #else
 #define TRACE(role, j, ev) do {} while (0)
 #endif
+#ifdef ASA_EXP_CTA
+__device__ unsigned long long g_cta[4][4096][4];
+__device__ __forceinline__ unsigned long long gtimer() {
+    unsigned long long t; asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t)); return t;
+}
+#define CTA_MARK(k, ev) do { if (threadIdx.x == 0) { const int c_ = blockIdx.y * gridDim.x + blockIdx.x; \
+    if (c_ < 4096) { g_cta[k][c_][ev] = gtimer(); if ((ev) == 0) { unsigned sm_; asm("mov.u32 %0, %smid;" : "=r"(sm_)); g_cta[k][c_][3] = sm_; } } } } while (0)
+#else
+#define CTA_MARK(k, ev) do {} while (0)
+#endif
 
 // ---- per-CTA tile schedule ----------------------------------------------------
 // Each CTA stages its tile sequence in shared memory once, so no role chases
@@ -218,6 +228,29 @@ __device__ __forceinline__ void store_row_chunk(uint8_t* tile, int row, int c, c
 __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
     __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
     return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// Packed (two-lane fp32) entmax weights for exponent classes 1, 2 and 4:
+// u = clamp(c1·raw - τ) with c1 = (α-1)·sm_scale, upper bound (α-1)·10 - τ
+// and lower bound 0 (callers take this path only when (α-1)·(-10) - τ <= 0,
+// so the score clamp at -10 can only meet u <= 0, where p = 0).  The EPS
+// floor of the reference changes p only below 1e-16 (exponent 2) and is
+// dropped.  p pairs are split into bf16 hi (rounded) and lo (remainder)
+// halves packed two per 32-bit word; the row sum gathers in two lanes.
+template <int PK>
+__device__ __forceinline__ float2 entmax_pair(uint32_t r0, uint32_t r1, float2 c1, float2 mtau, float uhi) {
+    float2 u = __ffma2_rn(make_float2(__uint_as_float(r0), __uint_as_float(r1)), c1, mtau);
+    u.x = fmaxf(fminf(u.x, uhi), 0.0f);
+    u.y = fmaxf(fminf(u.y, uhi), 0.0f);
+    if constexpr (PK == 1) return u;
+    else if constexpr (PK == 2) return __fmul2_rn(u, u);
+    else { const float2 q = __fmul2_rn(u, u); return __fmul2_rn(q, q); }
+}
+__device__ __forceinline__ void split_pair(float2 p, uint32_t& hi, uint32_t& lo) {
+    hi = pack_bf16(p.x, p.y);
+    const float2 hf = make_float2(__uint_as_float(hi << 16), __uint_as_float(hi & 0xffff0000u));
+    const float2 l = __ffma2_rn(hf, make_float2(-1.0f, -1.0f), p);
+    lo = pack_bf16(l.x, l.y);
 }
 
 // hi/lo split of 32 values: hi = bf16(x), lo = bf16(x - hi).  With split=false
@@ -360,6 +393,7 @@ k1_tau_mask(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
     constexpr int NPASS = TWO_PASS ? 2 : 1;
     constexpr int TB = D * TILE * 2;
     extern __shared__ uint8_t smem_raw[];
+    CTA_MARK(0, 0);
     uint8_t* base = align1024(smem_raw, err);
     uint8_t* sQ = base;
     uint8_t* sK = base + TB;
@@ -410,6 +444,7 @@ k1_tau_mask(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
     }
     tc_fence_before();
     __syncthreads();
+    CTA_MARK(0, 1);
     tc_fence_after();
     const uint32_t tbase = *holder;
     const int qmin_blk = s.causal ? bd.qmin[bh * s.nQB + qb] : INT_MIN;
@@ -586,6 +621,7 @@ k1_tau_mask(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
     }
     tc_fence_before();
     __syncthreads();
+    CTA_MARK(0, 2);
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tbase, 512);
@@ -631,6 +667,7 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
     constexpr int NB = 3;                     // S / P buffers in TMEM
     constexpr int TB = D * TILE * 2;
     extern __shared__ uint8_t smem_raw[];
+    CTA_MARK(1, 0);
     uint8_t* base = align1024(smem_raw, err);
     uint8_t* sQ = base;
     uint8_t* sK = base + TB;                  // S stages
@@ -677,6 +714,7 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
     }
     tc_fence_before();
     __syncthreads();
+    CTA_MARK(1, 1);
     tc_fence_after();
     const uint32_t tbase = *holder;
     constexpr uint32_t tO = 384;
@@ -789,6 +827,12 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
         const float tq = qv ? tau[qrow] : 0.0f;
         const uint32_t tl = tmem_lane_base(tbase, warp);
         float n = 0.0f;
+        constexpr bool kPacked = PINV == 1 || PINV == 2 || PINV == 4;
+        const float2 c1 = make_float2(__fmul_rn(s.am1, s.scale), __fmul_rn(s.am1, s.scale));
+        const float2 mtau = make_float2(-tq, -tq);
+        const float uhi = __fmaf_rn(s.am1, 10.0f, -tq);
+        const bool packed_row = kPacked && split && __fmaf_rn(s.am1, -10.0f, -tq) <= 0.0f;
+        float2 n2 = make_float2(0.0f, 0.0f);
         for (int j = 0; j < T; ++j) {
             const uint32_t e = sched[j];
             const int kb = (int)(e & SCHED_IDX);
@@ -797,6 +841,39 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
             mbar_wait(&s_full[b], (j / NB) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
             if (et == 0) TRACE(2, j, 0);
             tc_fence_after();
+#ifdef ASA_EXP_F_NOEPI
+            if (true) { tc_fence_before(); epi_arrive(&p_full[b]); continue; }
+#endif
+            if (kPacked && all && packed_row) {
+                // every key visible: both chunks loaded at once, packed math
+                uint32_t r[CPT][32];
+#pragma unroll
+                for (int cc = 0; cc < CPT; ++cc) tmem_ld32(tl + b * 128 + (h * CPT + cc) * 32, r[cc]);
+                tmem_ld_wait();
+#pragma unroll
+                for (int cc = 0; cc < CPT; ++cc) {
+                    const uint32_t col = tl + b * 128 + (h * CPT + cc) * 32;
+#pragma unroll
+                    for (int g = 0; g < 2; ++g) {
+                        uint32_t hi[8], lo[8];
+#pragma unroll
+                        for (int m = 0; m < 8; ++m) {
+                            const float2 pp = entmax_pair<PINV>(r[cc][16 * g + 2 * m], r[cc][16 * g + 2 * m + 1],
+                                                                c1, mtau, uhi);
+                            n2 = __fadd2_rn(n2, pp);
+                            split_pair(pp, hi[m], lo[m]);
+                        }
+                        tmem_st8(col + g * 16, hi);
+                        tmem_st8(col + g * 16 + 8, lo);
+                    }
+                }
+                if (et == 0) TRACE(2, j, 1);
+                tmem_st_wait();
+                if (et == 0) TRACE(2, j, 3);
+                tc_fence_before();
+                epi_arrive(&p_full[b]);
+                continue;
+            }
 #pragma unroll
             for (int cc = 0; cc < CPT; ++cc) {
                 const int c = h * CPT + cc;
@@ -844,6 +921,7 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
             tc_fence_before();
             epi_arrive(&p_full[b]);
         }
+        n += n2.x + n2.y;
         // row sum: the warpgroups' partial sums added in group order
         nsum[h * TILE + row] = n;
         epi_bar();
@@ -875,6 +953,7 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
     }
     tc_fence_before();
     __syncthreads();
+    CTA_MARK(1, 2);
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tbase, 512);
@@ -900,6 +979,7 @@ k4_dq(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
     constexpr int S = 2;
     constexpr int TB = D * TILE * 2;
     extern __shared__ uint8_t smem_raw[];
+    CTA_MARK(2, 0);
     uint8_t* base = align1024(smem_raw, err);
     uint8_t* sQ = base;
     uint8_t* sdO = base + TB;
@@ -950,6 +1030,7 @@ k4_dq(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
     }
     tc_fence_before();
     __syncthreads();
+    CTA_MARK(2, 1);
     tc_fence_after();
     const uint32_t tbase = *holder;
     constexpr uint32_t tS = 0, tP = 128, tQ = 256, tDh = 384, tDl = 448;
@@ -1106,6 +1187,7 @@ k4_dq(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
     }
     tc_fence_before();
     __syncthreads();
+    CTA_MARK(2, 2);
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tbase, 512);
@@ -1139,6 +1221,7 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
     constexpr int SQ = 2;                     // Q / dO stages
     constexpr int TB = D * TILE * 2;
     extern __shared__ uint8_t smem_raw[];
+    CTA_MARK(3, 0);
     uint8_t* base = align1024(smem_raw, err);
     uint8_t* sK = base;
     uint8_t* sV = base + TB;
@@ -1180,6 +1263,7 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
     if (threadIdx.x >= EPI0) sched_from_list(sched, list + e0, T, s, bd, bh, kb, true, threadIdx.x - EPI0);
     tc_fence_before();
     __syncthreads();
+    CTA_MARK(3, 1);
     tc_fence_after();
     const uint32_t tbase = *holder;
     constexpr uint32_t tS = 0, tP = 128, tV = 256, tK = 256 + D;
@@ -1369,6 +1453,7 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
     }
     tc_fence_before();
     __syncthreads();
+    CTA_MARK(3, 2);
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tbase, 512);
@@ -1627,6 +1712,13 @@ void* exp_trace_ptr_impl();
 extern "C" void* asa_exp_trace_ptr() {
     void* p = nullptr;
     cudaGetSymbolAddress(&p, asa::g_trace);
+    return p;
+}
+#endif
+#ifdef ASA_EXP_CTA
+extern "C" void* asa_exp_cta_ptr() {
+    void* p = nullptr;
+    cudaGetSymbolAddress(&p, asa::g_cta);
     return p;
 }
 #endif
