@@ -19,7 +19,10 @@ NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 FLAGS = ["-O3", "-std=c++17", "-gencode", "arch=compute_100a,code=sm_100a", "-lineinfo",
          "-Xcompiler", "-fPIC", "-Xcompiler", "-ffp-contract=off", "--expt-relaxed-constexpr",
          "-Xptxas", "-v" if os.environ.get("ASA_PTXAS_V") else "-O3"]
-SOURCES = ["asa_capi.cu", "asa_simt.cu", "asa_compact.cu", "asa_tc.cu"]
+SOURCES = ["asa_capi.cu", "asa_simt.cu", "asa_compact.cu"]
+# asa_tc.cu is compiled as four objects (τ/mask, forward, dQ, dK/dV) so the
+# template instantiations build in parallel.
+TC_PARTS = [("asa_tc.cu", part) for part in (1, 2, 3, 4)]
 
 
 def _deps():
@@ -27,12 +30,15 @@ def _deps():
         os.path.join(HERE, "..", "include", "asa.h")]
 
 
-def _compile(src):
-    obj = os.path.join(BUILD, os.path.basename(src) + ".o")
+def _compile(item):
+    src, part = item if isinstance(item, tuple) else (item, None)
+    tag = f".part{part}" if part else ""
+    obj = os.path.join(BUILD, os.path.basename(src) + tag + ".o")
     newest = max(os.path.getmtime(p) for p in _deps())
     if os.path.exists(obj) and os.path.getmtime(obj) >= newest:
         return obj
-    cmd = [NVCC] + FLAGS + ["-c", os.path.join(CSRC, src), "-o", obj + ".tmp"]
+    defs = [f"-DASA_TC_PART={part}"] if part else []
+    cmd = [NVCC] + FLAGS + defs + ["-c", os.path.join(CSRC, src), "-o", obj + ".tmp"]
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
         raise RuntimeError(f"nvcc failed for {src}:\n{r.stdout}\n{r.stderr}")
@@ -47,8 +53,9 @@ def build(force: bool = False) -> str:
     if force:
         for f in os.listdir(BUILD):
             os.remove(os.path.join(BUILD, f))
-    with cf.ThreadPoolExecutor(len(SOURCES)) as ex:
-        objs = list(ex.map(_compile, SOURCES))
+    items = SOURCES + TC_PARTS
+    with cf.ThreadPoolExecutor(len(items)) as ex:
+        objs = list(ex.map(_compile, items))
     if (not force and os.path.exists(LIB)
             and os.path.getmtime(LIB) >= max(os.path.getmtime(o) for o in objs)):
         return LIB

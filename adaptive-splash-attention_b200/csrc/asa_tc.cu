@@ -32,6 +32,14 @@
 #include <type_traits>
 
 namespace asa {
+
+struct Bounds {
+    const int* qmin;   // [BH][nQB]
+    const int* qmax;
+    const int* kmin;   // [BH][nKB]
+    const int* kmax;
+};
+
 namespace {
 
 using namespace sm100;
@@ -48,12 +56,6 @@ constexpr int NEPI = 128 * NWG;            // epilogue threads
 constexpr int NTHREADS = 64 + NEPI;        // + producer warp + MMA warp
 constexpr int EPI0 = 64;                   // first epilogue thread
 
-struct Bounds {
-    const int* qmin;   // [BH][nQB]
-    const int* qmax;
-    const int* kmin;   // [BH][nKB]
-    const int* kmax;
-};
 
 // Dynamic shared memory starts at the bottom of the CTA's window (these
 // kernels declare no static __shared__ data), which is 1024-byte aligned as
@@ -1556,6 +1558,12 @@ bool is_sm100() {
 
 }  // namespace
 
+#ifndef ASA_TC_PART
+#define ASA_TC_PART 0   // 0: everything; 1: τ/mask + sizing, 2: forward, 3: backward prologue + dQ, 4: dK/dV
+#endif
+#define ASA_PART(n) (ASA_TC_PART == 0 || ASA_TC_PART == (n))
+
+#if ASA_PART(1)
 bool tc_supported(const Shape& s) {
     return s.in_dtype == ASA_DTYPE_BF16 && (s.d == 64 || s.d == 128) && s.BM == TILE && s.BN == TILE &&
            s.NK > 0 && s.nKB <= 32768 && is_sm100();
@@ -1565,6 +1573,8 @@ size_t tc_fwd_workspace(const Shape& s) { return bounds_ints(s) * 4; }
 size_t tc_bwd_workspace(const Shape& s) {
     return ((bounds_ints(s) * 4 + 15) & ~size_t(15)) + (size_t)2 * s.BH * s.NQ * 4;
 }
+
+#endif  // part 1
 
 // Exponent classes the kernels are specialised for: (1/(α-1), (2-α)/(α-1))
 // kinds (2,1) for α=1.5, (1,5) for α=2, (4,3) for α=1.25; anything else runs
@@ -1590,6 +1600,7 @@ cudaError_t with_dtype_d(const Shape& s, F&& f) {
     return f(std::integral_constant<int, 64>{}, (bf*)nullptr);
 }
 
+#if ASA_PART(1)
 cudaError_t tc_tau_mask(const Shape& s, const void* Q, const void* K, const int32_t* Qidx,
                         const int32_t* Kidx, float* tau, uint8_t* M, void* ws, int* err,
                         cudaStream_t st) {
@@ -1622,6 +1633,9 @@ cudaError_t tc_tau_mask(const Shape& s, const void* Q, const void* K, const int3
     return go(k1_tau_mask<64, 32, TP>, 64, 32);
 }
 
+#endif  // part 1
+
+#if ASA_PART(2)
 cudaError_t tc_forward(const Shape& s, const void* Q, const void* K, const void* V, const int32_t* Qidx,
                        const int32_t* Kidx, const float* tau, const int32_t* ptr, const int32_t* idx,
                        void* O, float* O32, float* rownorm, void* ws, int* err, cudaStream_t st) {
@@ -1648,60 +1662,105 @@ cudaError_t tc_forward(const Shape& s, const void* Q, const void* K, const void*
     });
 }
 
-cudaError_t tc_backward(const Shape& s, const void* Q, const void* K, const void* V, const int32_t* Qidx,
-                        const int32_t* Kidx, const float* O32, const float* tau, const int32_t* ptr,
-                        const int32_t* idx, const int32_t* cptr, const int32_t* cidx,
-                        const float* rownorm, const void* dO, void* dQ, void* dK, void* dV, void* ws,
-                        int* err, cudaStream_t st, int stages) {
-    Bounds bd = bounds_at(s, ws);
-    float* Dq = (float*)((char*)ws + ((bounds_ints(s) * 4 + 15) & ~size_t(15)));
-    const size_t rows = (size_t)s.BH * s.NQ;
-    float* invNv = Dq + rows;
-    cudaError_t e = cudaSuccess;
-    if (stages & 1) {
-    e = launch_bounds(s, Qidx, Kidx, ws, st);
-    if (e != cudaSuccess) return e;
-    if (s.d == 128)
-        k4_pre<128><<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(O32, (const __nv_bfloat16*)dO, rownorm, Dq, invNv, rows);
-    else
-        k4_pre<64><<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(O32, (const __nv_bfloat16*)dO, rownorm, Dq, invNv, rows);
-    note_launch();
-    e = cudaGetLastError();
-    if (e != cudaSuccess) return e;
-    }
-    if (!(stages & 6)) return cudaSuccess;
+#endif  // part 2
+
+// Backward launch arguments shared by the dQ and dK/dV launchers.
+struct BwdArgs {
     CUtensorMap mQ, mK, mV, mdO;
-    if (!make_map(&mQ, Q, s.BH, s.NQ, s.d) || !make_map(&mK, K, s.BH, s.NK, s.d) ||
-        !make_map(&mV, V, s.BH, s.NK, s.d) || !make_map(&mdO, dO, s.BH, s.NQ, s.d))
-        return cudaErrorInvalidValue;
+    Bounds bd;
+    const int32_t *Qidx, *Kidx, *ptr, *idx, *cptr, *cidx;
+    const float *tau, *invNv, *Dq;
+    void *dQ, *dK, *dV;
+    int* err;
+};
+
+template <typename TO>
+size_t bwd_smem(const Shape& s, int D) {
+    return (size_t)D * TILE * 2 * 6 + kSmemTailBwd + (size_t)(s.nKB > s.nQB ? s.nKB : s.nQB) * 4;
+}
+
+cudaError_t tc_launch_dq(const Shape& s, const BwdArgs& a, cudaStream_t st);
+cudaError_t tc_launch_dkdv(const Shape& s, const BwdArgs& a, cudaStream_t st);
+
+#if ASA_PART(3)
+cudaError_t tc_launch_dq(const Shape& s, const BwdArgs& a, cudaStream_t st) {
     const int split = s.split;
     return with_dtype_d(s, [&](auto dtag, auto* out) -> cudaError_t {
         constexpr int D = decltype(dtag)::value;
         using TO = std::remove_pointer_t<decltype(out)>;
         return with_alpha(s, [&](auto ac) -> cudaError_t {
             auto kdq = k4_dq<D, TO, decltype(ac)::pe2>;
-            auto kkv = k4_dkdv<D, TO, decltype(ac)::pinv, decltype(ac)::pe2>;
-            const size_t smem = (size_t)D * TILE * 2 * 6 + kSmemTailBwd +
-                                (size_t)(s.nKB > s.nQB ? s.nKB : s.nQB) * 4;
+            const size_t smem = bwd_smem<TO>(s, D);
             cudaError_t r = prep(kdq, smem);
-            if (r == cudaSuccess) r = prep(kkv, smem);
             if (r != cudaSuccess) return r;
-            if (stages & 2) {
-                kdq<<<dim3(s.nQB, s.BH), NTHREADS, smem, st>>>(mQ, mK, mV, mdO, s, Qidx, Kidx, bd, tau,
-                                                              invNv, Dq, ptr, idx, (TO*)dQ, split, err);
-                note_launch();
-                r = cudaGetLastError();
-                if (r != cudaSuccess) return r;
-            }
-            if (!(stages & 4)) return cudaSuccess;
-            kkv<<<dim3(s.nKB, s.BH), NTHREADS, smem, st>>>(mQ, mK, mV, mdO, s, Qidx, Kidx, bd, tau,
-                                                          invNv, Dq, cptr, cidx, (TO*)dK, (TO*)dV,
-                                                          split, err);
+            kdq<<<dim3(s.nQB, s.BH), NTHREADS, smem, st>>>(a.mQ, a.mK, a.mV, a.mdO, s, a.Qidx, a.Kidx, a.bd,
+                                                          a.tau, a.invNv, a.Dq, a.ptr, a.idx, (TO*)a.dQ,
+                                                          split, a.err);
             note_launch();
             return cudaGetLastError();
         });
     });
 }
+
+cudaError_t tc_backward(const Shape& s, const void* Q, const void* K, const void* V, const int32_t* Qidx,
+                        const int32_t* Kidx, const float* O32, const float* tau, const int32_t* ptr,
+                        const int32_t* idx, const int32_t* cptr, const int32_t* cidx,
+                        const float* rownorm, const void* dO, void* dQ, void* dK, void* dV, void* ws,
+                        int* err, cudaStream_t st, int stages) {
+    BwdArgs a;
+    a.bd = bounds_at(s, ws);
+    float* Dq = (float*)((char*)ws + ((bounds_ints(s) * 4 + 15) & ~size_t(15)));
+    const size_t rows = (size_t)s.BH * s.NQ;
+    float* invNv = Dq + rows;
+    cudaError_t e = cudaSuccess;
+    if (stages & 1) {
+        e = launch_bounds(s, Qidx, Kidx, ws, st);
+        if (e != cudaSuccess) return e;
+        if (s.d == 128)
+            k4_pre<128><<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(O32, (const __nv_bfloat16*)dO, rownorm, Dq,
+                                                                     invNv, rows);
+        else
+            k4_pre<64><<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(O32, (const __nv_bfloat16*)dO, rownorm, Dq,
+                                                                    invNv, rows);
+        note_launch();
+        e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+    }
+    if (!(stages & 6)) return cudaSuccess;
+    if (!make_map(&a.mQ, Q, s.BH, s.NQ, s.d) || !make_map(&a.mK, K, s.BH, s.NK, s.d) ||
+        !make_map(&a.mV, V, s.BH, s.NK, s.d) || !make_map(&a.mdO, dO, s.BH, s.NQ, s.d))
+        return cudaErrorInvalidValue;
+    a.Qidx = Qidx; a.Kidx = Kidx; a.ptr = ptr; a.idx = idx; a.cptr = cptr; a.cidx = cidx;
+    a.tau = tau; a.invNv = invNv; a.Dq = Dq; a.dQ = dQ; a.dK = dK; a.dV = dV; a.err = err;
+    if (stages & 2) {
+        e = tc_launch_dq(s, a, st);
+        if (e != cudaSuccess) return e;
+    }
+    if (stages & 4) e = tc_launch_dkdv(s, a, st);
+    return e;
+}
+#endif  // part 3
+
+#if ASA_PART(4)
+cudaError_t tc_launch_dkdv(const Shape& s, const BwdArgs& a, cudaStream_t st) {
+    const int split = s.split;
+    return with_dtype_d(s, [&](auto dtag, auto* out) -> cudaError_t {
+        constexpr int D = decltype(dtag)::value;
+        using TO = std::remove_pointer_t<decltype(out)>;
+        return with_alpha(s, [&](auto ac) -> cudaError_t {
+            auto kkv = k4_dkdv<D, TO, decltype(ac)::pinv, decltype(ac)::pe2>;
+            const size_t smem = bwd_smem<TO>(s, D);
+            cudaError_t r = prep(kkv, smem);
+            if (r != cudaSuccess) return r;
+            kkv<<<dim3(s.nKB, s.BH), NTHREADS, smem, st>>>(a.mQ, a.mK, a.mV, a.mdO, s, a.Qidx, a.Kidx, a.bd,
+                                                          a.tau, a.invNv, a.Dq, a.cptr, a.cidx, (TO*)a.dK,
+                                                          (TO*)a.dV, split, a.err);
+            note_launch();
+            return cudaGetLastError();
+        });
+    });
+}
+#endif  // part 4
 
 }  // namespace asa
 
