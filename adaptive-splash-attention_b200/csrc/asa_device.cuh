@@ -72,6 +72,19 @@ __device__ __forceinline__ float pow_exact(float x, PowSpec s) {
     }
 }
 
+// pow_exact with the exponent class fixed at compile time (same arithmetic
+// per kind; KIND 0 classifies the runtime exponent as pow_exact does).
+template <int KIND>
+__device__ __forceinline__ float pow_exact_k(float x, float e) {
+    if constexpr (KIND == 1) return x;
+    else if constexpr (KIND == 2) return __fmul_rn(x, x);
+    else if constexpr (KIND == 3) { double x2 = (double)x * (double)x; return (float)(x2 * (double)x); }
+    else if constexpr (KIND == 4) { double x2 = (double)x * (double)x; return (float)(x2 * x2); }
+    else if constexpr (KIND == 5) return 1.0f;
+    else if constexpr (KIND == 6) return __fdiv_rn(1.0f, x);
+    else return pow_exact(x, make_pow(e));
+}
+
 // Reference entmax p for one score (:311-316): u = (α-1)s - τ;
 // p = u > 0 ? max(u, EPS)^{1/(α-1)} : 0; non-finite -> 0.
 __device__ __forceinline__ float entmax_p(float s, float am1, float tau, PowSpec pinv, float* u_out) {
@@ -134,17 +147,20 @@ struct TopK {
 // slots [KM-k, KM) of a TopK list.  At most five Halley steps with the
 // reference's bracket, early exit |f| < 1e-4, bisection fallback, per-step
 // clamp and second-derivative coefficient inv·(inv+1-α) (:85).
-template <int KM>
-__device__ float ref_tau(const float (&s)[KM], int k, float alpha_in) {
+template <int KM, int K1, int K2, int K3>
+__device__ __forceinline__ float ref_tau_k(const float (&s)[KM], int k, float alpha_in) {
     const float alpha = fmaxf(1.05f, fminf(alpha_in, 3.0f));
     const float am1 = __fadd_rn(alpha, -1.0f);
     const float inv = __fdiv_rn(1.0f, am1);
     const float e2 = __fmul_rn(__fadd_rn(2.0f, -alpha), inv);
     const float e3 = __fmul_rn(__fadd_rn(3.0f, -__fmul_rn(2.0f, alpha)), inv);
     const float c2 = __fmul_rn(inv, __fadd_rn(__fadd_rn(inv, 1.0f), -alpha));
-    const PowSpec P1 = make_pow(inv), P2 = make_pow(e2), P3 = make_pow(e3);
     const int first = KM - k;
-    const float s_max = s[first], s_min = s[KM - 1];
+    float s_max = s[KM - 1];
+#pragma unroll
+    for (int j = 0; j < KM; ++j)
+        if (j == first) s_max = s[j];   // unrolled select: no dynamically indexed (local) array
+    const float s_min = s[KM - 1];
     float lo = __fmaf_rn(am1, s_min, -2.0f);
     float hi = __fmaf_rn(am1, s_max, 2.0f);
     float tau = __fmul_rn(0.5f, __fadd_rn(lo, hi));
@@ -158,12 +174,12 @@ __device__ float ref_tau(const float (&s)[KM], int k, float alpha_in) {
             alive = alive && (u > 0.0f);   // the reference breaks at the first u <= 0
             if (alive) {
                 float uc = fmaxf(u, ASA_EPS);
-                float up = pow_exact(uc, P1);
+                float up = pow_exact_k<K1>(uc, inv);
                 if (!isfinite(up)) up = 0.0f;
                 f = __fadd_rn(f, up);
-                float dt = __fmul_rn(-inv, pow_exact(uc, P2));
+                float dt = __fmul_rn(-inv, pow_exact_k<K2>(uc, e2));
                 if (isfinite(dt)) fp = __fadd_rn(fp, dt);
-                float st = __fmul_rn(c2, pow_exact(uc, P3));
+                float st = __fmul_rn(c2, pow_exact_k<K3>(uc, e3));
                 if (isfinite(st)) fpp = __fadd_rn(fpp, st);
             }
         }
@@ -183,7 +199,7 @@ __device__ float ref_tau(const float (&s)[KM], int k, float alpha_in) {
             float u = __fmaf_rn(am1, s[j], -tn);
             alive = alive && (u > 0.0f);
             if (alive) {
-                float up = pow_exact(fmaxf(u, ASA_EPS), P1);
+                float up = pow_exact_k<K1>(fmaxf(u, ASA_EPS), inv);
                 if (isfinite(up)) f = __fadd_rn(f, up);
             }
         }
@@ -193,6 +209,25 @@ __device__ float ref_tau(const float (&s)[KM], int k, float alpha_in) {
         tau = fminf(tau, __fmaf_rn(s_max, am1, 10.0f));
     }
     return tau;
+}
+
+
+// Runtime dispatch over the exponent classes of α = 1.5, 2 and 1.25 (whose
+// τ-solve exponents are all exact small powers); other α take the powf
+// instantiation.  Compile-time classes keep the solve branch-free per
+// element: a runtime switch per pow costs ~3x the whole solve.
+template <int KM>
+__device__ float ref_tau(const float (&s)[KM], int k, float alpha_in) {
+    const float alpha = fmaxf(1.05f, fminf(alpha_in, 3.0f));
+    const float am1 = __fadd_rn(alpha, -1.0f);
+    const float inv = __fdiv_rn(1.0f, am1);
+    const int k1 = make_pow(inv).kind;
+    const int k2 = make_pow(__fmul_rn(__fadd_rn(2.0f, -alpha), inv)).kind;
+    const int k3 = make_pow(__fmul_rn(__fadd_rn(3.0f, -__fmul_rn(2.0f, alpha)), inv)).kind;
+    if (k1 == 2 && k2 == 1 && k3 == 5) return ref_tau_k<KM, 2, 1, 5>(s, k, alpha_in);   // α = 1.5
+    if (k1 == 1 && k2 == 5 && k3 == 6) return ref_tau_k<KM, 1, 5, 6>(s, k, alpha_in);   // α = 2
+    if (k1 == 4 && k2 == 3 && k3 == 2) return ref_tau_k<KM, 4, 3, 2>(s, k, alpha_in);   // α = 1.25
+    return ref_tau_k<KM, 0, 0, 0>(s, k, alpha_in);
 }
 
 // Record an error code in the device error word (first error wins).  The

@@ -92,25 +92,32 @@ __device__ __forceinline__ bool vis_all(const Shape& s, const Bounds& b, int bh,
     return b.kmax[bh * s.nKB + kb] <= b.qmin[bh * s.nQB + qb];
 }
 __device__ __forceinline__ bool needs_fix(const Shape& s, const Bounds& b, int bh, int qb, int kb) {
-    if (!s.ref_load) return false;
+    if (!s.ref_load || !s.causal) return false;   // bounds exist only for causal shapes
     return b.kmax[bh * s.nKB + kb] > b.qmin[bh * s.nQB + qb];
 }
 
 #ifdef ASA_EXP_TRACE
 __device__ unsigned long long g_trace[8][64][8];
+__device__ unsigned long long g_cnt[8];
 #define TRACE(role, j, ev) do { if (blockIdx.x == 0 && blockIdx.y == 0 && (j) < 64) g_trace[role][j][ev] = clock64(); } while (0)
 #else
 #define TRACE(role, j, ev) do {} while (0)
 #endif
 #ifdef ASA_EXP_CTA
-__device__ unsigned long long g_cta[4][4096][4];
+__device__ unsigned long long g_cta[4][4096][16];
 __device__ __forceinline__ unsigned long long gtimer() {
     unsigned long long t; asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t)); return t;
 }
 #define CTA_MARK(k, ev) do { if (threadIdx.x == 0) { const int c_ = blockIdx.y * gridDim.x + blockIdx.x; \
-    if (c_ < 4096) { g_cta[k][c_][ev] = gtimer(); if ((ev) == 0) { unsigned sm_; asm("mov.u32 %0, %smid;" : "=r"(sm_)); g_cta[k][c_][3] = sm_; } } } } while (0)
+    if (c_ < 4096) { g_cta[k][c_][ev] = gtimer(); if ((ev) == 0) { unsigned sm_; asm("mov.u32 %0, %smid;" : "=r"(sm_)); g_cta[k][c_][15] = sm_; } } } } while (0)
+#define CTA_MARK_T(k, ev) do { const int c_ = blockIdx.y * gridDim.x + blockIdx.x; \
+    if (c_ < 4096) g_cta[k][c_][ev] = gtimer(); } while (0)
+#define g_cta_n(k, n) do { const int c_ = blockIdx.y * gridDim.x + blockIdx.x; \
+    if (c_ < 4096) g_cta[k][c_][14] = (n); } while (0)
 #else
 #define CTA_MARK(k, ev) do {} while (0)
+#define CTA_MARK_T(k, ev) do {} while (0)
+#define g_cta_n(k, n) do {} while (0)
 #endif
 
 // ---- per-CTA tile schedule ----------------------------------------------------
@@ -171,33 +178,67 @@ __device__ int sched_visible(uint32_t* sched, int* warp_cnt, const Shape& s, con
 // see the key.  qidx_blk holds that block's 128 positions (INT_MAX past NQ,
 // which keeps the element, see ref_keep).  Executed by one full warp.
 template <int D>
+__device__ __forceinline__ uint4* fix_chunk(uint8_t* tile, int r, int t0) {
+    const int phys = ((t0 % BOX) / 8) ^ (r & 7);
+    return reinterpret_cast<uint4*>(tile + (t0 / BOX) * BOX_BYTES + r * 128 + phys * 16);
+}
+
+// Zero the elements of one 16-byte chunk whose bit in `keep` is clear.
+__device__ __forceinline__ void fix_apply(uint4* p, uint32_t keep) {
+    uint4 v = *p;
+    uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int e = 0; e < 8; ++e)
+        if (!((keep >> e) & 1u)) w[e >> 1] &= (e & 1) ? 0x0000ffffu : 0xffff0000u;
+    *p = make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+template <int D>
 __device__ void fix_tile(uint8_t* tile, const int* qidx_blk, int qmin_blk,
                          const int32_t* __restrict__ Kidx_bh, int kb, int NK, int lane) {
-    for (int r = lane; r < TILE; r += 32) {
-        const int kn = kb * TILE + r;
-        if (kn >= NK) continue;
-        const int kpos = Kidx_bh[kn];
-        if (kpos <= qmin_blk) continue;
-#pragma unroll 1
-        for (int ch = 0; ch < D / 8; ++ch) {
-            const int t0 = ch * 8;
-            // the 8 staging queries of this 16-byte chunk are consecutive
-            const int4* qp = reinterpret_cast<const int4*>(qidx_blk + ((r * D + t0) & (TILE - 1)));
-            const int4 qa = qp[0], qc = qp[1];
-            const uint32_t keep = (kpos <= qa.x ? 1u : 0u) | (kpos <= qa.y ? 2u : 0u) |
-                                  (kpos <= qa.z ? 4u : 0u) | (kpos <= qa.w ? 8u : 0u) |
-                                  (kpos <= qc.x ? 16u : 0u) | (kpos <= qc.y ? 32u : 0u) |
-                                  (kpos <= qc.z ? 64u : 0u) | (kpos <= qc.w ? 128u : 0u);
-            if (keep == 0xffu) continue;
-            const int box = t0 / BOX;
-            const int phys = ((t0 % BOX) / 8) ^ (r & 7);
-            uint4* p = reinterpret_cast<uint4*>(tile + box * BOX_BYTES + r * 128 + phys * 16);
-            uint4 v = *p;
-            uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    static_assert(D == 64 || D == 128, "staging windows assume D in {64, 128}");
+    int kp[TILE / 32];
 #pragma unroll
-            for (int e = 0; e < 8; ++e)
-                if (!((keep >> e) & 1u)) w[e >> 1] &= (e & 1) ? 0x0000ffffu : 0xffff0000u;
-            *p = make_uint4(w[0], w[1], w[2], w[3]);
+    for (int rr = 0; rr < TILE / 32; ++rr) {     // independent loads: one latency for all rows
+        const int kn = kb * TILE + lane + 32 * rr;
+        kp[rr] = kn < NK ? __ldg(Kidx_bh + kn) : INT_MIN;
+    }
+    // Row r's staging queries for dims 0..D-1 are the contiguous window
+    // [(r*D) % 128, (r*D) % 128 + D).  When the block's positions are
+    // nondecreasing (the usual arange case) the zeroed dims of a row are a
+    // prefix [0, n) with n = #{t : qidx[window + t] < kpos}: a branch-free
+    // binary search, then whole-chunk zero stores.
+    const int4 q4 = reinterpret_cast<const int4*>(qidx_blk)[lane];
+    const int qnext = lane < 31 ? qidx_blk[4 * lane + 4] : INT_MAX;
+    const bool mono = __all_sync(0xffffffffu, q4.x <= q4.y && q4.y <= q4.z && q4.z <= q4.w && q4.w <= qnext);
+#pragma unroll
+    for (int rr = 0; rr < TILE / 32; ++rr) {
+        const int r = lane + 32 * rr;
+        const int kpos = kp[rr];
+        if (kpos <= qmin_blk) continue;          // every staging query sees the key
+        const int base = (r * D) & (TILE - 1);
+        if (mono) {
+            int n = 0;
+#pragma unroll
+            for (int step = D / 2; step >= 1; step >>= 1)
+                if (qidx_blk[base + n + step - 1] < kpos) n += step;
+#pragma unroll
+            for (int ch = 0; ch < D / 8; ++ch) {
+                if ((ch + 1) * 8 <= n) *fix_chunk<D>(tile, r, ch * 8) = make_uint4(0u, 0u, 0u, 0u);
+                else if (ch * 8 < n) fix_apply(fix_chunk<D>(tile, r, ch * 8), 0xffu << (n - ch * 8));
+            }
+        } else {
+#pragma unroll 2
+            for (int ch = 0; ch < D / 8; ++ch) {
+                // the 8 staging queries of this 16-byte chunk are consecutive
+                const int4* qp = reinterpret_cast<const int4*>(qidx_blk + base + ch * 8);
+                const int4 qa = qp[0], qc = qp[1];
+                const uint32_t keep = (kpos <= qa.x ? 1u : 0u) | (kpos <= qa.y ? 2u : 0u) |
+                                      (kpos <= qa.z ? 4u : 0u) | (kpos <= qa.w ? 8u : 0u) |
+                                      (kpos <= qc.x ? 16u : 0u) | (kpos <= qc.y ? 32u : 0u) |
+                                      (kpos <= qc.z ? 64u : 0u) | (kpos <= qc.w ? 128u : 0u);
+                if (keep != 0xffu) fix_apply(fix_chunk<D>(tile, r, ch * 8), keep);
+            }
         }
     }
 }
@@ -267,19 +308,6 @@ __device__ __forceinline__ void split_pack(const float (&x)[32], uint32_t (&hi)[
     }
 }
 
-// v[i] for a runtime i in [0, 32) without local memory: a 5-level select tree.
-__device__ __forceinline__ float pick32(const float (&v)[32], int i) {
-    float a[16], b[8], c[4], d[2];
-#pragma unroll
-    for (int k = 0; k < 16; ++k) a[k] = (i & 1) ? v[2 * k + 1] : v[2 * k];
-#pragma unroll
-    for (int k = 0; k < 8; ++k) b[k] = (i & 2) ? a[2 * k + 1] : a[2 * k];
-#pragma unroll
-    for (int k = 0; k < 4; ++k) c[k] = (i & 4) ? b[2 * k + 1] : b[2 * k];
-#pragma unroll
-    for (int k = 0; k < 2; ++k) d[k] = (i & 8) ? c[2 * k + 1] : c[2 * k];
-    return (i & 16) ? d[1] : d[0];
-}
 
 // x^e with the exponent class fixed at compile time (PK = PowSpec kind:
 // 1 x, 2 x^2, 3 x^3, 4 x^4, 5 one, 0 powf with runtime e).
@@ -310,26 +338,31 @@ __device__ __forceinline__ float grad_pk(float u, float e, float dP, float Dq, f
     return isfinite(g) ? g : 0.0f;
 }
 
-// Positions of keys kn0 .. kn0+31 (INT_MAX past NK, INT_MIN when every key
-// is visible).  L1-cached loads; only partially visible tiles need them.
-__device__ __forceinline__ void load_kpos32(const int32_t* __restrict__ Kidx_bh, int kn0, int NK,
-                                            int causal, int (&kp)[32]) {
-    if (!causal) {
-#pragma unroll
-        for (int i = 0; i < 32; ++i) kp[i] = kn0 + i < NK ? INT_MIN : INT_MAX;
-        return;
-    }
-    if (kn0 + 32 <= NK && ((reinterpret_cast<uintptr_t>(Kidx_bh + kn0) & 15) == 0)) {
+// Visibility of keys kn0 .. kn0+31 to a query at position qpos, bit i for
+// key kn0+i: the key exists (< NK) and, when causal, K_idx <= qpos.
+// L1-cached position loads; only partially visible tiles need them.
+__device__ __forceinline__ uint32_t vis_mask32(const int32_t* __restrict__ Kidx_bh, int kn0, int NK,
+                                               int causal, int qpos) {
+    const int nv = NK - kn0;
+    const uint32_t exist = nv >= 32 ? 0xffffffffu : (nv <= 0 ? 0u : ((1u << nv) - 1u));
+    if (!causal) return exist;
+    uint32_t vis = 0;
+    if (nv >= 32 && ((reinterpret_cast<uintptr_t>(Kidx_bh + kn0) & 15) == 0)) {
         const int4* p = reinterpret_cast<const int4*>(Kidx_bh + kn0);
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
             const int4 v = __ldg(p + i);
-            kp[4 * i] = v.x; kp[4 * i + 1] = v.y; kp[4 * i + 2] = v.z; kp[4 * i + 3] = v.w;
+            vis |= (v.x <= qpos ? 1u : 0u) << (4 * i);
+            vis |= (v.y <= qpos ? 1u : 0u) << (4 * i + 1);
+            vis |= (v.z <= qpos ? 1u : 0u) << (4 * i + 2);
+            vis |= (v.w <= qpos ? 1u : 0u) << (4 * i + 3);
         }
-    } else {
-#pragma unroll
-        for (int i = 0; i < 32; ++i) kp[i] = kn0 + i < NK ? __ldg(Kidx_bh + kn0 + i) : INT_MAX;
+        return vis;
     }
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+        if (i < nv && __ldg(Kidx_bh + kn0 + i) <= qpos) vis |= 1u << i;
+    return vis;
 }
 
 __device__ __forceinline__ uint32_t tmem_lane_base(uint32_t tbase, int warp) {
@@ -375,33 +408,77 @@ __global__ void tc_bounds_kernel(Shape s, const int32_t* __restrict__ Qidx,
 // ===========================================================================
 // K1: τ and block mask
 // ===========================================================================
-// Two passes over the row's visible tiles (S = Q·K^T recomputed in TMEM for
-// each).  Pass A keeps, per thread, the k largest 32-column chunk maxima;
-// the k-th of them, t0, is a lower bound for the row half's k-th largest
-// score because those maxima are k distinct scores.  Pass B streams the
-// scores in key order and inserts only those >= t0 with the reference's
-// strict '>' rule, which yields exactly the list full insertion would.
-// The two epilogue warpgroups split every tile by columns (warpgroup h owns
-// keys [64h, 64h+64)) and keep one partial list per row; warpgroup 0 merges
-// them under (score desc, key asc) -- the order sequential insertion
-// produces -- and solves τ.
-template <int D, int KM, bool TWO_PASS>
-__global__ void __launch_bounds__(NTHREADS, 1)
+// 64-bit key ordered like (value desc, key index asc) as unsigned integers:
+// high word = the float's bits mapped to an increasing unsigned order, low
+// word = the complement of key + 2 (keys >= -2: -2 phantom, -1 seed).
+__device__ __forceinline__ unsigned long long order_key(float v, int key) {
+    const uint32_t b = __float_as_uint(v);
+    const uint32_t hi = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+    return ((unsigned long long)hi << 32) | (uint32_t)(0xffffffffu - (uint32_t)(key + 2));
+}
+
+__device__ __forceinline__ float order_value(unsigned long long e) {
+    const uint32_t hi = (uint32_t)(e >> 32);
+    return __uint_as_float((hi & 0x80000000u) ? (hi & 0x7fffffffu) : ~hi);
+}
+__device__ __forceinline__ int order_index(unsigned long long e) {
+    return (int)(0xffffffffu - (uint32_t)e) - 2;
+}
+
+// τ from each row's top-k scores (k1_tau_mask writes them in order, [rows][k]):
+// one thread per row, so the five-step solve runs at full occupancy instead
+// of in the mask kernel's tail.
+template <int KM>
+__global__ void __launch_bounds__(128)
+k1_tau_solve(const float* __restrict__ topv, float* __restrict__ tau, size_t rows, int k, float alpha) {
+    const size_t r = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= rows) return;
+    float v[KM];
+#pragma unroll
+    for (int i = 0; i < KM; ++i) {
+        const int j = i - (KM - k);
+        v[i] = j >= 0 ? topv[r * k + j] : __int_as_float(0x7f800000);
+    }
+    tau[r] = ref_tau<KM>(v, k, alpha);
+}
+
+// One pass over the row's visible tiles in ascending key-block order.  NW
+// epilogue warpgroups split every tile by columns (warpgroup h owns keys
+// [128h/NW, 128(h+1)/NW)) and keep one partial top-k list per row; the lists
+// are merged pairwise under (score desc, key asc) -- the order sequential
+// insertion produces -- and warpgroup 0 solves τ.
+//
+// Filter.  A score can only enter the row's final list if it is >= lim, the
+// largest of the partial lists' k-th values (each is a lower bound of the
+// row's k-th largest; the lists publish them in shared memory after every
+// tile).  lim is turned into a raw-dot bound rlo once per chunk
+// (clamp(x·scale) is monotone for scale > 0; rlo sits a relative 2^-20 below
+// lim/scale, so rounding can only let extra scores through), and rlo - x is
+// formed with packed fp32x2 FMAs whose sign bits are funnel-shifted into a
+// 32-bit candidate mask.  Candidates are read back from a per-thread
+// shared-memory copy of the chunk, re-scored exactly and inserted with the
+// reference's strict '>' rule, so the lists are those full insertion gives.
+// On the first tile, before any list holds k scores, lim is seeded with the
+// smallest of KM group maxima of the chunk (KM distinct scores of this row).
+template <int D, int KM, int NW>
+__global__ void __launch_bounds__(64 + 128 * NW, 1)
 k1_tau_mask(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK, Shape s,
             const int32_t* __restrict__ Qidx, const int32_t* __restrict__ Kidx, Bounds bd,
-            float* __restrict__ tau, uint8_t* __restrict__ M, int* err) {
-    constexpr int S = 4;                      // K stages
+            float* __restrict__ topv, uint8_t* __restrict__ M, int* err) {
+    constexpr int NE = 128 * NW;              // epilogue threads
+    constexpr int CP = 4 / NW;                // 32-column chunks per thread per tile
+    constexpr int S = 3;                      // K stages
     constexpr int NB = 4;                     // S buffers in TMEM (128 columns each)
-    constexpr int NPASS = TWO_PASS ? 2 : 1;
     constexpr int TB = D * TILE * 2;
+    constexpr int GSZ = TILE / KM;            // seed group size: KM groups per tile row
     extern __shared__ uint8_t smem_raw[];
-    CTA_MARK(0, 0);
     uint8_t* base = align1024(smem_raw, err);
     uint8_t* sQ = base;
     uint8_t* sK = base + TB;
-    float* topv_s = reinterpret_cast<float*>(sK + S * TB);     // [128][KM] warpgroup 1's lists
-    int* topi_s = reinterpret_cast<int*>(topv_s + TILE * KM);
-    uint64_t* bars = reinterpret_cast<uint64_t*>(topi_s + TILE * KM);
+    float4* cbuf = reinterpret_cast<float4*>(sK + S * TB);              // [NE][CP][8] chunk copies
+    float* thr_s = reinterpret_cast<float*>(cbuf + NE * CP * 8);        // [3][NW][128] published bounds
+    float* seed_s = thr_s + 3 * NW * TILE;                              // [NW][128] seed bounds
+    uint64_t* bars = reinterpret_cast<uint64_t*>(seed_s + NW * TILE);
     uint64_t* q_full = bars;
     uint64_t* k_full = bars + 1;
     uint64_t* k_empty = bars + 1 + S;
@@ -409,63 +486,45 @@ k1_tau_mask(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
     uint64_t* s_free = s_full + NB;           // [NB]
     uint32_t* holder = reinterpret_cast<uint32_t*>(bars + 24);
     int* qidx_blk = reinterpret_cast<int*>(holder + 4);      // [128]
-    int* misc = qidx_blk + TILE;                             // [8] warp counts, [8] tile count
+    int* misc = qidx_blk + TILE;                             // [8] warp counts, tile count, fix run
     uint32_t* sched = reinterpret_cast<uint32_t*>(misc + 16);   // [nKB]
     uint8_t* flags = reinterpret_cast<uint8_t*>(sched + s.nKB);
+    // merge staging (after the tile loop, over the K stages): [NW][KM][128] ordered keys
+    unsigned long long* lists = reinterpret_cast<unsigned long long*>(sK);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int bh = blockIdx.y;
     const int qb = s.causal ? (int)(gridDim.x - 1 - blockIdx.x) : (int)blockIdx.x;
     const int32_t* Kidx_bh = Kidx + (size_t)bh * s.NK;
+    CTA_MARK(0, 0);
 
     if (threadIdx.x == 0) {
         mbar_init(q_full, 1);
         for (int i = 0; i < S; ++i) { mbar_init(&k_full[i], 1); mbar_init(&k_empty[i], 1); }
-        for (int i = 0; i < NB; ++i) { mbar_init(&s_full[i], 1); mbar_init(&s_free[i], EPI_WARPS); }
+        for (int i = 0; i < NB; ++i) { mbar_init(&s_full[i], 1); mbar_init(&s_free[i], NE / 32); }
         fence_barrier_init();
     }
-#ifdef ASA_EXP_K1_NOTHING
-    if (true) return;
-#endif
-#ifndef ASA_EXP_K1_NOTMEM
     if (warp == 1) { tmem_alloc(holder, 512); tmem_relinquish(); }
-#endif
     if (threadIdx.x >= EPI0) {
         const int r = threadIdx.x - EPI0;
         if (r < TILE) {
             const int q = qb * TILE + r;
             qidx_blk[r] = (q < s.NQ && s.causal) ? Qidx[(size_t)bh * s.NQ + q] : INT_MAX;
         }
-        for (int i = r; i < s.nKB; i += NEPI) flags[i] = 0;
-#ifdef ASA_EXP_K1_NOSCHED
-        if (r == 0) misc[8] = qb + 1;
-#else
-        const int n = sched_visible(sched, misc, s, bd, bh, qb, r);
-        if (r == 0) misc[8] = n;
-#endif
+        for (int i = r; i < 3 * NW * TILE; i += NE) thr_s[i] = ASA_SENTINEL;
+        for (int i = r; i < s.nKB; i += NE) flags[i] = 0;
+        if (r < NEPI) {                       // the schedule builders' barrier counts NEPI threads
+            const int n = sched_visible(sched, misc, s, bd, bh, qb, r);
+            if (r == 0) misc[8] = n;
+        }
     }
     tc_fence_before();
     __syncthreads();
-    CTA_MARK(0, 1);
     tc_fence_after();
     const uint32_t tbase = *holder;
     const int qmin_blk = s.causal ? bd.qmin[bh * s.nQB + qb] : INT_MIN;
-    // visible tiles, visited twice in ascending key-block order
-#ifdef ASA_EXP_K1_EMPTY
-    if (true) {
-        tc_fence_before();
-        __syncthreads();
-#ifndef ASA_EXP_K1_NOTMEM
-        if (warp == 1) { tc_fence_after(); tmem_dealloc(tbase, 512); }
-#endif
-        return;
-    }
-#endif
-#ifdef ASA_EXP_K1_T1
-    const int T = misc[8] > 0 ? 1 : 0;
-#else
     const int T = misc[8];
-#endif
+    CTA_MARK(0, 1);
 
     if (warp == 0) {
         if (lane == 0 && T > 0) {
@@ -474,13 +533,11 @@ k1_tau_mask(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
             mbar_expect_tx(q_full, TB);
             for (int bx = 0; bx < D / BOX; ++bx)
                 tma_load_3d(sQ + bx * BOX_BYTES, &tmQ, q_full, bx * BOX, qb * TILE, bh);
-            for (int j = 0; j < NPASS * T; ++j) {
-                const int kb = (int)(sched[j < T ? j : j - T] & SCHED_IDX);
+            for (int j = 0; j < T; ++j) {
+                const int kb = (int)(sched[j] & SCHED_IDX);
                 const int st = j % S;
-#ifdef ASA_EXP_K1_NOTMA
-                if (j >= S) break;
-#endif
                 mbar_wait(&k_empty[st], ((j / S) & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+                TRACE(4, j, 0);
                 mbar_expect_tx(&k_full[st], TB);
                 for (int bx = 0; bx < D / BOX; ++bx)
                     tma_load_3d(sK + st * TB + bx * BOX_BYTES, &tmK, &k_full[st], bx * BOX, kb * TILE, bh);
@@ -489,141 +546,214 @@ k1_tau_mask(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
     } else if (warp == 1) {
         constexpr uint32_t idesc = idesc_bf16(128, 128, 0, 0);
         if (T > 0) mbar_wait(q_full, 0, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
-        for (int j = 0; j < NPASS * T; ++j) {
-            const uint32_t e = sched[j < T ? j : j - T];
+        if (lane == 0) CTA_MARK_T(0, 6);
+        for (int j = 0; j < T; ++j) {
+            const uint32_t e = sched[j];
             const int kb = (int)(e & SCHED_IDX);
             const int st = j % S, b = j % NB;
             uint8_t* kt = sK + st * TB;
-#ifdef ASA_EXP_K1_NOTMA
-            if (j < S)
-#endif
             mbar_wait(&k_full[st], (j / S) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
-#ifdef ASA_EXP_K1_NOFIX
-            if (false) {
-#else
+            if (lane == 0) TRACE(5, j, 0);
             if (e & SCHED_FIX) {
-#endif
                 fix_tile<D>(kt, qidx_blk, qmin_blk, Kidx_bh, kb, s.NK, lane);
                 fence_async_smem();
             }
             __syncwarp();
             mbar_wait(&s_free[b], ((j / NB) & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+            if (lane == 0) TRACE(5, j, 1);
             tc_fence_after();
             if (lane == 0) {
-#ifndef ASA_EXP_K1_NOMMA
 #pragma unroll
                 for (int kk = 0; kk < D / 16; ++kk)
                     mma_bf16_ss(tbase + b * 128, kdesc(sQ, kk), kdesc(kt, kk), idesc, kk > 0);
-#endif
+                TRACE(5, j, 2);
                 mma_commit(&s_full[b]);
                 mma_commit(&k_empty[st]);
+                if (j == 0) CTA_MARK_T(0, 7);
             }
             __syncwarp();
         }
     } else {
         const int row = (warp & 3) * 32 + lane;
         const int et = threadIdx.x - EPI0;
-        const int h = et / TILE;                  // column half of each tile
+        const int h = et / TILE;                  // column slice of each tile
         const int q = qb * TILE + row;
         const bool qv = q < s.NQ;
         const int qpos = !qv ? INT_MIN : (s.causal ? Qidx[(size_t)bh * s.NQ + q] : INT_MAX);
         const uint32_t tl = tmem_lane_base(tbase, warp);
         const bool scale_pos = s.scale > 0.0f;
+        const float inv_scale = scale_pos ? 1.0f / s.scale : 0.0f;
+        float4* my = cbuf + et * CP * 8;
+        const int sw = lane & 7;                  // 16-byte slot swizzle: conflict-free chunk stores
+        // Published bounds of the row's k-th score (each list holds distinct
+        // scores): b0 = this list's k-th; b1 = its ceil(k/NW)-th (the minimum
+        // over the NW lists bounds k scores); b2 = its ceil(k/2)-th (the
+        // second largest over the lists bounds k scores).
+        const int first = KM - s.k;
+        const int i1 = first + (s.k + NW - 1) / NW - 1, i2 = first + (s.k + 1) / 2 - 1;
         TopK<KM> tk;
         tk.init(s.k);
-        float t0 = neg_inf();
-        for (int j = 0; j < NPASS * T; ++j) {
-            const bool passB = !TWO_PASS || j >= T;
-            if (TWO_PASS && j == T) {
-                t0 = tk.threshold();          // k-th largest chunk maximum (or the sentinel)
-                tk.init(s.k);
-            }
-            const uint32_t e = sched[j < T ? j : j - T];
+        for (int j = 0; j < T; ++j) {
+            const uint32_t e = sched[j];
             const int kb = (int)(e & SCHED_IDX);
             const int b = j % NB;
             const bool all = (e & SCHED_ALL) != 0;
-            mbar_wait(&s_full[b], (j / NB) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
-            tc_fence_after();
-            uint32_t r2[CPT][32];
+            float lim = tk.threshold();
+            {
+                float m1 = __uint_as_float(0x7f800000u), x2 = neg_inf(), y2 = neg_inf();
 #pragma unroll
-            for (int cc = 0; cc < CPT; ++cc) tmem_ld32(tl + b * 128 + (h * CPT + cc) * 32, r2[cc]);
+                for (int g = 0; g < NW; ++g) {
+                    const volatile float* t = thr_s + g * TILE + row;
+                    if (g != h) lim = fmaxf(lim, t[0]);
+                    m1 = fminf(m1, t[NW * TILE]);
+                    const float c2 = t[2 * NW * TILE];
+                    y2 = fmaxf(y2, fminf(x2, c2));
+                    x2 = fmaxf(x2, c2);
+                }
+                lim = fmaxf(lim, fmaxf(m1, NW > 2 ? y2 : neg_inf()));
+            }
+            mbar_wait(&s_full[b], (j / NB) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+            if (j == 0 && et == 0) CTA_MARK_T(0, 8);
+            if (et == 0) TRACE(6, j, 0);
+            tc_fence_after();
+            uint32_t r2[CP][32];
+#pragma unroll
+            for (int cc = 0; cc < CP; ++cc) tmem_ld32(tl + b * 128 + (h * CP + cc) * 32, r2[cc]);
             tmem_ld_wait();
             tc_fence_before();
             epi_arrive(&s_free[b]);          // S is in registers: release the buffer
+            if (et == 0) TRACE(6, j, 1);
+            uint32_t vis[CP];
 #pragma unroll
-            for (int cc = 0; cc < CPT; ++cc) {
-                const int c = h * CPT + cc;
-                const int kn0 = kb * TILE + c * 32;
+            for (int cc = 0; cc < CP; ++cc) {
+                vis[cc] = 0xffffffffu;
+                if (!all) {
+                    vis[cc] = vis_mask32(Kidx_bh, kb * TILE + (h * CP + cc) * 32, s.NK, s.causal, qpos);
+#pragma unroll
+                    for (int i = 0; i < 32; ++i)
+                        if (!((vis[cc] >> i) & 1u)) r2[cc][i] = 0xff800000u;   // -inf: never a candidate
+                }
+            }
+            if (j == 0 && all && scale_pos) {
+                // Seed on a fully visible first tile: the KM groups of GSZ
+                // consecutive scores of the row's 128 have KM distinct
+                // maxima, so the smallest bounds the row's k-th score.
+                float t0 = __uint_as_float(0x7f800000u);
+#pragma unroll
+                for (int g = 0; g < CP * 32 / GSZ; ++g) {
+                    float m = __uint_as_float(r2[(g * GSZ) / 32][(g * GSZ) % 32]);
+#pragma unroll
+                    for (int i = 1; i < GSZ; ++i)
+                        m = fmaxf(m, __uint_as_float(r2[(g * GSZ + i) / 32][(g * GSZ + i) % 32]));
+                    t0 = fminf(t0, m);
+                }
+                seed_s[h * TILE + row] = t0;
+                asm volatile("bar.sync 2, %0;" ::"n"(NE) : "memory");   // uniform: same schedule everywhere
+#pragma unroll
+                for (int g = 0; g < NW; ++g) t0 = fminf(t0, seed_s[g * TILE + row]);
+                lim = fmaxf(lim, clamp_score(t0, s.scale));
+            }
+#pragma unroll
+            for (int cc = 0; cc < CP; ++cc) {
+                const int kn0 = kb * TILE + (h * CP + cc) * 32;
                 const uint32_t (&r)[32] = r2[cc];
-                float mraw = __uint_as_float(r[0]);
+                // candidate mask: bit i set when score i may reach lim
+                uint32_t cand;
+                if (scale_pos && lim > -10.0f) {
+                    const float rlo = (lim - fmaf(fabsf(lim), 0x1p-20f, 0x1p-100f)) * inv_scale;
+                    const float2 lo2 = make_float2(rlo, rlo), m1 = make_float2(-1.0f, -1.0f);
+                    uint32_t c4[4] = {0u, 0u, 0u, 0u};
 #pragma unroll
-                for (int i = 1; i < 32; ++i) mraw = fmaxf(mraw, __uint_as_float(r[i]));
-                const bool fast = all && scale_pos;
-                if (!passB) {
-                    // pass A: this chunk's largest visible score
-                    float m;
-                    if (fast) {
-                        m = clamp_score(mraw, s.scale);    // clamp(x·scale) is monotone in x
-                    } else {
-                        int kp[32];
-                        load_kpos32(Kidx_bh, kn0, s.NK, s.causal, kp);
-                        m = neg_inf();
+                    for (int i = 3; i >= 0; --i) {
 #pragma unroll
-                        for (int i = 0; i < 32; ++i)
-                            if (all || kp[i] <= qpos) m = fmaxf(m, clamp_score(__uint_as_float(r[i]), s.scale));
+                        for (int q4 = 0; q4 < 4; ++q4) {
+                            const int i0 = q4 * 8 + 2 * i;
+                            const float2 dlt = __ffma2_rn(make_float2(__uint_as_float(r[i0]),
+                                                                      __uint_as_float(r[i0 + 1])), m1, lo2);
+                            c4[q4] = __funnelshift_l(__float_as_uint(dlt.y), c4[q4], 1);
+                            c4[q4] = __funnelshift_l(__float_as_uint(dlt.x), c4[q4], 1);
+                        }
                     }
-                    if (m > tk.threshold()) tk.insert(m, 0);
-                    continue;
+                    cand = (c4[0] | (c4[1] << 8) | (c4[2] << 16) | (c4[3] << 24)) & vis[cc];
+                } else {
+                    cand = vis[cc];               // no bound above the clamp floor yet: every score
                 }
-                const float lim = fmaxf(tk.threshold(), t0);
-                if (fast && !(clamp_score(mraw, s.scale) >= lim)) continue;
-                int kp[32];
-                if (!all) load_kpos32(Kidx_bh, kn0, s.NK, s.causal, kp);
-                float sv[32];
-                uint32_t cand = 0;
+                if (cand) {
 #pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    const bool v = all || kp[i] <= qpos;
-                    sv[i] = v ? clamp_score(__uint_as_float(r[i]), s.scale) : neg_inf();
-                    cand |= (sv[i] >= t0 && sv[i] > tk.threshold() ? 1u : 0u) << i;
+                    for (int m = 0; m < 8; ++m)
+                        my[cc * 8 + (m ^ sw)] = make_float4(__uint_as_float(r[4 * m]), __uint_as_float(r[4 * m + 1]),
+                                                            __uint_as_float(r[4 * m + 2]), __uint_as_float(r[4 * m + 3]));
                 }
+                const float* myf = reinterpret_cast<const float*>(my + cc * 8);
                 while (cand) {
                     const int i = __ffs(cand) - 1;
                     cand &= cand - 1;
-                    const float val = pick32(sv, i);
-                    if (val > tk.threshold()) tk.insert(val, kn0 + i);
+                    const float v = clamp_score(myf[(((i >> 2) ^ sw) << 2) | (i & 3)], s.scale);
+                    if (v > tk.threshold()) tk.insert(v, kn0 + i);   // keys ascend per thread
                 }
             }
-        }
-        // warpgroup 0 merges the other groups' lists one at a time
-        for (int g = 1; g < NWG; ++g) {
-            if (h == g) {
+            {
+                float v1 = tk.v[KM - 1], v2 = tk.v[KM - 1];
 #pragma unroll
                 for (int i = 0; i < KM; ++i) {
-                    topv_s[row * KM + i] = tk.v[i];
-                    topi_s[row * KM + i] = tk.i[i];
+                    if (i == i1) v1 = tk.v[i];
+                    if (i == i2) v2 = tk.v[i];
                 }
+                volatile float* t = thr_s + h * TILE + row;
+                t[0] = tk.threshold();
+                t[NW * TILE] = v1;
+                t[2 * NW * TILE] = v2;
             }
-            epi_bar();
-            if (h == 0)
-                for (int i = KM - s.k; i < KM; ++i) tk.insert_lex(topv_s[row * KM + i], topi_s[row * KM + i]);
-            epi_bar();
+            if (et == 0) TRACE(6, j, 2);
+            if (j == 0 && et == 0) CTA_MARK_T(0, 2);
         }
-        if (h == 0) {
-            if (qv) {
-                tau[(size_t)bh * s.NQ + q] = ref_tau<KM>(tk.v, s.k, s.alpha);
+        if (et == 0) CTA_MARK_T(0, 3);
+        // Merge: one thread per row walks the NW sorted lists (64-bit keys
+        // ordered like (score desc, key index asc); identical keys -- the
+        // -1e6 seeds -- go by list number) and emits the row's top-k in
+        // order; τ is solved from them by k1_tau_solve.
+        asm volatile("bar.sync 2, %0;" ::"n"(NE) : "memory");   // K stages no longer read
 #pragma unroll
-                for (int i = 0; i < KM; ++i)
-                    if (tk.i[i] >= 0) flags[tk.i[i] / TILE] = 1;
+        for (int i = 0; i < KM; ++i) lists[(h * KM + i) * TILE + row] = order_key(tk.v[i], tk.i[i]);
+        asm volatile("bar.sync 2, %0;" ::"n"(NE) : "memory");
+        if (et == 0) CTA_MARK_T(0, 9);
+        if (h == 0 && qv) {
+            int pos[NW];
+            unsigned long long cur[NW];
+#pragma unroll
+            for (int g = 0; g < NW; ++g) {
+                pos[g] = first;
+                cur[g] = lists[(g * KM + first) * TILE + row];
+            }
+            float* out = topv + ((size_t)bh * s.NQ + q) * s.k;
+            for (int rk = 0; rk < s.k; ++rk) {
+                int bg = 0;
+                unsigned long long best = cur[0];
+#pragma unroll
+                for (int g = 1; g < NW; ++g)
+                    if (cur[g] > best) { best = cur[g]; bg = g; }
+                out[rk] = order_value(best);
+                const int key = order_index(best);
+                if (key >= 0) flags[key / TILE] = 1;
+#pragma unroll
+                for (int g = 0; g < NW; ++g)
+                    if (g == bg) {
+                        ++pos[g];
+                        cur[g] = pos[g] < KM ? lists[(g * KM + pos[g]) * TILE + row] : 0ull;
+                    }
             }
         }
-        epi_bar();
+        if (et == 0) CTA_MARK_T(0, 10);
+        asm volatile("bar.sync 2, %0;" ::"n"(NE) : "memory");
+        if (et == 0) CTA_MARK_T(0, 13);
         uint8_t* Mrow = M + ((size_t)bh * s.nQB + qb) * s.nKB;
-        for (int i = et; i < s.nKB; i += NEPI) Mrow[i] = flags[i];
+        for (int i = et; i < s.nKB; i += NE) Mrow[i] = flags[i];
+        if (et == 0) CTA_MARK_T(0, 4);
     }
     tc_fence_before();
     __syncthreads();
-    CTA_MARK(0, 2);
+    CTA_MARK(0, 5);
+    if (threadIdx.x == 0) g_cta_n(0, T);
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tbase, 512);
@@ -891,11 +1021,10 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
                         n += p[i];
                     }
                 } else {
-                    int kp[32];
-                    load_kpos32(Kidx_bh, kb * TILE + c * 32, s.NK, s.causal, kp);
+                    const uint32_t vis = vis_mask32(Kidx_bh, kb * TILE + c * 32, s.NK, s.causal, qpos);
 #pragma unroll
                     for (int i = 0; i < 32; ++i) {
-                        const bool v = kp[i] <= qpos;
+                        const bool v = (vis >> i) & 1u;
                         const float u = __fmaf_rn(s.am1, clamp_score(__uint_as_float(r[i]), s.scale), -tq);
                         p[i] = v ? entmax_pk<PINV>(u, s.pinv.e) : 0.0f;
                         n += p[i];
@@ -1145,12 +1274,12 @@ k4_dq(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
                 tmem_ld32(tl + tS + c * 32, rs);
                 tmem_ld32(tl + tP + c * 32, rp);
                 tmem_ld_wait();
-                int kp[32];
-                if (!all) load_kpos32(Kidx_bh, kb * TILE + c * 32, s.NK, s.causal, kp);
+                const uint32_t vis = all ? 0xffffffffu
+                                         : (qv ? vis_mask32(Kidx_bh, kb * TILE + c * 32, s.NK, s.causal, qpos) : 0u);
                 float g[32];
 #pragma unroll
                 for (int i = 0; i < 32; ++i) {
-                    const bool v = all || (qv && kp[i] <= qpos);
+                    const bool v = (vis >> i) & 1u;
                     const float u = __fmaf_rn(s.am1, clamp_score(__uint_as_float(rs[i]), s.scale), -tq);
                     g[i] = v ? grad_pk<PE2>(u, s.pe2.e, __uint_as_float(rp[i]), Dq, invN) : 0.0f;
                 }
@@ -1566,10 +1695,12 @@ bool is_sm100() {
 #if ASA_PART(1)
 bool tc_supported(const Shape& s) {
     return s.in_dtype == ASA_DTYPE_BF16 && (s.d == 64 || s.d == 128) && s.BM == TILE && s.BN == TILE &&
-           s.NK > 0 && s.nKB <= 32768 && is_sm100();
+           s.NK > 0 && s.nKB <= 2048 && is_sm100();   // per-CTA schedules live in shared memory
 }
 
-size_t tc_fwd_workspace(const Shape& s) { return bounds_ints(s) * 4; }
+// Forward workspace: [per-block index bounds | per-row top-k scores (k1 -> τ solve)]
+size_t topv_offset(const Shape& s) { return (bounds_ints(s) * 4 + 15) & ~size_t(15); }
+size_t tc_fwd_workspace(const Shape& s) { return topv_offset(s) + (size_t)s.BH * s.NQ * s.k * 4; }
 size_t tc_bwd_workspace(const Shape& s) {
     return ((bounds_ints(s) * 4 + 15) & ~size_t(15)) + (size_t)2 * s.BH * s.NQ * 4;
 }
@@ -1610,27 +1741,30 @@ cudaError_t tc_tau_mask(const Shape& s, const void* Q, const void* K, const int3
     if (!make_map(&mQ, Q, s.BH, s.NQ, s.d) || !make_map(&mK, K, s.BH, s.NK, s.d)) return cudaErrorInvalidValue;
     Bounds bd = bounds_at(s, ws);
     dim3 grid(s.nQB, s.BH);
-    auto go = [&](auto kern, int D, int KM) -> cudaError_t {
-        const size_t smem = (size_t)D * TILE * 2 * 5 + (size_t)TILE * KM * 8 + kSmemTail + (size_t)s.nKB * 5 + 64;
+    float* topv = (float*)((char*)ws + topv_offset(s));
+    const size_t rows = (size_t)s.BH * s.NQ;
+    auto go = [&](auto kern, auto solve, int D, int NW) -> cudaError_t {
+        const int S = 3;
+        const size_t smem = (size_t)D * TILE * 2 * (1 + S) + (size_t)128 * 128 * 4 + (size_t)NW * TILE * 16 +
+                            24 * 8 + 16 + 2 * TILE * 4 + 64 + (size_t)s.nKB * 5 + 64;
         cudaError_t r = prep(kern, smem);
         if (r != cudaSuccess) return r;
-        kern<<<grid, NTHREADS, smem, st>>>(mQ, mK, s, Qidx, Kidx, bd, tau, M, err);
+        kern<<<grid, 64 + 128 * NW, smem, st>>>(mQ, mK, s, Qidx, Kidx, bd, topv, M, err);
+        note_launch();
+        r = cudaGetLastError();
+        if (r != cudaSuccess) return r;
+        solve<<<(unsigned)((rows + 127) / 128), 128, 0, st>>>(topv, tau, rows, s.k, s.alpha);
         note_launch();
         return cudaGetLastError();
     };
-#ifdef ASA_K1_TWO_PASS
-    constexpr bool TP = true;
-#else
-    constexpr bool TP = false;
-#endif
     if (s.d == 128) {
-        if (s.k <= 8) return go(k1_tau_mask<128, 8, TP>, 128, 8);
-        if (s.k <= 16) return go(k1_tau_mask<128, 16, TP>, 128, 16);
-        return go(k1_tau_mask<128, 32, TP>, 128, 32);
+        if (s.k <= 8) return go(k1_tau_mask<128, 8, 4>, k1_tau_solve<8>, 128, 4);
+        if (s.k <= 16) return go(k1_tau_mask<128, 16, 2>, k1_tau_solve<16>, 128, 2);
+        return go(k1_tau_mask<128, 32, 2>, k1_tau_solve<32>, 128, 2);
     }
-    if (s.k <= 8) return go(k1_tau_mask<64, 8, TP>, 64, 8);
-    if (s.k <= 16) return go(k1_tau_mask<64, 16, TP>, 64, 16);
-    return go(k1_tau_mask<64, 32, TP>, 64, 32);
+    if (s.k <= 8) return go(k1_tau_mask<64, 8, 4>, k1_tau_solve<8>, 64, 4);
+    if (s.k <= 16) return go(k1_tau_mask<64, 16, 2>, k1_tau_solve<16>, 64, 2);
+    return go(k1_tau_mask<64, 32, 2>, k1_tau_solve<32>, 64, 2);
 }
 
 #endif  // part 1
@@ -1771,6 +1905,11 @@ void* exp_trace_ptr_impl();
 extern "C" void* asa_exp_trace_ptr() {
     void* p = nullptr;
     cudaGetSymbolAddress(&p, asa::g_trace);
+    return p;
+}
+extern "C" void* asa_exp_cnt_ptr() {
+    void* p = nullptr;
+    cudaGetSymbolAddress(&p, asa::g_cnt);
     return p;
 }
 #endif

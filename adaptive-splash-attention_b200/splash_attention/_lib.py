@@ -7,7 +7,8 @@ import ctypes
 import os
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(HERE, "libasa.so")
+# ASA_LIBRARY selects another build of the same C ABI (e.g. an instrumented one).
+LIB_PATH = os.environ.get("ASA_LIBRARY") or os.path.join(HERE, "libasa.so")
 
 ASA_OK, ASA_ERR_INVALID, ASA_ERR_UNSUPPORTED, ASA_ERR_WORKSPACE, ASA_ERR_CUDA, \
     ASA_ERR_DEVICE_TIMEOUT = range(6)

@@ -18,9 +18,7 @@ import json
 import math
 import os
 import statistics
-import subprocess
 import sys
-import tempfile
 import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
@@ -83,59 +81,70 @@ def make_inputs(c, rank, device, torch):
 
 
 class Clocks:
-    """nvidia-smi samples during the timed region."""
+    """SM clock and throttle reasons sampled through NVML every 5 ms by a
+    background thread while the timed region runs (a 200 ms nvidia-smi poll
+    sees nothing of a 50 ms region).  Read-only: no clock or power setting
+    is touched."""
 
-    def __init__(self, device_index):
-        self.proc = None
-        self.path = None
+    NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+
+    def __init__(self, device_index, period_s=0.005):
+        import threading
         self.dev = device_index
+        self.period = period_s
+        self.samples = []
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+        self._nvml = None
+
+    def _run(self):
+        nv, h = self._nvml
+        bits = (nv.nvmlClocksEventReasonHwSlowdown, nv.nvmlClocksEventReasonHwThermalSlowdown,
+                nv.nvmlClocksEventReasonSwThermalSlowdown, nv.nvmlClocksEventReasonSwPowerCap)
+        while not self._stop.is_set():
+            try:
+                mhz = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                r = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                self.samples.append((mhz, tuple(n for n, b_ in zip(self.NAMES, bits) if r & b_)))
+            except Exception:
+                return
+            self._stop.wait(self.period)
 
     def __enter__(self):
         try:
-            fd, self.path = tempfile.mkstemp(suffix=".csv")
-            os.close(fd)
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.dev),
-                 "--query-gpu=clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-                 "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-                 "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
-                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+            import threading
+            import pynvml as nv
+            nv.nvmlInit()
+            bus = None
+            try:
+                import torch
+                pr = torch.cuda.get_device_properties(self.dev)
+                bus = f"{pr.pci_domain_id:08X}:{pr.pci_bus_id:02X}:{pr.pci_device_id:02X}.0"
+            except Exception:
+                pass
+            h = (nv.nvmlDeviceGetHandleByPciBusId(bus) if bus
+                 else nv.nvmlDeviceGetHandleByIndex(self.dev))
+            self.max_mhz = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+            self._nvml = (nv, h)
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
         except Exception:
-            self.proc = None
+            self._thread = None
         return self
 
     def __exit__(self, *a):
-        if self.proc:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except Exception:
-                self.proc.kill()
+        if self._thread:
+            self._stop.set()
+            self._thread.join(timeout=2)
         return False
 
     def summary(self):
-        if not self.path or not os.path.exists(self.path):
+        if not self.samples:
             return None
-        mhz, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in open(self.path):
-            f = [x.strip() for x in line.split(",")]
-            if len(f) < 8:
-                continue
-            try:
-                mhz.append(float(f[0]))
-                mx = float(f[1])
-            except ValueError:
-                continue
-            for n, v in zip(names, f[4:8]):
-                if v.lower() == "active":
-                    reasons.add(n)
-        os.unlink(self.path)
-        if not mhz:
-            return None
-        return {"sm_mhz": statistics.median(mhz), "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(mhz)}
+        reasons = sorted({n for _, rs in self.samples for n in rs})
+        return {"sm_mhz": statistics.median(m for m, _ in self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": reasons, "samples": len(self.samples), "source": "nvml, 5 ms"}
 
 
 def cpu_baseline(c, steps=1):

@@ -26,6 +26,12 @@ CASES = {
     "bf16_c3s": (1, 2, 512, 512, 128, 128, 128, 8, 1.5, 128 ** -0.5, True, 1.0, torch.bfloat16, 0, 0, "auto"),
     "bf16_c5s": (2, 1, 512, 512, 64, 128, 128, 16, 1.25, 0.125, False, 2.0, torch.bfloat16, 0, 0, "auto"),
     "bf16_c4s": (1, 2, 1024, 1024, 128, 128, 128, 8, 2.0, 128 ** -0.5, True, 1.0, torch.bfloat16, 0, 64, "auto"),
+    # tensor-core path: ragged NQ != NK with shifted query positions, ragged
+    # non-causal keys, many key blocks per row, scores saturating the ±10 clamp
+    "bf16_ragged": (1, 2, 200, 300, 128, 128, 128, 8, 1.5, 128 ** -0.5, True, 1.0, torch.bfloat16, 100, 0, "auto"),
+    "bf16_noncausal_ragged": (1, 2, 200, 330, 64, 128, 128, 16, 1.5, 0.125, False, 1.0, torch.bfloat16, 0, 0, "auto"),
+    "bf16_n2048": (1, 2, 2048, 2048, 128, 128, 128, 8, 1.5, 128 ** -0.5, True, 1.0, torch.bfloat16, 0, 0, "auto"),
+    "bf16_saturated": (1, 1, 512, 512, 128, 128, 128, 8, 1.5, 0.3, True, 3.0, torch.bfloat16, 0, 0, "auto"),
 }
 
 
