@@ -55,6 +55,8 @@ constexpr int CPT = 4 / NWG;               // 32-column chunks per epilogue thre
 constexpr int NEPI = 128 * NWG;            // epilogue threads
 constexpr int NTHREADS = 64 + NEPI;        // + producer warp + MMA warp
 constexpr int EPI0 = 64;                   // first epilogue thread
+constexpr int K3_EPI0 = 96;                // forward: producer, S-issuer and P·V-issuer warps first
+constexpr int K3_THREADS = K3_EPI0 + NEPI;
 
 
 // Dynamic shared memory starts at the bottom of the CTA's window (these
@@ -253,6 +255,14 @@ __device__ __forceinline__ uint64_t kdesc(const uint8_t* tile, int kk) {
 // kk covers rows [16kk, 16kk+16); boxes are BOX_BYTES apart along M/N.
 __device__ __forceinline__ uint64_t mndesc(const uint8_t* tile, int kk) {
     return sdesc(smem_u32(tile + kk * 16 * 128), BOX_BYTES, 1024);
+}
+// The same descriptors from a base descriptor of the tile: k-steps only move
+// the 14-bit start-address field (shared addresses stay below 2^18 bytes).
+__device__ __forceinline__ uint64_t kdesc_step(uint64_t base, int kk) {
+    return base + (uint64_t)((((kk >> 2) * BOX_BYTES) + (kk & 3) * 32) >> 4);
+}
+__device__ __forceinline__ uint64_t mndesc_step(uint64_t base, int kk) {
+    return base + (uint64_t)((kk * 16 * 128) >> 4);
 }
 
 // Store 32 consecutive columns [32c, 32c+32) of row `row` of a 128x128 bf16
@@ -788,14 +798,19 @@ __device__ __forceinline__ void store_out32(TO* dst_row, int c, const float (&o)
 // A operand of O += P·V; a buffer is reused once that P·V completes.  The MMA
 // warp issues S two tiles ahead of the P·V it waits for.
 template <int D, typename TO, int PINV>
-__global__ void __launch_bounds__(NTHREADS, 1)
+__global__ void __launch_bounds__(K3_THREADS, 1)
 k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
            const __grid_constant__ CUtensorMap tmV, Shape s, const int32_t* __restrict__ Qidx,
            const int32_t* __restrict__ Kidx, Bounds bd, const float* __restrict__ tau,
            const int32_t* __restrict__ ptr, const int32_t* __restrict__ idx, TO* __restrict__ O,
            float* __restrict__ O32, float* __restrict__ rownorm, int split, int* err) {
+#ifdef ASA_EXP_F_S2V3
+    constexpr int S = 2;                      // K stages
+    constexpr int SV = 3;                     // V stages
+#else
     constexpr int S = 3;                      // K stages
     constexpr int SV = 2;                     // V stages
+#endif
     constexpr int NB = 3;                     // S / P buffers in TMEM
     constexpr int TB = D * TILE * 2;
     extern __shared__ uint8_t smem_raw[];
@@ -838,8 +853,8 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
         fence_barrier_init();
     }
     if (warp == 1) { tmem_alloc(holder, 512); tmem_relinquish(); }
-    if (threadIdx.x >= EPI0) {
-        const int r = threadIdx.x - EPI0;
+    if (threadIdx.x >= K3_EPI0) {
+        const int r = threadIdx.x - K3_EPI0;
         const int q = qb * TILE + r;
         if (r < TILE) qidx_blk[r] = (q < s.NQ && s.causal) ? Qidx[(size_t)bh * s.NQ + q] : INT_MAX;
         sched_from_list(sched, list + e0, T, s, bd, bh, qb, false, r);
@@ -869,7 +884,21 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
                 for (int bx = 0; bx < D / BOX; ++bx)
                     tma_load_3d(sK + st * TB + bx * BOX_BYTES, &tmK, &k_full[st], bx * BOX, kb * TILE, bh);
             }
-        } else if (lane == 1 && T > 0) {
+        }
+#ifdef ASA_EXP_TRACE
+        else if (lane == 2 && blockIdx.x == 0 && blockIdx.y == 0) {
+            for (int j = 0; j < T && j < 64; ++j) {
+                mbar_wait(&k_full[j % S], (j / S) & 1, s.spins, nullptr, 0);
+                TRACE(3, j, 0);
+            }
+        } else if (lane == 3 && blockIdx.x == 0 && blockIdx.y == 0) {
+            for (int j = 0; j < T && j < 64; ++j) {
+                mbar_wait(&v_full[j % SV], (j / SV) & 1, s.spins, nullptr, 0);
+                TRACE(3, j, 1);
+            }
+        }
+#endif
+        else if (lane == 1 && T > 0) {
             // V runs on its own thread: its ring (freed after P·V) must not
             // hold back the K ring (freed after S)
             for (int j = 0; j < T; ++j) {
@@ -883,74 +912,75 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
             }
         }
     } else if (warp == 1) {
+        // S = Q·K^T issuer.  tcgen05.mma issue blocks at the tensor pipe's
+        // rate, so S and P·V come from two warps: while one waits for its
+        // inputs the other keeps the pipe fed.  S(n) needs its K tile and
+        // TMEM buffer n % NB, which P·V(n - NB) frees.
         constexpr uint32_t idS = idesc_bf16(128, 128, 0, 0);
-        constexpr uint32_t idPV = idesc_bf16(128, D, 0, 1);
         if (T > 0) mbar_wait(q_full, 0, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
-        auto issue_s = [&](int j) {
-            const uint32_t e = sched[j];
-            const int kb = (int)(e & SCHED_IDX);
-            const int st = j % S, b = j % NB;
+        const uint64_t dQ = kdesc(sQ, 0);
+        for (int n = 0; n < T; ++n) {
+            const uint32_t e = sched[n];
+            const int st = n % S, b = n % NB;
             uint8_t* kt = sK + st * TB;
-            mbar_wait(&k_full[st], (j / S) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
-            if (lane == 0) TRACE(1, j, 0);
+            mbar_wait(&k_full[st], (n / S) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+            if (lane == 0) TRACE(1, n, 0);
             if (e & SCHED_FIX) {   // V is fixed before its P·V
-                fix_tile<D>(kt, qidx_blk, qmin_blk, Kidx_bh, kb, s.NK, lane);
+                fix_tile<D>(kt, qidx_blk, qmin_blk, Kidx_bh, (int)(e & SCHED_IDX), s.NK, lane);
                 fence_async_smem();
             }
             __syncwarp();
-            mbar_wait(&s_free[b], ((j / NB) & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
-            if (lane == 0) TRACE(1, j, 1);
+            mbar_wait(&s_free[b], ((n / NB) & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
             tc_fence_after();
             if (lane == 0) {
-#ifndef ASA_EXP_F_NOS
+                const uint64_t dK = kdesc(kt, 0);
 #pragma unroll
                 for (int kk = 0; kk < D / 16; ++kk)
-                    mma_bf16_ss(tbase + b * 128, kdesc(sQ, kk), kdesc(kt, kk), idS, kk > 0);
-#endif
+                    mma_bf16_ss(tbase + b * 128, kdesc_step(dQ, kk), kdesc_step(dK, kk), idS, kk > 0);
                 mma_commit(&s_full[b]);
                 mma_commit(&k_empty[st]);
+                TRACE(1, n, 3);
             }
-            if (lane == 0) TRACE(1, j, 3);
             __syncwarp();
-        };
-        if (T > 0) issue_s(0);
-        if (T > 1) issue_s(1);
-        for (int j = 0; j < T; ++j) {
-            if (j + 2 < T) issue_s(j + 2);
-            const int b = j % NB, sv = j % SV;
-            const uint8_t* vt = sV + sv * TB;
-            mbar_wait(&v_full[sv], (j / SV) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
-            if (sched[j] & SCHED_FIX) {
-                fix_tile<D>(sV + sv * TB, qidx_blk, qmin_blk, Kidx_bh, (int)(sched[j] & SCHED_IDX), s.NK, lane);
+        }
+    } else if (warp == 2) {
+        // O += P·V issuer: P·V(m) needs its V tile and the epilogue's P.
+        constexpr uint32_t idPV = idesc_bf16(128, D, 0, 1);
+        for (int m = 0; m < T; ++m) {
+            const uint32_t e = sched[m];
+            const int b = m % NB, sv = m % SV;
+            uint8_t* vt = sV + sv * TB;
+            mbar_wait(&v_full[sv], (m / SV) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+            if (e & SCHED_FIX) {
+                fix_tile<D>(vt, qidx_blk, qmin_blk, Kidx_bh, (int)(e & SCHED_IDX), s.NK, lane);
                 fence_async_smem();
             }
             __syncwarp();
-            mbar_wait(&p_full[b], (j / NB) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
-            if (lane == 0) TRACE(1, j, 2);
+            mbar_wait(&p_full[b], (m / NB) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+            if (lane == 0) TRACE(1, m, 2);
             tc_fence_after();
             if (lane == 0) {
                 const uint32_t pb = tbase + b * 128;
-#ifndef ASA_EXP_F_NOPV
+                const uint64_t dV = mndesc(vt, 0);
 #pragma unroll
                 for (int kk = 0; kk < TILE / 16; ++kk)
-                    mma_bf16_ts(tbase + tO, pb + kk * 16, mndesc(vt, kk), idPV, (j > 0 || kk > 0));
+                    mma_bf16_ts(tbase + tO, pb + kk * 16, mndesc_step(dV, kk), idPV, (m > 0 || kk > 0));
                 if (split) {
 #pragma unroll
                     for (int kk = 0; kk < TILE / 16; ++kk)
-                        mma_bf16_ts(tbase + tO, pb + kk * 16 + 8, mndesc(vt, kk), idPV, 1);
+                        mma_bf16_ts(tbase + tO, pb + kk * 16 + 8, mndesc_step(dV, kk), idPV, 1);
                 }
-#endif
                 mma_commit(&s_free[b]);
                 mma_commit(&v_empty[sv]);
+                TRACE(1, m, 4);
             }
-            if (lane == 0) TRACE(1, j, 4);
             __syncwarp();
         }
         if (lane == 0) mma_commit(o_full);
         __syncwarp();
     } else {
         const int row = (warp & 3) * 32 + lane;
-        const int et = threadIdx.x - EPI0;
+        const int et = threadIdx.x - K3_EPI0;
         const int h = et / TILE;
         const int q = qb * TILE + row;
         const bool qv = q < s.NQ;
@@ -1788,7 +1818,7 @@ cudaError_t tc_forward(const Shape& s, const void* Q, const void* K, const void*
             const size_t smem = (size_t)D * TILE * 2 * 6 + kSmemTail + (size_t)s.nKB * 4;
             cudaError_t r = prep(k, smem);
             if (r != cudaSuccess) return r;
-            k<<<grid, NTHREADS, smem, st>>>(mQ, mK, mV, s, Qidx, Kidx, bd, tau, ptr, idx, (TO*)O, O32,
+            k<<<grid, K3_THREADS, smem, st>>>(mQ, mK, mV, s, Qidx, Kidx, bd, tau, ptr, idx, (TO*)O, O32,
                                             rownorm, split, err);
             note_launch();
             return cudaGetLastError();
