@@ -28,6 +28,7 @@
 #include "asa_internal.h"
 #include "asa_sm100.cuh"
 #include <climits>
+#include <cstdio>
 #include <cudaTypedefs.h>
 #include <type_traits>
 
@@ -57,6 +58,10 @@ constexpr int NTHREADS = 64 + NEPI;        // + producer warp + MMA warp
 constexpr int EPI0 = 64;                   // first epilogue thread
 constexpr int K3_EPI0 = 96;                // forward: producer, S-issuer and P·V-issuer warps first
 constexpr int K3_THREADS = K3_EPI0 + NEPI;
+constexpr int DQ_NW = 4;                   // dQ: epilogue warpgroups (one 32-column chunk each)
+constexpr int DQ_NE = 128 * DQ_NW;
+constexpr int DQ_EPI0 = 96;                // dQ: producer, S/dP-issuer and dQ-issuer warps first
+constexpr int DQ_THREADS = DQ_EPI0 + DQ_NE;
 
 
 // Dynamic shared memory starts at the bottom of the CTA's window (these
@@ -1129,30 +1134,32 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
 // dQ 256-383, dS hi 384-447, dS lo 448-511.  K and V have two stages each;
 // V is released after dP, K after dQ.
 // ===========================================================================
-template <int D, typename TO, int PE2>
-__global__ void __launch_bounds__(NTHREADS, 1)
+template <int D, typename TO, int PE2, int SV>
+__global__ void __launch_bounds__(DQ_THREADS, 1)
 k4_dq(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
       const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO, Shape s,
       const int32_t* __restrict__ Qidx, const int32_t* __restrict__ Kidx, Bounds bd,
       const float* __restrict__ tau, const float* __restrict__ invNv, const float* __restrict__ Dqv,
       const int32_t* __restrict__ ptr, const int32_t* __restrict__ idx, TO* __restrict__ dQ, int split,
       int* err) {
-    constexpr int S = 2;
+    // K is held from S(j) until dQ(j) (a tile later), V only until dP(j):
+    // three K stages, SV V stages (two when shared memory allows).
+    constexpr int SK = 3;
     constexpr int TB = D * TILE * 2;
     extern __shared__ uint8_t smem_raw[];
     CTA_MARK(2, 0);
     uint8_t* base = align1024(smem_raw, err);
     uint8_t* sQ = base;
     uint8_t* sdO = base + TB;
-    uint8_t* sK = base + 2 * TB;              // S stages
-    uint8_t* sV = sK + S * TB;                // S stages
-    uint64_t* bars = reinterpret_cast<uint64_t*>(sV + S * TB);
+    uint8_t* sK = base + 2 * TB;              // SK stages
+    uint8_t* sV = sK + SK * TB;               // SV stages
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sV + SV * TB);
     uint64_t* q_full = bars;
     uint64_t* k_full = bars + 1;
-    uint64_t* k_empty = k_full + S;
-    uint64_t* v_full = k_empty + S;
-    uint64_t* v_empty = v_full + S;
-    uint64_t* sd_full = v_empty + S;
+    uint64_t* k_empty = k_full + SK;
+    uint64_t* v_full = k_empty + SK;
+    uint64_t* v_empty = v_full + SV;
+    uint64_t* sd_full = v_empty + SV;
     uint64_t* sd_free = sd_full + 1;
     uint64_t* ds_full = sd_free + 1;
     uint64_t* ds_free = ds_full + 1;
@@ -1171,23 +1178,21 @@ k4_dq(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
 
     if (threadIdx.x == 0) {
         mbar_init(q_full, 1);
-        for (int i = 0; i < S; ++i) {
-            mbar_init(&k_full[i], 1); mbar_init(&k_empty[i], 1);
-            mbar_init(&v_full[i], 1); mbar_init(&v_empty[i], 1);
-        }
+        for (int i = 0; i < SK; ++i) { mbar_init(&k_full[i], 1); mbar_init(&k_empty[i], 1); }
+        for (int i = 0; i < SV; ++i) { mbar_init(&v_full[i], 1); mbar_init(&v_empty[i], 1); }
         mbar_init(sd_full, 1);
-        mbar_init(sd_free, EPI_WARPS);
-        mbar_init(ds_full, EPI_WARPS);
+        mbar_init(sd_free, DQ_NE / 32);
+        mbar_init(ds_full, DQ_NE / 32);
         mbar_init(ds_free, 1);
         mbar_init(dq_full, 1);
         fence_barrier_init();
     }
     if (warp == 1) { tmem_alloc(holder, 512); tmem_relinquish(); }
-    if (threadIdx.x >= EPI0) {
-        const int r = threadIdx.x - EPI0;
+    if (threadIdx.x >= DQ_EPI0) {
+        const int r = threadIdx.x - DQ_EPI0;
         const int q = qb * TILE + r;
         if (r < TILE) qidx_blk[r] = (q < s.NQ && s.causal) ? Qidx[(size_t)bh * s.NQ + q] : INT_MAX;
-        sched_from_list(sched, list + e0, T, s, bd, bh, qb, false, r);
+        if (r < NEPI) sched_from_list(sched, list + e0, T, s, bd, bh, qb, false, r);
     }
     tc_fence_before();
     __syncthreads();
@@ -1206,8 +1211,9 @@ k4_dq(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
             }
             for (int j = 0; j < T; ++j) {
                 const int kb = (int)(sched[j] & SCHED_IDX);
-                const int st = j % S;
-                mbar_wait(&k_empty[st], ((j / S) & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+                const int st = j % SK;
+                mbar_wait(&k_empty[st], ((j / SK) & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+                TRACE(4, j, 0);
                 mbar_expect_tx(&k_full[st], TB);
                 for (int bx = 0; bx < D / BOX; ++bx)
                     tma_load_3d(sK + st * TB + bx * BOX_BYTES, &tmK, &k_full[st], bx * BOX, kb * TILE, bh);
@@ -1216,45 +1222,29 @@ k4_dq(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
             // V (freed after dP) on its own thread, ahead of K (freed after dQ)
             for (int j = 0; j < T; ++j) {
                 const int kb = (int)(sched[j] & SCHED_IDX);
-                const int st = j % S;
-                mbar_wait(&v_empty[st], ((j / S) & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+                const int st = j % SV;
+                mbar_wait(&v_empty[st], ((j / SV) & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+                TRACE(4, j, 1);
                 mbar_expect_tx(&v_full[st], TB);
                 for (int bx = 0; bx < D / BOX; ++bx)
                     tma_load_3d(sV + st * TB + bx * BOX_BYTES, &tmV, &v_full[st], bx * BOX, kb * TILE, bh);
             }
         }
     } else if (warp == 1) {
+        // S = Q·K^T and dP = dO·V^T issuer.  dQ comes from warp 2, so the
+        // tensor pipe always has the other warp's work while one waits.
         constexpr uint32_t idS = idesc_bf16(128, 128, 0, 0);
-        constexpr uint32_t idQ = idesc_bf16(128, D, 0, 1);
         if (T > 0) mbar_wait(q_full, 0, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
-        auto do_dq = [&](int i) {
-            const int st = i % S;
-            const uint8_t* kt = sK + st * TB;
-            mbar_wait(ds_full, i & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
-            tc_fence_after();
-            if (lane == 0) {
-#pragma unroll
-                for (int kk = 0; kk < TILE / 16; ++kk)
-                    mma_bf16_ts(tbase + tQ, tbase + tDh + kk * 8, mndesc(kt, kk), idQ, (i > 0 || kk > 0));
-                if (split) {
-#pragma unroll
-                    for (int kk = 0; kk < TILE / 16; ++kk)
-                        mma_bf16_ts(tbase + tQ, tbase + tDl + kk * 8, mndesc(kt, kk), idQ, 1);
-                }
-                mma_commit(ds_free);
-                mma_commit(&k_empty[st]);
-            }
-            __syncwarp();
-        };
+        const uint64_t dQd = kdesc(sQ, 0), dOd = kdesc(sdO, 0);
         for (int j = 0; j < T; ++j) {
             const uint32_t e = sched[j];
             const int kb = (int)(e & SCHED_IDX);
             const bool fix = (e & SCHED_FIX) != 0;
-            const int st = j % S;
+            const int st = j % SK, sv = j % SV;
             uint8_t* kt = sK + st * TB;
-            uint8_t* vt = sV + st * TB;
-            mbar_wait(&k_full[st], (j / S) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
-            mbar_wait(&v_full[st], (j / S) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+            uint8_t* vt = sV + sv * TB;
+            mbar_wait(&k_full[st], (j / SK) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+            mbar_wait(&v_full[sv], (j / SV) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
             if (fix) {
                 fix_tile<D>(kt, qidx_blk, qmin_blk, Kidx_bh, kb, s.NK, lane);
                 fix_tile<D>(vt, qidx_blk, qmin_blk, Kidx_bh, kb, s.NK, lane);
@@ -1262,25 +1252,54 @@ k4_dq(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
             }
             __syncwarp();
             mbar_wait(sd_free, (j & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+            if (lane == 0) TRACE(5, j, 0);
             tc_fence_after();
             if (lane == 0) {
+                const uint64_t dK = kdesc(kt, 0), dV = kdesc(vt, 0);
 #pragma unroll
                 for (int kk = 0; kk < D / 16; ++kk) {
-                    mma_bf16_ss(tbase + tS, kdesc(sQ, kk), kdesc(kt, kk), idS, kk > 0);
-                    mma_bf16_ss(tbase + tP, kdesc(sdO, kk), kdesc(vt, kk), idS, kk > 0);
+                    mma_bf16_ss(tbase + tS, kdesc_step(dQd, kk), kdesc_step(dK, kk), idS, kk > 0);
+                    mma_bf16_ss(tbase + tP, kdesc_step(dOd, kk), kdesc_step(dV, kk), idS, kk > 0);
                 }
                 mma_commit(sd_full);
-                mma_commit(&v_empty[st]);
+                mma_commit(&v_empty[sv]);
+                TRACE(5, j, 1);
             }
             __syncwarp();
-            if (j > 0) do_dq(j - 1);
         }
-        if (T > 0) do_dq(T - 1);
+    } else if (warp == 2) {
+        // dQ += dS·K issuer (in tile order: a deterministic sum)
+        constexpr uint32_t idQ = idesc_bf16(128, D, 0, 1);
+        for (int i = 0; i < T; ++i) {
+            const int st = i % SK;
+            const uint8_t* kt = sK + st * TB;
+            mbar_wait(ds_full, i & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+            if (lane == 0) TRACE(5, i, 2);
+            tc_fence_after();
+            if (lane == 0) {
+                const uint64_t dK = mndesc(kt, 0);
+#pragma unroll
+                for (int kk = 0; kk < TILE / 16; ++kk)
+                    mma_bf16_ts(tbase + tQ, tbase + tDh + kk * 8, mndesc_step(dK, kk), idQ, (i > 0 || kk > 0));
+                if (split) {
+#pragma unroll
+                    for (int kk = 0; kk < TILE / 16; ++kk)
+                        mma_bf16_ts(tbase + tQ, tbase + tDl + kk * 8, mndesc_step(dK, kk), idQ, 1);
+                }
+                mma_commit(ds_free);
+                mma_commit(&k_empty[st]);
+                TRACE(5, i, 3);
+            }
+            __syncwarp();
+        }
         if (lane == 0) mma_commit(dq_full);
         __syncwarp();
     } else {
+        // DQ_NW warpgroups; warpgroup h owns the 32-column chunk h of every
+        // tile (D = 128: four chunks).  S and dP are released as soon as they
+        // are in registers, so the next tile's S/dP overlaps this gradient.
         const int row = (warp & 3) * 32 + lane;
-        const int et = threadIdx.x - EPI0;
+        const int et = threadIdx.x - DQ_EPI0;
         const int h = et / TILE;
         const int q = qb * TILE + row;
         const bool qv = q < s.NQ;
@@ -1290,22 +1309,49 @@ k4_dq(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
         const float invN = qv ? invNv[qrow] : 0.0f;
         const float Dq = qv ? Dqv[qrow] : 0.0f;
         const uint32_t tl = tmem_lane_base(tbase, warp);
+        // packed path: u = min(raw·(α-1)·scale - τ, (α-1)·10 - τ); the clamp
+        // at -10 can only meet u <= 0, where the gradient is 0
+        constexpr bool kPacked = PE2 == 1 || PE2 == 3 || PE2 == 5;
+        const bool packed_row = kPacked && qv && __fmaf_rn(s.am1, -10.0f, -tq) <= 0.0f;
+        const float2 c1 = make_float2(__fmul_rn(s.am1, s.scale), __fmul_rn(s.am1, s.scale));
+        const float2 mtau = make_float2(-tq, -tq), mD = make_float2(-Dq, -Dq), iN = make_float2(invN, invN);
+        const float uhi = __fmaf_rn(s.am1, 10.0f, -tq);
         for (int j = 0; j < T; ++j) {
             const uint32_t e = sched[j];
             const int kb = (int)(e & SCHED_IDX);
             const bool all = qv && (e & SCHED_ALL) != 0;
             mbar_wait(sd_full, j & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+            if (et == 0) TRACE(6, j, 0);
             tc_fence_after();
-            uint32_t hi[CPT][16], lo[CPT][16];
+            uint32_t rs[32], rp[32];
+            tmem_ld32(tl + tS + h * 32, rs);
+            tmem_ld32(tl + tP + h * 32, rp);
+            tmem_ld_wait();
+            tc_fence_before();
+            epi_arrive(sd_free);
+            uint32_t hi[16], lo[16];
+            if (all && packed_row) {
 #pragma unroll
-            for (int cc = 0; cc < CPT; ++cc) {
-                const int c = h * CPT + cc;
-                uint32_t rs[32], rp[32];
-                tmem_ld32(tl + tS + c * 32, rs);
-                tmem_ld32(tl + tP + c * 32, rp);
-                tmem_ld_wait();
+                for (int m = 0; m < 16; ++m) {
+                    float2 u = __ffma2_rn(make_float2(__uint_as_float(rs[2 * m]), __uint_as_float(rs[2 * m + 1])),
+                                          c1, mtau);
+                    u.x = fminf(u.x, uhi);
+                    u.y = fminf(u.y, uhi);
+                    const float2 t = __fadd2_rn(make_float2(__uint_as_float(rp[2 * m]), __uint_as_float(rp[2 * m + 1])),
+                                                mD);
+                    float2 g;
+                    if constexpr (PE2 == 5) g = t;
+                    else if constexpr (PE2 == 1) g = __fmul2_rn(u, t);
+                    else g = __fmul2_rn(__fmul2_rn(__fmul2_rn(u, u), u), t);
+                    g = __fmul2_rn(g, iN);
+                    // u <= EPS or a non-finite product -> 0 (reference :481-507)
+                    g.x = (u.x > ASA_EPS && fabsf(g.x) < __int_as_float(0x7f800000)) ? g.x : 0.0f;
+                    g.y = (u.y > ASA_EPS && fabsf(g.y) < __int_as_float(0x7f800000)) ? g.y : 0.0f;
+                    split_pair(g, hi[m], lo[m]);
+                }
+            } else {
                 const uint32_t vis = all ? 0xffffffffu
-                                         : (qv ? vis_mask32(Kidx_bh, kb * TILE + c * 32, s.NK, s.causal, qpos) : 0u);
+                                         : (qv ? vis_mask32(Kidx_bh, kb * TILE + h * 32, s.NK, s.causal, qpos) : 0u);
                 float g[32];
 #pragma unroll
                 for (int i = 0; i < 32; ++i) {
@@ -1313,26 +1359,23 @@ k4_dq(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
                     const float u = __fmaf_rn(s.am1, clamp_score(__uint_as_float(rs[i]), s.scale), -tq);
                     g[i] = v ? grad_pk<PE2>(u, s.pe2.e, __uint_as_float(rp[i]), Dq, invN) : 0.0f;
                 }
-                split_pack(g, hi[cc], lo[cc]);
+                split_pack(g, hi, lo);
             }
-            tc_fence_before();
-            epi_arrive(sd_free);
+            if (et == 0) TRACE(6, j, 1);
             mbar_wait(ds_free, (j & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+            if (et == 0) TRACE(6, j, 2);
             tc_fence_after();
-#pragma unroll
-            for (int cc = 0; cc < CPT; ++cc) {
-                const int c = h * CPT + cc;
-                tmem_st16(tl + tDh + c * 16, hi[cc]);
-                if (split) tmem_st16(tl + tDl + c * 16, lo[cc]);
-            }
+            tmem_st16(tl + tDh + h * 16, hi);
+            if (split) tmem_st16(tl + tDl + h * 16, lo);
             tmem_st_wait();
             tc_fence_before();
             epi_arrive(ds_full);
+            if (et == 0) TRACE(6, j, 3);
         }
         mbar_wait(dq_full, 0, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
         tc_fence_after();
 #pragma unroll 1
-        for (int c = h; c < D / 32; c += NWG) {
+        for (int c = h; c < D / 32; c += DQ_NW) {
             uint32_t r[32];
             tmem_ld32(tl + tQ + c * 32, r);
             tmem_ld_wait();
@@ -1853,13 +1896,17 @@ cudaError_t tc_launch_dq(const Shape& s, const BwdArgs& a, cudaStream_t st) {
         constexpr int D = decltype(dtag)::value;
         using TO = std::remove_pointer_t<decltype(out)>;
         return with_alpha(s, [&](auto ac) -> cudaError_t {
-            auto kdq = k4_dq<D, TO, decltype(ac)::pe2>;
-            const size_t smem = bwd_smem<TO>(s, D);
+            // Q, dO, three K stages, SV V stages, barriers/holder (256 B),
+            // block positions (512 B), the tile schedule
+            auto smem_for = [&](int sv) { return (size_t)D * TILE * 2 * (5 + sv) + 256 + 512 + (size_t)s.nKB * 4; };
+            const bool two = smem_for(2) <= 232448;
+            auto kdq = two ? k4_dq<D, TO, decltype(ac)::pe2, 2> : k4_dq<D, TO, decltype(ac)::pe2, 1>;
+            const size_t smem = smem_for(two ? 2 : 1);
             cudaError_t r = prep(kdq, smem);
             if (r != cudaSuccess) return r;
-            kdq<<<dim3(s.nQB, s.BH), NTHREADS, smem, st>>>(a.mQ, a.mK, a.mV, a.mdO, s, a.Qidx, a.Kidx, a.bd,
-                                                          a.tau, a.invNv, a.Dq, a.ptr, a.idx, (TO*)a.dQ,
-                                                          split, a.err);
+            kdq<<<dim3(s.nQB, s.BH), DQ_THREADS, smem, st>>>(a.mQ, a.mK, a.mV, a.mdO, s, a.Qidx, a.Kidx, a.bd,
+                                                             a.tau, a.invNv, a.Dq, a.ptr, a.idx, (TO*)a.dQ,
+                                                             split, a.err);
             note_launch();
             return cudaGetLastError();
         });
