@@ -62,6 +62,9 @@ constexpr int DQ_NW = 4;                   // dQ: epilogue warpgroups (one 32-co
 constexpr int DQ_NE = 128 * DQ_NW;
 constexpr int DQ_EPI0 = 96;                // dQ: producer, S/dP-issuer and dQ-issuer warps first
 constexpr int DQ_THREADS = DQ_EPI0 + DQ_NE;
+constexpr int DKV_NW = 4;                  // dK/dV: epilogue warpgroups (32 queries of a tile each)
+constexpr int DKV_NE = 128 * DKV_NW;
+constexpr int DKV_THREADS = 64 + DKV_NE;
 
 
 // Dynamic shared memory starts at the bottom of the CTA's window (these
@@ -1415,7 +1418,7 @@ __device__ __forceinline__ uint32_t pair_col(int kk, bool lo) {
 }
 
 template <int D, typename TO, int PINV, int PE2>
-__global__ void __launch_bounds__(NTHREADS, 1)
+__global__ void __launch_bounds__(DKV_THREADS, 1)
 k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
         const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO, Shape s,
         const int32_t* __restrict__ Qidx, const int32_t* __restrict__ Kidx, Bounds bd,
@@ -1440,9 +1443,10 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
     uint64_t* pd_free = pd_full + 1;
     uint64_t* out_full = pd_free + 1;
     uint32_t* holder = reinterpret_cast<uint32_t*>(bars + 16);
-    // per query of the current (and next) block: {τ, 1/n, D, position}
-    float4* qinfo = reinterpret_cast<float4*>(holder + 4);   // [2][128]
-    int* qidx_blk = reinterpret_cast<int*>(qinfo + 2 * TILE); // [128] for the tile-load fix
+    // per query of the current (and next) block, one array each (pairs load
+    // as float2): -τ, lower and upper u bound, 1/n, -D, position
+    float* qinfo = reinterpret_cast<float*>(holder + 4);     // [2][6][128]
+    int* qidx_blk = reinterpret_cast<int*>(qinfo + 2 * 6 * TILE); // [128] for the tile-load fix
     uint32_t* sched = reinterpret_cast<uint32_t*>(qidx_blk + TILE);   // [T]
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -1458,13 +1462,14 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
         mbar_init(kv_full, 1);
         for (int i = 0; i < SQ; ++i) { mbar_init(&q_full[i], 1); mbar_init(&q_empty[i], 1); }
         mbar_init(sd_full, 1);
-        mbar_init(pd_full, EPI_WARPS);
+        mbar_init(pd_full, DKV_NE / 32);
         mbar_init(pd_free, 1);
         mbar_init(out_full, 1);
         fence_barrier_init();
     }
     if (warp == 1) { tmem_alloc(holder, 512); tmem_relinquish(); }
-    if (threadIdx.x >= EPI0) sched_from_list(sched, list + e0, T, s, bd, bh, kb, true, threadIdx.x - EPI0);
+    if (threadIdx.x >= EPI0 && threadIdx.x < EPI0 + NEPI)
+        sched_from_list(sched, list + e0, T, s, bd, bh, kb, true, threadIdx.x - EPI0);
     tc_fence_before();
     __syncthreads();
     CTA_MARK(3, 1);
@@ -1558,6 +1563,8 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
         if (lane == 0) mma_commit(out_full);
         __syncwarp();
     } else {
+        // DKV_NW warpgroups; warpgroup h owns queries [32h, 32h+32) of every
+        // query tile (two 16-query groups)
         const int row = (warp & 3) * 32 + lane;
         const int et = threadIdx.x - EPI0;
         const int h = et / TILE;
@@ -1566,58 +1573,88 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
         const size_t krow = (size_t)bh * s.NK + (kv ? kn : 0);
         const int kpos = !kv ? INT_MAX : (s.causal ? Kidx_bh[kn] : INT_MIN);
         const uint32_t tl = tmem_lane_base(tbase, warp);
+        constexpr bool kPacked = (PINV == 1 || PINV == 2 || PINV == 4) && (PE2 == 1 || PE2 == 3 || PE2 == 5);
+        const float2 c1 = make_float2(__fmul_rn(s.am1, s.scale), __fmul_rn(s.am1, s.scale));
         // Query-block metadata of pair i lives in qinfo[i & 1]; it is fetched
         // one pair ahead so its global loads overlap the previous pair.
-        auto fetch = [&](int i, float4& out) {
+        auto fetch = [&](int i, float* dst) {
             const int qb = (int)(sched[i] & SCHED_IDX);
             const int q = qb * TILE + et;
             const bool ok = q < s.NQ;
             const size_t r = (size_t)bh * s.NQ + (ok ? q : 0);
-            out = make_float4(ok ? tau[r] : 0.0f, ok ? invNv[r] : 0.0f, ok ? Dqv[r] : 0.0f,
-                              __int_as_float(ok ? (s.causal ? Qidx_bh[q] : INT_MAX) : INT_MIN));
+            const float tq = ok ? tau[r] : 0.0f;
+            dst[0 * TILE + et] = -tq;
+            dst[1 * TILE + et] = __fmaf_rn(s.am1, -10.0f, -tq);
+            dst[2 * TILE + et] = __fmaf_rn(s.am1, 10.0f, -tq);
+            dst[3 * TILE + et] = ok ? invNv[r] : 0.0f;
+            dst[4 * TILE + et] = ok ? -Dqv[r] : 0.0f;
+            dst[5 * TILE + et] = __int_as_float(ok ? (s.causal ? Qidx_bh[q] : INT_MAX) : INT_MIN);
         };
-        if (T > 0 && et < TILE) {
-            float4 v;
-            fetch(0, v);
-            qinfo[et] = v;
-        }
+        if (T > 0 && et < TILE) fetch(0, qinfo);
         for (int i = 0; i < T; ++i) {
             const uint32_t e = sched[i];
-            epi_bar();   // qinfo[i&1] written; every reader of qinfo[(i+1)&1] (pair i-1) done
-            if (i + 1 < T && et < TILE) {
-                float4 v;
-                fetch(i + 1, v);
-                qinfo[((i + 1) & 1) * TILE + et] = v;
-            }
-            const float4* qi = qinfo + (i & 1) * TILE;
+            asm volatile("bar.sync 2, %0;" ::"n"(DKV_NE) : "memory");   // qinfo[i&1] written; pair i-1 done
+            if (i + 1 < T && et < TILE) fetch(i + 1, qinfo + ((i + 1) & 1) * 6 * TILE);
+            const float* qi = qinfo + (i & 1) * 6 * TILE;
             const bool all = kv && (e & SCHED_ALL) != 0;
             mbar_wait(sd_full, i & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
             tc_fence_after();
 #pragma unroll 1
-            for (int gq = h * 2 * CPT; gq < (h + 1) * 2 * CPT; ++gq) {     // 16-query groups
+            for (int gq = 2 * h; gq < 2 * h + 2; ++gq) {     // 16-query groups
                 uint32_t rs[16], rp[16];
                 tmem_ld16(tl + tS + gq * 16, rs);
                 tmem_ld16(tl + tP + gq * 16, rp);
                 tmem_ld_wait();
                 uint32_t ph[8], pl[8], gh[8], gl[8];
+                if (kPacked && all) {
 #pragma unroll
-                for (int k = 0; k < 16; k += 2) {
-                    float pv[2], gv[2];
-#pragma unroll
-                    for (int t = 0; t < 2; ++t) {
-                        const float4 m = qi[gq * 16 + k + t];
-                        const bool v = all || (kv && kpos <= __float_as_int(m.w));
-                        const float u = __fmaf_rn(s.am1, clamp_score(__uint_as_float(rs[k + t]), s.scale), -m.x);
-                        pv[t] = v ? entmax_pk<PINV>(u, s.pinv.e) * m.y : 0.0f;
-                        gv[t] = v ? grad_pk<PE2>(u, s.pe2.e, __uint_as_float(rp[k + t]), m.z, m.y) : 0.0f;
+                    for (int m = 0; m < 8; ++m) {
+                        const int qq = gq * 16 + 2 * m;
+                        const float2 ntau = *reinterpret_cast<const float2*>(qi + 0 * TILE + qq);
+                        const float2 ulo = *reinterpret_cast<const float2*>(qi + 1 * TILE + qq);
+                        const float2 uhi = *reinterpret_cast<const float2*>(qi + 2 * TILE + qq);
+                        const float2 iN = *reinterpret_cast<const float2*>(qi + 3 * TILE + qq);
+                        const float2 nD = *reinterpret_cast<const float2*>(qi + 4 * TILE + qq);
+                        float2 u = __ffma2_rn(make_float2(__uint_as_float(rs[2 * m]), __uint_as_float(rs[2 * m + 1])),
+                                              c1, ntau);
+                        u.x = fmaxf(fminf(u.x, uhi.x), ulo.x);
+                        u.y = fmaxf(fminf(u.y, uhi.y), ulo.y);
+                        const float2 up = make_float2(fmaxf(u.x, 0.0f), fmaxf(u.y, 0.0f));
+                        float2 pv;
+                        if constexpr (PINV == 1) pv = up;
+                        else if constexpr (PINV == 2) pv = __fmul2_rn(up, up);
+                        else { const float2 q2 = __fmul2_rn(up, up); pv = __fmul2_rn(q2, q2); }
+                        pv = __fmul2_rn(pv, iN);
+                        const float2 t = __fadd2_rn(make_float2(__uint_as_float(rp[2 * m]), __uint_as_float(rp[2 * m + 1])),
+                                                    nD);
+                        float2 g;
+                        if constexpr (PE2 == 5) g = t;
+                        else if constexpr (PE2 == 1) g = __fmul2_rn(u, t);
+                        else g = __fmul2_rn(__fmul2_rn(__fmul2_rn(u, u), u), t);
+                        g = __fmul2_rn(g, iN);
+                        g.x = (u.x > ASA_EPS && fabsf(g.x) < __int_as_float(0x7f800000)) ? g.x : 0.0f;
+                        g.y = (u.y > ASA_EPS && fabsf(g.y) < __int_as_float(0x7f800000)) ? g.y : 0.0f;
+                        split_pair(pv, ph[m], pl[m]);
+                        split_pair(g, gh[m], gl[m]);
                     }
-                    const __nv_bfloat162 a = __floats2bfloat162_rn(pv[0], pv[1]);
-                    const __nv_bfloat162 c2 = __floats2bfloat162_rn(gv[0], gv[1]);
-                    const float2 af = __bfloat1622float2(a), cf = __bfloat1622float2(c2);
-                    ph[k >> 1] = *reinterpret_cast<const uint32_t*>(&a);
-                    gh[k >> 1] = *reinterpret_cast<const uint32_t*>(&c2);
-                    pl[k >> 1] = pack_bf16(pv[0] - af.x, pv[1] - af.y);
-                    gl[k >> 1] = pack_bf16(gv[0] - cf.x, gv[1] - cf.y);
+                } else {
+#pragma unroll
+                    for (int k = 0; k < 16; k += 2) {
+                        float pv[2], gv[2];
+#pragma unroll
+                        for (int t = 0; t < 2; ++t) {
+                            const int qq = gq * 16 + k + t;
+                            const bool v = all || (kv && kpos <= __float_as_int(qi[5 * TILE + qq]));
+                            const float u = __fmaf_rn(s.am1, clamp_score(__uint_as_float(rs[k + t]), s.scale),
+                                                      qi[0 * TILE + qq]);
+                            const float iN = qi[3 * TILE + qq];
+                            pv[t] = v ? entmax_pk<PINV>(u, s.pinv.e) * iN : 0.0f;
+                            gv[t] = v ? grad_pk<PE2>(u, s.pe2.e, __uint_as_float(rp[k + t]), -qi[4 * TILE + qq], iN)
+                                      : 0.0f;
+                        }
+                        split_pair(make_float2(pv[0], pv[1]), ph[k >> 1], pl[k >> 1]);
+                        split_pair(make_float2(gv[0], gv[1]), gh[k >> 1], gl[k >> 1]);
+                    }
                 }
                 tmem_st8(tl + tS + gq * 16, ph);
                 if (split) tmem_st8(tl + tS + gq * 16 + 8, pl);
@@ -1638,7 +1675,7 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
             const float mul = part == 0 ? 1.0f : s.scale;
             const uint32_t col0 = part == 0 ? tV : tK;
 #pragma unroll 1
-            for (int c = h; c < D / 32; c += NWG) {
+            for (int c = h; c < D / 32; c += DKV_NW) {
                 uint32_t r[32];
                 if (T > 0) {
                     tmem_ld32(tl + col0 + c * 32, r);
@@ -1745,7 +1782,7 @@ cudaError_t prep(F* f, size_t smem) {
 }
 
 constexpr size_t kSmemTail = 24 * 8 + 16 + (NWG + 1) * 128 * 4 + 64;  // barriers, TMEM holder, per-row arrays
-constexpr size_t kSmemTailBwd = 16 * 8 + 16 + 2 * 128 * 16 + 128 * 4;  // + per-query float4 x2
+constexpr size_t kSmemTailBwd = 16 * 8 + 16 + 2 * 6 * 128 * 4 + 128 * 4;  // + per-query arrays x2
 
 bool is_sm100() {
     static int cached = -1;
@@ -1963,7 +2000,7 @@ cudaError_t tc_launch_dkdv(const Shape& s, const BwdArgs& a, cudaStream_t st) {
             const size_t smem = bwd_smem<TO>(s, D);
             cudaError_t r = prep(kkv, smem);
             if (r != cudaSuccess) return r;
-            kkv<<<dim3(s.nKB, s.BH), NTHREADS, smem, st>>>(a.mQ, a.mK, a.mV, a.mdO, s, a.Qidx, a.Kidx, a.bd,
+            kkv<<<dim3(s.nKB, s.BH), DKV_THREADS, smem, st>>>(a.mQ, a.mK, a.mV, a.mdO, s, a.Qidx, a.Kidx, a.bd,
                                                           a.tau, a.invNv, a.Dq, a.cptr, a.cidx, (TO*)a.dK,
                                                           (TO*)a.dV, split, a.err);
             note_launch();
