@@ -64,7 +64,8 @@ constexpr int DQ_EPI0 = 96;                // dQ: producer, S/dP-issuer and dQ-i
 constexpr int DQ_THREADS = DQ_EPI0 + DQ_NE;
 constexpr int DKV_NW = 4;                  // dK/dV: epilogue warpgroups (32 queries of a tile each)
 constexpr int DKV_NE = 128 * DKV_NW;
-constexpr int DKV_THREADS = 64 + DKV_NE;
+constexpr int DKV_EPI0 = 96;               // dK/dV: producer, S/dP-issuer and dV/dK-issuer warps first
+constexpr int DKV_THREADS = DKV_EPI0 + DKV_NE;
 
 
 // Dynamic shared memory starts at the bottom of the CTA's window (these
@@ -1425,8 +1426,13 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
         const float* __restrict__ tau, const float* __restrict__ invNv, const float* __restrict__ Dqv,
         const int32_t* __restrict__ cptr, const int32_t* __restrict__ cidx, TO* __restrict__ dK,
         TO* __restrict__ dV, int split, int* err) {
+    // Each 128-query tile is handled as two 64-query halves with their own
+    // TMEM buffers (S^T 64 columns + dP^T 64 columns each, P^T / dS^T written
+    // back over them), so the tensor pipe computes one half's S^T/dP^T while
+    // the epilogue works on the other and the dV/dK MMAs drain a third.
     constexpr int SQ = 2;                     // Q / dO stages
     constexpr int TB = D * TILE * 2;
+    constexpr int HQ = TILE / 2;              // queries per half
     extern __shared__ uint8_t smem_raw[];
     CTA_MARK(3, 0);
     uint8_t* base = align1024(smem_raw, err);
@@ -1438,10 +1444,10 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
     uint64_t* kv_full = bars;
     uint64_t* q_full = bars + 1;              // [SQ]
     uint64_t* q_empty = q_full + SQ;          // [SQ]
-    uint64_t* sd_full = q_empty + SQ;
-    uint64_t* pd_full = sd_full + 1;
-    uint64_t* pd_free = pd_full + 1;
-    uint64_t* out_full = pd_free + 1;
+    uint64_t* sd_full = q_empty + SQ;         // [2] per half buffer
+    uint64_t* pd_full = sd_full + 2;          // [2]
+    uint64_t* pd_free = pd_full + 2;          // [2]
+    uint64_t* out_full = pd_free + 2;
     uint32_t* holder = reinterpret_cast<uint32_t*>(bars + 16);
     // per query of the current (and next) block, one array each (pairs load
     // as float2): -τ, lower and upper u bound, 1/n, -D, position
@@ -1461,21 +1467,22 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
     if (threadIdx.x == 0) {
         mbar_init(kv_full, 1);
         for (int i = 0; i < SQ; ++i) { mbar_init(&q_full[i], 1); mbar_init(&q_empty[i], 1); }
-        mbar_init(sd_full, 1);
-        mbar_init(pd_full, DKV_NE / 32);
-        mbar_init(pd_free, 1);
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&sd_full[i], 1); mbar_init(&pd_full[i], DKV_NE / 32); mbar_init(&pd_free[i], 1);
+        }
         mbar_init(out_full, 1);
         fence_barrier_init();
     }
     if (warp == 1) { tmem_alloc(holder, 512); tmem_relinquish(); }
-    if (threadIdx.x >= EPI0 && threadIdx.x < EPI0 + NEPI)
-        sched_from_list(sched, list + e0, T, s, bd, bh, kb, true, threadIdx.x - EPI0);
+    if (threadIdx.x >= DKV_EPI0 && threadIdx.x < DKV_EPI0 + NEPI)
+        sched_from_list(sched, list + e0, T, s, bd, bh, kb, true, threadIdx.x - DKV_EPI0);
     tc_fence_before();
     __syncthreads();
     CTA_MARK(3, 1);
     tc_fence_after();
     const uint32_t tbase = *holder;
-    constexpr uint32_t tS = 0, tP = 128, tV = 256, tK = 256 + D;
+    // half buffer hb: S^T at 128*hb, dP^T at 128*hb + 64; then dV, dK
+    constexpr uint32_t tV = 256, tK = 256 + D;
 
     if (warp == 0) {
         if (lane == 0 && T > 0) {
@@ -1491,8 +1498,8 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
             }
         }
     } else if (warp == 1) {
-        constexpr uint32_t idS = idesc_bf16(128, 128, 0, 0);
-        constexpr uint32_t idO = idesc_bf16(128, D, 0, 1);
+        // S^T = K·Q^T and dP^T = V·dO^T per half (N = 64 queries)
+        constexpr uint32_t idS = idesc_bf16(128, HQ, 0, 0);
         int loads = 0;
         bool dirty = true;   // K/V not loaded yet
         for (int i = 0; i < T; ++i) {
@@ -1501,8 +1508,11 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
             const bool fix = (e & SCHED_FIX) != 0;
             const int st = i % SQ;
             if (dirty || fix) {
-                // (re)load pristine K/V once the previous pair's S/dP MMAs are done
-                if (i > 0) mbar_wait(sd_full, (i - 1) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+                // (re)load pristine K/V once the previous tile's S/dP MMAs are done
+                if (i > 0) {
+                    mbar_wait(&sd_full[0], (i - 1) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+                    mbar_wait(&sd_full[1], (i - 1) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+                }
                 if (lane == 0) {
                     mbar_expect_tx(kv_full, 2 * TB);
                     for (int bx = 0; bx < D / BOX; ++bx) {
@@ -1527,46 +1537,70 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
             }
             __syncwarp();
             mbar_wait(&q_full[st], (i / SQ) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
-            mbar_wait(pd_free, (i & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
-            tc_fence_after();
             const uint8_t* qt = sQ + st * TB;
             const uint8_t* ot = sdO + st * TB;
-            if (lane == 0) {
+            const uint64_t dKd = kdesc(sK, 0), dVd = kdesc(sV, 0);
+#pragma unroll 1
+            for (int hb = 0; hb < 2; ++hb) {
+                mbar_wait(&pd_free[hb], (i & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+                if (lane == 0 && hb == 0) TRACE(1, i, 1);
+                tc_fence_after();
+                if (lane == 0) {
+                    const uint64_t dQh = kdesc(qt + hb * HQ * 128, 0), dOh = kdesc(ot + hb * HQ * 128, 0);
 #pragma unroll
-                for (int kk = 0; kk < D / 16; ++kk) {
-                    mma_bf16_ss(tbase + tS, kdesc(sK, kk), kdesc(qt, kk), idS, kk > 0);
-                    mma_bf16_ss(tbase + tP, kdesc(sV, kk), kdesc(ot, kk), idS, kk > 0);
-                }
-                mma_commit(sd_full);
-            }
-            __syncwarp();
-            mbar_wait(pd_full, i & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
-            tc_fence_after();
-            if (lane == 0) {
-#pragma unroll
-                for (int kk = 0; kk < TILE / 16; ++kk) {
-                    mma_bf16_ts(tbase + tV, tbase + tS + pair_col(kk, false), mndesc(ot, kk), idO, (i > 0 || kk > 0));
-                    mma_bf16_ts(tbase + tK, tbase + tP + pair_col(kk, false), mndesc(qt, kk), idO, (i > 0 || kk > 0));
-                }
-                if (split) {
-#pragma unroll
-                    for (int kk = 0; kk < TILE / 16; ++kk) {
-                        mma_bf16_ts(tbase + tV, tbase + tS + pair_col(kk, true), mndesc(ot, kk), idO, 1);
-                        mma_bf16_ts(tbase + tK, tbase + tP + pair_col(kk, true), mndesc(qt, kk), idO, 1);
+                    for (int kk = 0; kk < D / 16; ++kk) {
+                        mma_bf16_ss(tbase + 128 * hb, kdesc_step(dKd, kk), kdesc_step(dQh, kk), idS, kk > 0);
+                        mma_bf16_ss(tbase + 128 * hb + 64, kdesc_step(dVd, kk), kdesc_step(dOh, kk), idS, kk > 0);
                     }
+                    mma_commit(&sd_full[hb]);
+                    if (hb == 1) TRACE(1, i, 2);
                 }
-                mma_commit(pd_free);
-                mma_commit(&q_empty[st]);
+                __syncwarp();
             }
-            __syncwarp();
+        }
+    } else if (warp == 2) {
+        // dV += P^T·dO and dK += dS^T·Q per half (K = the half's 64 queries),
+        // in tile order: deterministic sums
+        constexpr uint32_t idO = idesc_bf16(128, D, 0, 1);
+        for (int i = 0; i < T; ++i) {
+            const int st = i % SQ;
+            const uint8_t* qt = sQ + st * TB;
+            const uint8_t* ot = sdO + st * TB;
+            const uint64_t dOd = mndesc(ot, 0), dQd = mndesc(qt, 0);
+#pragma unroll 1
+            for (int hb = 0; hb < 2; ++hb) {
+                mbar_wait(&pd_full[hb], i & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+                if (lane == 0 && hb == 0) TRACE(1, i, 3);
+                tc_fence_after();
+                if (lane == 0) {
+                    const uint32_t cS = tbase + 128 * hb, cP = cS + 64;
+#pragma unroll
+                    for (int k4 = 0; k4 < HQ / 16; ++k4) {
+                        const int kk = hb * (HQ / 16) + k4;
+                        const bool acc = i > 0 || kk > 0;
+                        mma_bf16_ts(tbase + tV, cS + pair_col(k4, false), mndesc_step(dOd, kk), idO, acc);
+                        mma_bf16_ts(tbase + tK, cP + pair_col(k4, false), mndesc_step(dQd, kk), idO, acc);
+                    }
+                    if (split) {
+#pragma unroll
+                        for (int k4 = 0; k4 < HQ / 16; ++k4) {
+                            const int kk = hb * (HQ / 16) + k4;
+                            mma_bf16_ts(tbase + tV, cS + pair_col(k4, true), mndesc_step(dOd, kk), idO, 1);
+                            mma_bf16_ts(tbase + tK, cP + pair_col(k4, true), mndesc_step(dQd, kk), idO, 1);
+                        }
+                    }
+                    mma_commit(&pd_free[hb]);
+                    if (hb == 1) { mma_commit(&q_empty[st]); TRACE(1, i, 4); }
+                }
+                __syncwarp();
+            }
         }
         if (lane == 0) mma_commit(out_full);
         __syncwarp();
     } else {
-        // DKV_NW warpgroups; warpgroup h owns queries [32h, 32h+32) of every
-        // query tile (two 16-query groups)
+        // DKV_NW warpgroups; in each half warpgroup h owns one 16-query group
         const int row = (warp & 3) * 32 + lane;
-        const int et = threadIdx.x - EPI0;
+        const int et = threadIdx.x - DKV_EPI0;
         const int h = et / TILE;
         const int kn = kb * TILE + row;
         const bool kv = kn < s.NK;
@@ -1575,8 +1609,8 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
         const uint32_t tl = tmem_lane_base(tbase, warp);
         constexpr bool kPacked = (PINV == 1 || PINV == 2 || PINV == 4) && (PE2 == 1 || PE2 == 3 || PE2 == 5);
         const float2 c1 = make_float2(__fmul_rn(s.am1, s.scale), __fmul_rn(s.am1, s.scale));
-        // Query-block metadata of pair i lives in qinfo[i & 1]; it is fetched
-        // one pair ahead so its global loads overlap the previous pair.
+        // Query-block metadata of tile i lives in qinfo[i & 1]; it is fetched
+        // one tile ahead so its global loads overlap the previous tile.
         auto fetch = [&](int i, float* dst) {
             const int qb = (int)(sched[i] & SCHED_IDX);
             const int q = qb * TILE + et;
@@ -1593,17 +1627,20 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
         if (T > 0 && et < TILE) fetch(0, qinfo);
         for (int i = 0; i < T; ++i) {
             const uint32_t e = sched[i];
-            asm volatile("bar.sync 2, %0;" ::"n"(DKV_NE) : "memory");   // qinfo[i&1] written; pair i-1 done
+            asm volatile("bar.sync 2, %0;" ::"n"(DKV_NE) : "memory");   // qinfo[i&1] written; tile i-1 done
             if (i + 1 < T && et < TILE) fetch(i + 1, qinfo + ((i + 1) & 1) * 6 * TILE);
             const float* qi = qinfo + (i & 1) * 6 * TILE;
             const bool all = kv && (e & SCHED_ALL) != 0;
-            mbar_wait(sd_full, i & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
-            tc_fence_after();
 #pragma unroll 1
-            for (int gq = 2 * h; gq < 2 * h + 2; ++gq) {     // 16-query groups
+            for (int hb = 0; hb < 2; ++hb) {
+                const int gq = hb * 4 + h;            // 16-query group of the tile
+                const uint32_t cS = 128 * hb, cP = cS + 64;
+                mbar_wait(&sd_full[hb], i & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+                if (et == 0 && hb == 0) TRACE(2, i, 0);
+                tc_fence_after();
                 uint32_t rs[16], rp[16];
-                tmem_ld16(tl + tS + gq * 16, rs);
-                tmem_ld16(tl + tP + gq * 16, rp);
+                tmem_ld16(tl + cS + h * 16, rs);
+                tmem_ld16(tl + cP + h * 16, rp);
                 tmem_ld_wait();
                 uint32_t ph[8], pl[8], gh[8], gl[8];
                 if (kPacked && all) {
@@ -1656,14 +1693,15 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
                         split_pair(make_float2(gv[0], gv[1]), gh[k >> 1], gl[k >> 1]);
                     }
                 }
-                tmem_st8(tl + tS + gq * 16, ph);
-                if (split) tmem_st8(tl + tS + gq * 16 + 8, pl);
-                tmem_st8(tl + tP + gq * 16, gh);
-                if (split) tmem_st8(tl + tP + gq * 16 + 8, gl);
+                tmem_st8(tl + cS + h * 16, ph);
+                if (split) tmem_st8(tl + cS + h * 16 + 8, pl);
+                tmem_st8(tl + cP + h * 16, gh);
+                if (split) tmem_st8(tl + cP + h * 16 + 8, gl);
+                tmem_st_wait();
+                tc_fence_before();
+                epi_arrive(&pd_full[hb]);
+                if (et == 0 && hb == 1) TRACE(2, i, 1);
             }
-            tmem_st_wait();
-            tc_fence_before();
-            epi_arrive(pd_full);
         }
         if (T > 0) {
             mbar_wait(out_full, 0, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
