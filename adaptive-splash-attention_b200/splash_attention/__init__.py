@@ -21,11 +21,12 @@ import torch
 from . import _lib
 from .ops import Settings, forward_saved, backward_saved, tau_mask, scrub_, device_error, \
     resolved_backend, make_params
+from .streamed import forward_backward_host
 
 _lib.lib()  # fail at import time if the native library is missing
 
 __all__ = ["AdaptiveSplashAttention", "splash_attention", "forward", "backward", "tau_mask",
-           "Settings", "device_error"]
+           "Settings", "device_error", "forward_backward_host"]
 
 # Reference compile-time defaults (adasplashattention.cu:8-19).
 REF_BLOCK_M, REF_BLOCK_N, REF_K_KEEP = 32, 64, 8
