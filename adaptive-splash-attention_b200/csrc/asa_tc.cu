@@ -1449,8 +1449,9 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
     uint64_t* pd_free = pd_full + 2;          // [2]
     uint64_t* out_full = pd_free + 2;
     uint32_t* holder = reinterpret_cast<uint32_t*>(bars + 16);
-    // per query of the current (and next) block, one array each (pairs load
-    // as float2): -τ, lower and upper u bound, 1/n, -D, position
+    // per query of the current (and next) block: query pairs as float4
+    // (-τ, -τ', max(lo, 0), max(lo', 0)) and (hi, hi', 1/n, 1/n') with lo/hi
+    // the u bounds of the score clamp, then -D and the position per query
     float* qinfo = reinterpret_cast<float*>(holder + 4);     // [2][6][128]
     int* qidx_blk = reinterpret_cast<int*>(qinfo + 2 * 6 * TILE); // [128] for the tile-load fix
     uint32_t* sched = reinterpret_cast<uint32_t*>(qidx_blk + TILE);   // [T]
@@ -1617,12 +1618,13 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
             const bool ok = q < s.NQ;
             const size_t r = (size_t)bh * s.NQ + (ok ? q : 0);
             const float tq = ok ? tau[r] : 0.0f;
-            dst[0 * TILE + et] = -tq;
-            dst[1 * TILE + et] = __fmaf_rn(s.am1, -10.0f, -tq);
-            dst[2 * TILE + et] = __fmaf_rn(s.am1, 10.0f, -tq);
-            dst[3 * TILE + et] = ok ? invNv[r] : 0.0f;
-            dst[4 * TILE + et] = ok ? -Dqv[r] : 0.0f;
-            dst[5 * TILE + et] = __int_as_float(ok ? (s.causal ? Qidx_bh[q] : INT_MAX) : INT_MIN);
+            const int pq = (et >> 1) * 4 + (et & 1);
+            dst[pq] = -tq;
+            dst[pq + 2] = fmaxf(__fmaf_rn(s.am1, -10.0f, -tq), 0.0f);
+            dst[256 + pq] = __fmaf_rn(s.am1, 10.0f, -tq);
+            dst[256 + pq + 2] = ok ? invNv[r] : 0.0f;
+            dst[512 + et] = ok ? -Dqv[r] : 0.0f;
+            dst[640 + et] = __int_as_float(ok ? (s.causal ? Qidx_bh[q] : INT_MAX) : INT_MIN);
         };
         if (T > 0 && et < TILE) fetch(0, qinfo);
         for (int i = 0; i < T; ++i) {
@@ -1647,16 +1649,18 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
 #pragma unroll
                     for (int m = 0; m < 8; ++m) {
                         const int qq = gq * 16 + 2 * m;
-                        const float2 ntau = *reinterpret_cast<const float2*>(qi + 0 * TILE + qq);
-                        const float2 ulo = *reinterpret_cast<const float2*>(qi + 1 * TILE + qq);
-                        const float2 uhi = *reinterpret_cast<const float2*>(qi + 2 * TILE + qq);
-                        const float2 iN = *reinterpret_cast<const float2*>(qi + 3 * TILE + qq);
-                        const float2 nD = *reinterpret_cast<const float2*>(qi + 4 * TILE + qq);
+                        // pair of queries: (-τ, -τ', max(lo,0), max(lo',0)), (hi, hi', 1/n, 1/n')
+                        const float4 qa = *reinterpret_cast<const float4*>(qi + (qq >> 1) * 4);
+                        const float4 qb4 = *reinterpret_cast<const float4*>(qi + 256 + (qq >> 1) * 4);
+                        const float2 nD = *reinterpret_cast<const float2*>(qi + 512 + qq);
+                        const float2 iN = make_float2(qb4.z, qb4.w);
                         float2 u = __ffma2_rn(make_float2(__uint_as_float(rs[2 * m]), __uint_as_float(rs[2 * m + 1])),
-                                              c1, ntau);
-                        u.x = fmaxf(fminf(u.x, uhi.x), ulo.x);
-                        u.y = fmaxf(fminf(u.y, uhi.y), ulo.y);
-                        const float2 up = make_float2(fmaxf(u.x, 0.0f), fmaxf(u.y, 0.0f));
+                                              c1, make_float2(qa.x, qa.y));
+                        // clamp to [max(lo, 0), hi]: below 0 both the weight and the
+                        // gradient are 0, so the floor at 0 also gives max(u, 0)
+                        u.x = fmaxf(fminf(u.x, qb4.x), qa.z);
+                        u.y = fmaxf(fminf(u.y, qb4.y), qa.w);
+                        const float2 up = u;
                         float2 pv;
                         if constexpr (PINV == 1) pv = up;
                         else if constexpr (PINV == 2) pv = __fmul2_rn(up, up);
@@ -1681,12 +1685,12 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
 #pragma unroll
                         for (int t = 0; t < 2; ++t) {
                             const int qq = gq * 16 + k + t;
-                            const bool v = all || (kv && kpos <= __float_as_int(qi[5 * TILE + qq]));
+                            const bool v = all || (kv && kpos <= __float_as_int(qi[640 + qq]));
                             const float u = __fmaf_rn(s.am1, clamp_score(__uint_as_float(rs[k + t]), s.scale),
-                                                      qi[0 * TILE + qq]);
-                            const float iN = qi[3 * TILE + qq];
+                                                      qi[(qq >> 1) * 4 + (qq & 1)]);
+                            const float iN = qi[256 + (qq >> 1) * 4 + 2 + (qq & 1)];
                             pv[t] = v ? entmax_pk<PINV>(u, s.pinv.e) * iN : 0.0f;
-                            gv[t] = v ? grad_pk<PE2>(u, s.pe2.e, __uint_as_float(rp[k + t]), -qi[4 * TILE + qq], iN)
+                            gv[t] = v ? grad_pk<PE2>(u, s.pe2.e, __uint_as_float(rp[k + t]), -qi[512 + qq], iN)
                                       : 0.0f;
                         }
                         split_pair(make_float2(pv[0], pv[1]), ph[k >> 1], pl[k >> 1]);

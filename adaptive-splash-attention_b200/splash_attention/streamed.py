@@ -6,12 +6,15 @@ inputs are copied in on one stream while chunk c-1 computes on a second and
 chunk c-2's outputs are copied out on a third.  The results equal those of
 the device API on the whole batch; only the copies move.
 """
+import ctypes
+
 import torch
 
-from .ops import Settings, forward_saved, backward_saved
+from . import _lib as L
+from .ops import Settings, make_params, _workspace, _ptr, _torch_dtype
 
 
-def forward_backward_host(Q, K, V, dO, Q_idx=None, K_idx=None, out=None, heads_per_chunk=8,
+def forward_backward_host(Q, K, V, dO, Q_idx=None, K_idx=None, out=None, heads_per_chunk=4,
                           slots=3, synchronize=True, **settings):
     """Q, K, V, dO: pinned host tensors [B, H, N, d] (bfloat16 or float32).
     Q_idx / K_idx: positions [B*H, N] (host or device; [N] broadcasts).
@@ -51,33 +54,73 @@ def forward_backward_host(Q, K, V, dO, Q_idx=None, K_idx=None, out=None, heads_p
         s_.wait_stream(main)
     hc = max(1, min(heads_per_chunk, BH))
     chunks = [(c0, min(c0 + hc, BH)) for c0 in range(0, BH, hc)]
-    bufs = [tuple(torch.empty(hc, n, d, device=dev, dtype=Q.dtype) for n in (NQ, NK, NK, NQ))
-            for _ in range(min(slots, len(chunks)))]
-    comp_done = []
+    nslots = min(slots, len(chunks))
+    # Everything a chunk needs is allocated once per slot, and the C ABI is
+    # called directly: per chunk the host only enqueues copies and two calls.
+    params = {}
+
+    def chunk_params(n):
+        if n not in params:
+            shp_q = torch.empty(1, n, NQ, d, device="meta", dtype=Q.dtype)
+            shp_k = torch.empty(1, n, NK, d, device="meta", dtype=Q.dtype)
+            p = make_params(shp_q, shp_k, st)
+            params[n] = (p, _workspace(p, dev))
+        return params[n]
+
+    p_full, (fwd_b, bwd_b) = chunk_params(hc)
+    out_dt = _torch_dtype(p_full.out_dtype)
+    nqb, nkb = -(-NQ // p_full.block_m), -(-NK // p_full.block_n)
+
+    def slot_buffers():
+        e = lambda *shape, dt=torch.float32: torch.empty(*shape, device=dev, dtype=dt)
+        return dict(q=e(hc, NQ, d, dt=Q.dtype), k=e(hc, NK, d, dt=Q.dtype), v=e(hc, NK, d, dt=Q.dtype),
+                    do=e(hc, NQ, d, dt=Q.dtype), O=e(hc, NQ, d, dt=out_dt),
+                    O32=e(hc, NQ, d) if out_dt != torch.float32 else None,
+                    tau=e(hc, NQ), M=e(hc, nqb, nkb, dt=torch.uint8), ptr=e(hc, nqb + 1, dt=torch.int32),
+                    idx=e(hc, nqb * nkb, dt=torch.int32), rn=e(hc, NQ),
+                    dQ=e(hc, NQ, d, dt=out_dt), dK=e(hc, NK, d, dt=out_dt), dV=e(hc, NK, d, dt=out_dt),
+                    wf=e(fwd_b, dt=torch.uint8), wb=e(bwd_b, dt=torch.uint8))
+
+    bufs = [slot_buffers() for _ in range(nslots)]
+    lib = L.lib()
+    comp_stream = ctypes.c_void_p(s_comp.cuda_stream)
+    comp_done, out_done = [], []
     for c, (a, b) in enumerate(chunks):
         n = b - a
-        slot = bufs[c % len(bufs)]
+        B_ = bufs[c % nslots]
+        p, (fwd_n, bwd_n) = chunk_params(n)
         with torch.cuda.stream(s_in):
-            if c >= len(bufs):
-                s_in.wait_event(comp_done[c - len(bufs)])     # this slot's inputs consumed
-            for dst, src in zip(slot, (hq, hk, hv, hdo)):
-                dst[:n].copy_(src[a:b], non_blocking=True)
+            if c >= nslots:
+                s_in.wait_event(comp_done[c - nslots])     # this slot is free again
+            for key, src in (("q", hq), ("k", hk), ("v", hv), ("do", hdo)):
+                B_[key][:n].copy_(src[a:b], non_blocking=True)
             ev_in = torch.cuda.Event()
             ev_in.record(s_in)
-        with torch.cuda.stream(s_comp):
-            s_comp.wait_event(ev_in)
-            q, k, v, do = (x[:n].unsqueeze(0) for x in slot)
-            O, saved = forward_saved(q, k, v, qi[a:b] if qi is not None else None,
-                                     ki[a:b] if ki is not None else None, st)
-            dQ, dK, dV = backward_saved(q, k, v, do, saved)
-            ev_c = torch.cuda.Event()
-            ev_c.record(s_comp)
-            comp_done.append(ev_c)
+        s_comp.wait_event(ev_in)
+        if c >= nslots:
+            s_comp.wait_event(out_done[c - nslots])       # this slot's outputs copied out
+        pq = _ptr(qi[a:b]) if qi is not None else None
+        pk = _ptr(ki[a:b]) if ki is not None else None
+        O32 = B_["O32"] if B_["O32"] is not None else B_["O"]
+        L.check(lib.asa_forward(ctypes.byref(p), _ptr(B_["q"]), _ptr(B_["k"]), _ptr(B_["v"]), pq, pk,
+                                _ptr(B_["O"]), _ptr(O32), _ptr(B_["tau"]), _ptr(B_["M"]), _ptr(B_["ptr"]),
+                                _ptr(B_["idx"]), _ptr(B_["rn"]), _ptr(B_["wf"]), fwd_n, comp_stream),
+                "asa_forward")
+        L.check(lib.asa_backward(ctypes.byref(p), _ptr(B_["q"]), _ptr(B_["k"]), _ptr(B_["v"]), pq, pk,
+                                 _ptr(O32), _ptr(B_["tau"]), _ptr(B_["M"]), _ptr(B_["ptr"]), _ptr(B_["idx"]),
+                                 _ptr(B_["rn"]), _ptr(B_["do"]), _ptr(B_["dQ"]), _ptr(B_["dK"]),
+                                 _ptr(B_["dV"]), _ptr(B_["wb"]), bwd_n, comp_stream),
+                "asa_backward")
+        ev_c = torch.cuda.Event()
+        ev_c.record(s_comp)
+        comp_done.append(ev_c)
         with torch.cuda.stream(s_out):
             s_out.wait_event(ev_c)
-            for dst, src in zip((hO, hdQ, hdK, hdV), (O, dQ, dK, dV)):
-                src.record_stream(s_out)
-                dst[a:b].copy_(src.reshape(n, src.shape[2], d), non_blocking=True)
+            for dst, key in ((hO, "O"), (hdQ, "dQ"), (hdK, "dK"), (hdV, "dV")):
+                dst[a:b].copy_(B_[key][:n], non_blocking=True)
+            ev_o = torch.cuda.Event()
+            ev_o.record(s_out)
+            out_done.append(ev_o)
     main.wait_stream(s_out)
     main.wait_stream(s_in)
     main.wait_stream(s_comp)

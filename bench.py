@@ -218,7 +218,7 @@ def main():
     ap.add_argument("--precision", default="split")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--e2e-chunk", type=int, default=8, help="heads per chunk in the e2e leg")
+    ap.add_argument("--e2e-chunk", type=int, default=4, help="heads per chunk in the e2e leg")
     a = ap.parse_args()
     c = dict(CONFIGS[a.config])
     rank = int(os.environ.get("RANK", 0))
