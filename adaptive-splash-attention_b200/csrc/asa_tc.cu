@@ -1124,6 +1124,7 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
     tc_fence_before();
     __syncthreads();
     CTA_MARK(1, 2);
+    if (threadIdx.x == 0) g_cta_n(1, T);
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tbase, 512);
@@ -1396,6 +1397,7 @@ k4_dq(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
     tc_fence_before();
     __syncthreads();
     CTA_MARK(2, 2);
+    if (threadIdx.x == 0) g_cta_n(2, T);
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tbase, 512);
@@ -1737,6 +1739,7 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
     tc_fence_before();
     __syncthreads();
     CTA_MARK(3, 2);
+    if (threadIdx.x == 0) g_cta_n(3, T);
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tbase, 512);
