@@ -779,6 +779,33 @@ k1_tau_mask(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
     }
 }
 
+// Coalesced store of a warp's 32 rows x 32 columns (lane i holds row i's
+// values o[0..31]) through 4 KB of shared staging: row-per-lane stores write
+// 32 different lines per instruction, partial sectors that cost more than
+// the whole tile's MMAs.  Rows at or beyond nrows are skipped.
+template <typename TO>
+__device__ __forceinline__ void warp_store_rows(TO* base, int ld, int nrows, int col0, const float (&o)[32],
+                                                float* stage, int lane) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) stage[lane * 33 + i] = o[i];
+    __syncwarp();
+    if constexpr (sizeof(TO) == 4) {
+#pragma unroll 4
+        for (int r = 0; r < 32; ++r)
+            if (r < nrows) base[(size_t)r * ld + col0 + lane] = stage[r * 33 + lane];
+    } else {
+        const int cc = (lane & 15) * 2;
+#pragma unroll 4
+        for (int r2 = 0; r2 < 16; ++r2) {
+            const int r = 2 * r2 + (lane >> 4);
+            if (r < nrows)
+                *reinterpret_cast<uint32_t*>(base + (size_t)r * ld + col0 + cc) =
+                    pack_bf16(stage[r * 33 + cc], stage[r * 33 + cc + 1]);
+        }
+    }
+    __syncwarp();
+}
+
 // Store this thread's fp32 values o[0..31] (columns [32c, 32c+32) of `row`)
 // to a row-major [rows][D] output of type TO.
 template <int D, typename TO>
@@ -1010,6 +1037,7 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
             const bool all = (e & SCHED_ALL) != 0;
             const int b = j % NB;
             mbar_wait(&s_full[b], (j / NB) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+            if (et == 0 && j == 0) CTA_MARK_T(1, 3);
             if (et == 0) TRACE(2, j, 0);
             tc_fence_after();
 #ifdef ASA_EXP_F_NOEPI
@@ -1102,24 +1130,32 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
         }
         epi_bar();
         n = nsum[row];
+        if (et == 0) CTA_MARK_T(1, 4);
         mbar_wait(o_full, 0, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+        if (et == 0) CTA_MARK_T(1, 5);
         tc_fence_after();
         const float inv = __fdiv_rn(1.0f, __fadd_rn(n, ASA_EPS));
+        // every MMA is done: the K stages are free for the store staging
+        float* stage = reinterpret_cast<float*>(sK) + (et >> 5) * (32 * 33);
+        const int q0 = qb * TILE + (warp & 3) * 32;
+        const int nrows = min(32, s.NQ - q0);
+        const size_t row0 = (size_t)bh * s.NQ + q0;
 #pragma unroll 1
         for (int c = h; c < D / 32; c += NWG) {
             uint32_t r[32];
             tmem_ld32(tl + tO + c * 32, r);
             tmem_ld_wait();
-            if (!qv) continue;
+            if (nrows <= 0) continue;
             float o[32];
 #pragma unroll
             for (int i = 0; i < 32; ++i) {
                 float v = T > 0 ? __uint_as_float(r[i]) * inv : 0.0f;
                 o[i] = isfinite(v) ? v : 0.0f;
             }
-            if (O32) store_out32<D, float>(O32 + qrow * D, c, o);
-            if (sizeof(TO) == 2 || (void*)O != (void*)O32) store_out32<D, TO>(O + qrow * D, c, o);
+            if (O32) warp_store_rows<float>(O32 + row0 * D, D, nrows, c * 32, o, stage, lane);
+            if (sizeof(TO) == 2 || (void*)O != (void*)O32) warp_store_rows<TO>(O + row0 * D, D, nrows, c * 32, o, stage, lane);
         }
+        if (et == 0) CTA_MARK_T(1, 6);
     }
     tc_fence_before();
     __syncthreads();
@@ -1379,19 +1415,24 @@ k4_dq(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
         }
         mbar_wait(dq_full, 0, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
         tc_fence_after();
+        // every MMA is done: the Q/dO/K/V tiles are free for the store staging
+        float* stage = reinterpret_cast<float*>(sQ) + (et >> 5) * (32 * 33);
+        const int q0 = qb * TILE + (warp & 3) * 32;
+        const int nrows = min(32, s.NQ - q0);
+        const size_t row0 = (size_t)bh * s.NQ + q0;
 #pragma unroll 1
         for (int c = h; c < D / 32; c += DQ_NW) {
             uint32_t r[32];
             tmem_ld32(tl + tQ + c * 32, r);
             tmem_ld_wait();
-            if (!qv) continue;
+            if (nrows <= 0) continue;
             float o[32];
 #pragma unroll
             for (int i = 0; i < 32; ++i) {
                 float v = T > 0 ? __uint_as_float(r[i]) * s.scale : 0.0f;
                 o[i] = isfinite(v) ? v : 0.0f;
             }
-            store_out32<D, TO>(dQ + qrow * D, c, o);
+            warp_store_rows<TO>(dQ + row0 * D, D, nrows, c * 32, o, stage, lane);
         }
     }
     tc_fence_before();
@@ -1713,6 +1754,11 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
             mbar_wait(out_full, 0, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
             tc_fence_after();
         }
+        // every MMA is done: the K/V and Q/dO tiles are free for the store staging
+        float* stage = reinterpret_cast<float*>(sK) + (et >> 5) * (32 * 33);
+        const int k0 = kb * TILE + (warp & 3) * 32;
+        const int nrows = min(32, s.NK - k0);
+        const size_t row0 = (size_t)bh * s.NK + k0;
 #pragma unroll 1
         for (int part = 0; part < 2; ++part) {
             TO* dst_base = part == 0 ? dV : dK;
@@ -1725,14 +1771,14 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
                     tmem_ld32(tl + col0 + c * 32, r);
                     tmem_ld_wait();
                 }
-                if (!kv) continue;
+                if (nrows <= 0) continue;
                 float o[32];
 #pragma unroll
                 for (int k = 0; k < 32; ++k) {
                     float v = T > 0 ? __uint_as_float(r[k]) * mul : 0.0f;
                     o[k] = isfinite(v) ? v : 0.0f;
                 }
-                store_out32<D, TO>(dst_base + krow * D, c, o);
+                warp_store_rows<TO>(dst_base + row0 * D, D, nrows, c * 32, o, stage, lane);
             }
         }
     }
