@@ -98,3 +98,17 @@ def test_full_rows_mode_matches_oracle(cuda, dt, BM, BN, d):
     assert_tau(got["tau"], ref["tau"], tensor_core=got["backend"] == "tc")
     for k in ("O", "dQ", "dK", "dV"):
         assert_close(k, got[k], ref[k], OUT_ATOL[dt])
+
+
+def test_many_items_match_head_chunks(cuda):
+    # more (head, query block) items than SMs: the persistent forward walks
+    # several items per CTA; each head must equal the same head computed in a
+    # call small enough for one item per CTA (the kernels are deterministic)
+    Q, K, V, dO, Qi, Ki = make_inputs(1, 24, 1024, 1024, 128, seed=5, dtype=torch.bfloat16)
+    full = run_engine(Q, K, V, dO, Qi, Ki, 128, 128, 8, 1.5, 128 ** -0.5, True, "auto")
+    for h0 in range(0, 24, 6):
+        sl = slice(h0, h0 + 6)
+        part = run_engine(Q[:, sl], K[:, sl], V[:, sl], dO[:, sl], Qi[sl], Ki[sl], 128, 128, 8, 1.5,
+                          128 ** -0.5, True, "auto")
+        for k in ("O", "dQ", "dK", "dV", "tau", "rownorm"):
+            assert np.array_equal(full[k][sl], part[k]), (k, h0)
