@@ -522,6 +522,12 @@ k1_tau_mask(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
         for (int i = 0; i < S; ++i) { mbar_init(&k_full[i], 1); mbar_init(&k_empty[i], 1); }
         for (int i = 0; i < NB; ++i) { mbar_init(&s_full[i], 1); mbar_init(&s_free[i], NE / 32); }
         fence_barrier_init();
+        // Q does not depend on the schedule built below: issue it now
+        tma_prefetch_desc(&tmQ);
+        tma_prefetch_desc(&tmK);
+        mbar_expect_tx(q_full, TB);
+        for (int bx = 0; bx < D / BOX; ++bx)
+            tma_load_3d(sQ + bx * BOX_BYTES, &tmQ, q_full, bx * BOX, qb * TILE, bh);
     }
     if (warp == 1) { tmem_alloc(holder, 512); tmem_relinquish(); }
     if (threadIdx.x >= EPI0) {
@@ -547,11 +553,6 @@ k1_tau_mask(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
 
     if (warp == 0) {
         if (lane == 0 && T > 0) {
-            tma_prefetch_desc(&tmQ);
-            tma_prefetch_desc(&tmK);
-            mbar_expect_tx(q_full, TB);
-            for (int bx = 0; bx < D / BOX; ++bx)
-                tma_load_3d(sQ + bx * BOX_BYTES, &tmQ, q_full, bx * BOX, qb * TILE, bh);
             for (int j = 0; j < T; ++j) {
                 const int kb = (int)(sched[j] & SCHED_IDX);
                 const int st = j % S;
@@ -564,7 +565,7 @@ k1_tau_mask(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
         }
     } else if (warp == 1) {
         constexpr uint32_t idesc = idesc_bf16(128, 128, 0, 0);
-        if (T > 0) mbar_wait(q_full, 0, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+        mbar_wait(q_full, 0, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);   // issued at set-up even when T = 0
         if (lane == 0) CTA_MARK_T(0, 6);
         for (int j = 0; j < T; ++j) {
             const uint32_t e = sched[j];
@@ -887,6 +888,22 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
         }
         mbar_init(o_full, 1);
         fence_barrier_init();
+        if (T > 0) {
+            // Q and the first K/V tiles do not depend on the schedule being
+            // built below: issue them now so their latency hides the set-up
+            const int kb0 = list[e0];
+            tma_prefetch_desc(&tmQ);
+            tma_prefetch_desc(&tmK);
+            tma_prefetch_desc(&tmV);
+            mbar_expect_tx(q_full, TB);
+            mbar_expect_tx(&k_full[0], TB);
+            mbar_expect_tx(&v_full[0], TB);
+            for (int bx = 0; bx < D / BOX; ++bx) {
+                tma_load_3d(sQ + bx * BOX_BYTES, &tmQ, q_full, bx * BOX, qb * TILE, bh);
+                tma_load_3d(sK + bx * BOX_BYTES, &tmK, &k_full[0], bx * BOX, kb0 * TILE, bh);
+                tma_load_3d(sV + bx * BOX_BYTES, &tmV, &v_full[0], bx * BOX, kb0 * TILE, bh);
+            }
+        }
     }
     if (warp == 1) { tmem_alloc(holder, 512); tmem_relinquish(); }
     if (threadIdx.x >= K3_EPI0) {
@@ -905,13 +922,7 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
 
     if (warp == 0) {
         if (lane == 0 && T > 0) {
-            tma_prefetch_desc(&tmQ);
-            tma_prefetch_desc(&tmK);
-            tma_prefetch_desc(&tmV);
-            mbar_expect_tx(q_full, TB);
-            for (int bx = 0; bx < D / BOX; ++bx)
-                tma_load_3d(sQ + bx * BOX_BYTES, &tmQ, q_full, bx * BOX, qb * TILE, bh);
-            for (int j = 0; j < T; ++j) {
+            for (int j = 1; j < T; ++j) {   // Q and tile 0 were issued at set-up
                 const int kb = (int)(sched[j] & SCHED_IDX);
                 const int st = j % S;
                 mbar_wait(&k_empty[st], ((j / S) & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
@@ -937,7 +948,7 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
         else if (lane == 1 && T > 0) {
             // V runs on its own thread: its ring (freed after P·V) must not
             // hold back the K ring (freed after S)
-            for (int j = 0; j < T; ++j) {
+            for (int j = 1; j < T; ++j) {
                 const int kb = (int)(sched[j] & SCHED_IDX);
                 const int sv = j % SV;
                 mbar_wait(&v_empty[sv], ((j / SV) & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
@@ -1227,6 +1238,20 @@ k4_dq(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
         mbar_init(ds_free, 1);
         mbar_init(dq_full, 1);
         fence_barrier_init();
+        if (T > 0) {
+            // Q, dO and the first K/V tiles do not depend on the schedule
+            // built below: issue them now so their latency hides the set-up
+            const int kb0 = list[e0];
+            mbar_expect_tx(q_full, 2 * TB);
+            mbar_expect_tx(&k_full[0], TB);
+            mbar_expect_tx(&v_full[0], TB);
+            for (int bx = 0; bx < D / BOX; ++bx) {
+                tma_load_3d(sQ + bx * BOX_BYTES, &tmQ, q_full, bx * BOX, qb * TILE, bh);
+                tma_load_3d(sdO + bx * BOX_BYTES, &tmdO, q_full, bx * BOX, qb * TILE, bh);
+                tma_load_3d(sK + bx * BOX_BYTES, &tmK, &k_full[0], bx * BOX, kb0 * TILE, bh);
+                tma_load_3d(sV + bx * BOX_BYTES, &tmV, &v_full[0], bx * BOX, kb0 * TILE, bh);
+            }
+        }
     }
     if (warp == 1) { tmem_alloc(holder, 512); tmem_relinquish(); }
     if (threadIdx.x >= DQ_EPI0) {
@@ -1245,12 +1270,7 @@ k4_dq(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
 
     if (warp == 0) {
         if (lane == 0 && T > 0) {
-            mbar_expect_tx(q_full, 2 * TB);
-            for (int bx = 0; bx < D / BOX; ++bx) {
-                tma_load_3d(sQ + bx * BOX_BYTES, &tmQ, q_full, bx * BOX, qb * TILE, bh);
-                tma_load_3d(sdO + bx * BOX_BYTES, &tmdO, q_full, bx * BOX, qb * TILE, bh);
-            }
-            for (int j = 0; j < T; ++j) {
+            for (int j = 1; j < T; ++j) {   // Q, dO and tile 0 were issued at set-up
                 const int kb = (int)(sched[j] & SCHED_IDX);
                 const int st = j % SK;
                 mbar_wait(&k_empty[st], ((j / SK) & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
@@ -1261,7 +1281,7 @@ k4_dq(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
             }
         } else if (lane == 1 && T > 0) {
             // V (freed after dP) on its own thread, ahead of K (freed after dQ)
-            for (int j = 0; j < T; ++j) {
+            for (int j = 1; j < T; ++j) {
                 const int kb = (int)(sched[j] & SCHED_IDX);
                 const int st = j % SV;
                 mbar_wait(&v_empty[st], ((j / SV) & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
@@ -1516,6 +1536,15 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
         }
         mbar_init(out_full, 1);
         fence_barrier_init();
+        if (T > 0) {
+            // the first Q/dO tile does not depend on the schedule built below
+            const int qb0 = list[e0];
+            mbar_expect_tx(&q_full[0], 2 * TB);
+            for (int bx = 0; bx < D / BOX; ++bx) {
+                tma_load_3d(sQ + bx * BOX_BYTES, &tmQ, &q_full[0], bx * BOX, qb0 * TILE, bh);
+                tma_load_3d(sdO + bx * BOX_BYTES, &tmdO, &q_full[0], bx * BOX, qb0 * TILE, bh);
+            }
+        }
     }
     if (warp == 1) { tmem_alloc(holder, 512); tmem_relinquish(); }
     if (threadIdx.x >= DKV_EPI0 && threadIdx.x < DKV_EPI0 + NEPI)
@@ -1530,7 +1559,7 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
 
     if (warp == 0) {
         if (lane == 0 && T > 0) {
-            for (int i = 0; i < T; ++i) {
+            for (int i = 1; i < T; ++i) {   // tile 0 was issued at set-up
                 const int qb = (int)(sched[i] & SCHED_IDX);
                 const int st = i % SQ;
                 mbar_wait(&q_empty[st], ((i / SQ) & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
