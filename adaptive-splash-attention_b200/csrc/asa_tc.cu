@@ -204,14 +204,16 @@ __device__ __forceinline__ void fix_apply(uint4* p, uint32_t keep) {
     *p = make_uint4(w[0], w[1], w[2], w[3]);
 }
 
-template <int D>
+// Rows row0 + lane + 32*rr (rr < NR) of the tile; fix_tile: all 128 rows
+// by one warp.
+template <int D, int NR = TILE / 32>
 __device__ void fix_tile(uint8_t* tile, const int* qidx_blk, int qmin_blk,
-                         const int32_t* __restrict__ Kidx_bh, int kb, int NK, int lane) {
+                         const int32_t* __restrict__ Kidx_bh, int kb, int NK, int lane, int row0 = 0) {
     static_assert(D == 64 || D == 128, "staging windows assume D in {64, 128}");
-    int kp[TILE / 32];
+    int kp[NR];
 #pragma unroll
-    for (int rr = 0; rr < TILE / 32; ++rr) {     // independent loads: one latency for all rows
-        const int kn = kb * TILE + lane + 32 * rr;
+    for (int rr = 0; rr < NR; ++rr) {     // independent loads: one latency for all rows
+        const int kn = kb * TILE + row0 + lane + 32 * rr;
         kp[rr] = kn < NK ? __ldg(Kidx_bh + kn) : INT_MIN;
     }
     // Row r's staging queries for dims 0..D-1 are the contiguous window
@@ -223,8 +225,8 @@ __device__ void fix_tile(uint8_t* tile, const int* qidx_blk, int qmin_blk,
     const int qnext = lane < 31 ? qidx_blk[4 * lane + 4] : INT_MAX;
     const bool mono = __all_sync(0xffffffffu, q4.x <= q4.y && q4.y <= q4.z && q4.z <= q4.w && q4.w <= qnext);
 #pragma unroll
-    for (int rr = 0; rr < TILE / 32; ++rr) {
-        const int r = lane + 32 * rr;
+    for (int rr = 0; rr < NR; ++rr) {
+        const int r = row0 + lane + 32 * rr;
         const int kpos = kp[rr];
         if (kpos <= qmin_blk) continue;          // every staging query sees the key
         const int base = (r * D) & (TILE - 1);
@@ -866,6 +868,7 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
     uint64_t* s_free = s_full + NB;           // [NB]
     uint64_t* p_full = s_free + NB;           // [NB]
     uint64_t* o_full = p_full + NB;
+    uint64_t* fixed = o_full + 1;             // K/V of a tile-load-zeroing tile fixed
     uint32_t* holder = reinterpret_cast<uint32_t*>(bars + 24);
     float* nsum = reinterpret_cast<float*>(holder + 4);     // [NWG][128]
     int* qidx_blk = reinterpret_cast<int*>(nsum + NWG * TILE);    // [128]
@@ -887,6 +890,7 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
             mbar_init(&s_full[i], 1); mbar_init(&s_free[i], 1); mbar_init(&p_full[i], EPI_WARPS);
         }
         mbar_init(o_full, 1);
+        mbar_init(fixed, EPI_WARPS);
         fence_barrier_init();
         if (T > 0) {
             // Q and the first K/V tiles do not depend on the schedule being
@@ -966,16 +970,15 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
         constexpr uint32_t idS = idesc_bf16(128, 128, 0, 0);
         if (T > 0) mbar_wait(q_full, 0, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
         const uint64_t dQ = kdesc(sQ, 0);
+        int nfix = 0;
         for (int n = 0; n < T; ++n) {
             const uint32_t e = sched[n];
             const int st = n % S, b = n % NB;
             uint8_t* kt = sK + st * TB;
             mbar_wait(&k_full[st], (n / S) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
             if (lane == 0) TRACE(1, n, 0);
-            if (e & SCHED_FIX) {   // V is fixed before its P·V
-                fix_tile<D>(kt, qidx_blk, qmin_blk, Kidx_bh, (int)(e & SCHED_IDX), s.NK, lane);
-                fence_async_smem();
-            }
+            if (e & SCHED_FIX)     // the epilogue warps zero K and V of this tile
+                mbar_wait(fixed, (nfix++) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
             __syncwarp();
             mbar_wait(&s_free[b], ((n / NB) & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
             tc_fence_after();
@@ -993,15 +996,13 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
     } else if (warp == 2) {
         // O += P·V issuer: P·V(m) needs its V tile and the epilogue's P.
         constexpr uint32_t idPV = idesc_bf16(128, D, 0, 1);
+        int nfix = 0;
         for (int m = 0; m < T; ++m) {
             const uint32_t e = sched[m];
             const int b = m % NB, sv = m % SV;
             uint8_t* vt = sV + sv * TB;
             mbar_wait(&v_full[sv], (m / SV) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
-            if (e & SCHED_FIX) {
-                fix_tile<D>(vt, qidx_blk, qmin_blk, Kidx_bh, (int)(e & SCHED_IDX), s.NK, lane);
-                fence_async_smem();
-            }
+            if (e & SCHED_FIX) mbar_wait(fixed, (nfix++) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
             __syncwarp();
             mbar_wait(&p_full[b], (m / NB) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
             if (lane == 0) TRACE(1, m, 2);
@@ -1047,6 +1048,23 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
             const int kb = (int)(e & SCHED_IDX);
             const bool all = (e & SCHED_ALL) != 0;
             const int b = j % NB;
+            if (e & SCHED_FIX) {
+                // The reference's tile-load zeroing of this tile's K and V, by
+                // the eight epilogue warps (32 rows each of K or V) instead of
+                // one control warp: S and P·V wait for it.
+                const int ew = et >> 5;
+                uint8_t* tile;
+                if (ew < 4) {
+                    mbar_wait(&k_full[j % S], (j / S) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+                    tile = sK + (j % S) * TB;
+                } else {
+                    mbar_wait(&v_full[j % SV], (j / SV) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+                    tile = sV + (j % SV) * TB;
+                }
+                fix_tile<D, 1>(tile, qidx_blk, qmin_blk, Kidx_bh, kb, s.NK, lane, 32 * (ew & 3));
+                fence_async_smem();
+                epi_arrive(fixed);
+            }
             mbar_wait(&s_full[b], (j / NB) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
             if (et == 0 && j == 0) CTA_MARK_T(1, 3);
             if (et == 0) TRACE(2, j, 0);
