@@ -505,6 +505,7 @@ k1_tau_mask(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
     uint64_t* k_empty = bars + 1 + S;
     uint64_t* s_full = bars + 1 + 2 * S;      // [NB]
     uint64_t* s_free = s_full + NB;           // [NB]
+    uint64_t* fixed = s_free + NB;            // K of a tile-load-zeroing tile fixed
     uint32_t* holder = reinterpret_cast<uint32_t*>(bars + 24);
     int* qidx_blk = reinterpret_cast<int*>(holder + 4);      // [128]
     int* misc = qidx_blk + TILE;                             // [8] warp counts, tile count, fix run
@@ -523,6 +524,7 @@ k1_tau_mask(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
         mbar_init(q_full, 1);
         for (int i = 0; i < S; ++i) { mbar_init(&k_full[i], 1); mbar_init(&k_empty[i], 1); }
         for (int i = 0; i < NB; ++i) { mbar_init(&s_full[i], 1); mbar_init(&s_free[i], NE / 32); }
+        mbar_init(fixed, 4);
         fence_barrier_init();
         // Q does not depend on the schedule built below: issue it now
         tma_prefetch_desc(&tmQ);
@@ -569,17 +571,15 @@ k1_tau_mask(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
         constexpr uint32_t idesc = idesc_bf16(128, 128, 0, 0);
         mbar_wait(q_full, 0, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);   // issued at set-up even when T = 0
         if (lane == 0) CTA_MARK_T(0, 6);
+        int nfix = 0;
         for (int j = 0; j < T; ++j) {
             const uint32_t e = sched[j];
-            const int kb = (int)(e & SCHED_IDX);
             const int st = j % S, b = j % NB;
             uint8_t* kt = sK + st * TB;
             mbar_wait(&k_full[st], (j / S) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
             if (lane == 0) TRACE(5, j, 0);
-            if (e & SCHED_FIX) {
-                fix_tile<D>(kt, qidx_blk, qmin_blk, Kidx_bh, kb, s.NK, lane);
-                fence_async_smem();
-            }
+            if (e & SCHED_FIX)     // four epilogue warps zero K of this tile
+                mbar_wait(fixed, (nfix++) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
             __syncwarp();
             mbar_wait(&s_free[b], ((j / NB) & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
             if (lane == 0) TRACE(5, j, 1);
@@ -620,6 +620,13 @@ k1_tau_mask(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
             const int kb = (int)(e & SCHED_IDX);
             const int b = j % NB;
             const bool all = (e & SCHED_ALL) != 0;
+            if ((e & SCHED_FIX) && et < 4 * 32) {
+                // the reference's tile-load zeroing of K, 32 rows per warp
+                mbar_wait(&k_full[j % S], (j / S) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+                fix_tile<D, 1>(sK + (j % S) * TB, qidx_blk, qmin_blk, Kidx_bh, kb, s.NK, lane, 32 * (et >> 5));
+                fence_async_smem();
+                epi_arrive(fixed);
+            }
             float lim = tk.threshold();
             {
                 float m1 = __uint_as_float(0x7f800000u), x2 = neg_inf(), y2 = neg_inf();
@@ -1234,6 +1241,7 @@ k4_dq(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
     uint64_t* ds_full = sd_free + 1;
     uint64_t* ds_free = ds_full + 1;
     uint64_t* dq_full = ds_free + 1;
+    uint64_t* fixed = dq_full + 1;            // K/V of a tile-load-zeroing tile fixed
     uint32_t* holder = reinterpret_cast<uint32_t*>(bars + 24);
     int* qidx_blk = reinterpret_cast<int*>(holder + 4);
     uint32_t* sched = reinterpret_cast<uint32_t*>(qidx_blk + TILE);   // [T]
@@ -1255,6 +1263,7 @@ k4_dq(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
         mbar_init(ds_full, DQ_NE / 32);
         mbar_init(ds_free, 1);
         mbar_init(dq_full, 1);
+        mbar_init(fixed, 8);
         fence_barrier_init();
         if (T > 0) {
             // Q, dO and the first K/V tiles do not depend on the schedule
@@ -1315,6 +1324,7 @@ k4_dq(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
         constexpr uint32_t idS = idesc_bf16(128, 128, 0, 0);
         if (T > 0) mbar_wait(q_full, 0, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
         const uint64_t dQd = kdesc(sQ, 0), dOd = kdesc(sdO, 0);
+        int nfix = 0;
         for (int j = 0; j < T; ++j) {
             const uint32_t e = sched[j];
             const int kb = (int)(e & SCHED_IDX);
@@ -1324,11 +1334,8 @@ k4_dq(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
             uint8_t* vt = sV + sv * TB;
             mbar_wait(&k_full[st], (j / SK) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
             mbar_wait(&v_full[sv], (j / SV) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
-            if (fix) {
-                fix_tile<D>(kt, qidx_blk, qmin_blk, Kidx_bh, kb, s.NK, lane);
-                fix_tile<D>(vt, qidx_blk, qmin_blk, Kidx_bh, kb, s.NK, lane);
-                fence_async_smem();
-            }
+            if (fix)      // the epilogue warps zero K and V of this tile
+                mbar_wait(fixed, (nfix++) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
             __syncwarp();
             mbar_wait(sd_free, (j & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
             if (lane == 0) TRACE(5, j, 0);
@@ -1399,6 +1406,22 @@ k4_dq(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
             const uint32_t e = sched[j];
             const int kb = (int)(e & SCHED_IDX);
             const bool all = qv && (e & SCHED_ALL) != 0;
+            if ((e & SCHED_FIX) && et < 8 * 32) {
+                // the reference's tile-load zeroing of K and V, by eight
+                // epilogue warps (32 rows each of K or V); S/dP waits for it
+                const int ew = et >> 5;
+                uint8_t* tile;
+                if (ew < 4) {
+                    mbar_wait(&k_full[j % SK], (j / SK) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+                    tile = sK + (j % SK) * TB;
+                } else {
+                    mbar_wait(&v_full[j % SV], (j / SV) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+                    tile = sV + (j % SV) * TB;
+                }
+                fix_tile<D, 1>(tile, qidx_blk, qmin_blk, Kidx_bh, kb, s.NK, lane, 32 * (ew & 3));
+                fence_async_smem();
+                epi_arrive(fixed);
+            }
             mbar_wait(sd_full, j & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
             if (et == 0) TRACE(6, j, 0);
             tc_fence_after();
