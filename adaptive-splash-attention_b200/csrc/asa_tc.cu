@@ -1552,6 +1552,8 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
     uint64_t* pd_full = sd_full + 2;          // [2]
     uint64_t* pd_free = pd_full + 2;          // [2]
     uint64_t* out_full = pd_free + 2;
+    uint64_t* kv_ready = out_full + 1;        // pristine K/V and block positions in place
+    uint64_t* fixed = kv_ready + 1;           // ... and zeroed by the epilogue warps
     uint32_t* holder = reinterpret_cast<uint32_t*>(bars + 16);
     // per query of the current (and next) block: query pairs as float4
     // (-τ, -τ', max(lo, 0), max(lo', 0)) and (hi, hi', 1/n, 1/n') with lo/hi
@@ -1576,6 +1578,8 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
             mbar_init(&sd_full[i], 1); mbar_init(&pd_full[i], DKV_NE / 32); mbar_init(&pd_free[i], 1);
         }
         mbar_init(out_full, 1);
+        mbar_init(kv_ready, 1);
+        mbar_init(fixed, 8);
         fence_barrier_init();
         if (T > 0) {
             // the first Q/dO tile does not depend on the schedule built below
@@ -1614,7 +1618,7 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
     } else if (warp == 1) {
         // S^T = K·Q^T and dP^T = V·dO^T per half (N = 64 queries)
         constexpr uint32_t idS = idesc_bf16(128, HQ, 0, 0);
-        int loads = 0;
+        int loads = 0, nfix = 0;
         bool dirty = true;   // K/V not loaded yet
         for (int i = 0; i < T; ++i) {
             const uint32_t e = sched[i];
@@ -1642,10 +1646,11 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
                         qidx_blk[r] = q < s.NQ ? Qidx_bh[q] : INT_MAX;
                     }
                     __syncwarp();
-                    const int qmin_blk = bd.qmin[bh * s.nQB + qb];
-                    fix_tile<D>(sK, qidx_blk, qmin_blk, Kidx_bh, kb, s.NK, lane);
-                    fix_tile<D>(sV, qidx_blk, qmin_blk, Kidx_bh, kb, s.NK, lane);
-                    fence_async_smem();
+                    // eight epilogue warps zero K and V (32 rows each) while
+                    // they would otherwise wait for this tile's S^T/dP^T
+                    if (lane == 0) mbar_arrive(kv_ready);
+                    mbar_wait(fixed, nfix & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+                    ++nfix;
                 }
                 dirty = fix;
             }
@@ -1740,11 +1745,22 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
             dst[640 + et] = __int_as_float(ok ? (s.causal ? Qidx_bh[q] : INT_MAX) : INT_MIN);
         };
         if (T > 0 && et < TILE) fetch(0, qinfo);
+        int nfix = 0;
         for (int i = 0; i < T; ++i) {
             const uint32_t e = sched[i];
             asm volatile("bar.sync 2, %0;" ::"n"(DKV_NE) : "memory");   // qinfo[i&1] written; tile i-1 done
             if (i + 1 < T && et < TILE) fetch(i + 1, qinfo + ((i + 1) & 1) * 6 * TILE);
             const float* qi = qinfo + (i & 1) * 6 * TILE;
+            if ((e & SCHED_FIX) && et < 8 * 32) {
+                const int ew = et >> 5;
+                mbar_wait(kv_ready, nfix & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+                const int qbf = (int)(e & SCHED_IDX);
+                fix_tile<D, 1>(ew < 4 ? sK : sV, qidx_blk, bd.qmin[bh * s.nQB + qbf], Kidx_bh, kb, s.NK, lane,
+                               32 * (ew & 3));
+                fence_async_smem();
+                epi_arrive(fixed);
+            }
+            if (e & SCHED_FIX) ++nfix;
             const bool all = kv && (e & SCHED_ALL) != 0;
 #pragma unroll 1
             for (int hb = 0; hb < 2; ++hb) {
