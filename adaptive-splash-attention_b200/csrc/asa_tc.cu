@@ -1048,7 +1048,8 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
         const float2 c1 = make_float2(__fmul_rn(s.am1, s.scale), __fmul_rn(s.am1, s.scale));
         const float2 mtau = make_float2(-tq, -tq);
         const float uhi = __fmaf_rn(s.am1, 10.0f, -tq);
-        const bool packed_row = kPacked && split && __fmaf_rn(s.am1, -10.0f, -tq) <= 0.0f;
+        // warp-uniform: the packed path issues warp-collective TMEM loads/stores
+        const bool packed_row = __all_sync(0xffffffffu, kPacked && split && __fmaf_rn(s.am1, -10.0f, -tq) <= 0.0f);
         float2 n2 = make_float2(0.0f, 0.0f);
         for (int j = 0; j < T; ++j) {
             const uint32_t e = sched[j];
@@ -1079,11 +1080,16 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
 #ifdef ASA_EXP_F_NOEPI
             if (true) { tc_fence_before(); epi_arrive(&p_full[b]); continue; }
 #endif
-            if (kPacked && all && packed_row) {
-                // every key visible: both chunks loaded at once, packed math
+            if (kPacked && packed_row) {
+                // both chunks loaded at once, packed math; on partially
+                // visible tiles invisible keys are masked to p = 0
                 uint32_t r[CPT][32];
 #pragma unroll
                 for (int cc = 0; cc < CPT; ++cc) tmem_ld32(tl + b * 128 + (h * CPT + cc) * 32, r[cc]);
+                uint32_t vis[CPT];
+#pragma unroll
+                for (int cc = 0; cc < CPT; ++cc)
+                    vis[cc] = all ? 0xffffffffu : vis_mask32(Kidx_bh, kb * TILE + (h * CPT + cc) * 32, s.NK, s.causal, qpos);
                 tmem_ld_wait();
 #pragma unroll
                 for (int cc = 0; cc < CPT; ++cc) {
@@ -1093,8 +1099,11 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
                         uint32_t hi[8], lo[8];
 #pragma unroll
                         for (int m = 0; m < 8; ++m) {
-                            const float2 pp = entmax_pair<PINV>(r[cc][16 * g + 2 * m], r[cc][16 * g + 2 * m + 1],
-                                                                c1, mtau, uhi);
+                            float2 pp = entmax_pair<PINV>(r[cc][16 * g + 2 * m], r[cc][16 * g + 2 * m + 1],
+                                                          c1, mtau, uhi);
+                            const int bit = 16 * g + 2 * m;
+                            pp.x = (vis[cc] >> bit) & 1u ? pp.x : 0.0f;
+                            pp.y = (vis[cc] >> (bit + 1)) & 1u ? pp.y : 0.0f;
                             n2 = __fadd2_rn(n2, pp);
                             split_pair(pp, hi[m], lo[m]);
                         }
