@@ -7,6 +7,7 @@
 // device, launches go on the caller's stream, and errors come back as status
 // codes instead of exceptions.
 #include "asa_internal.h"
+#include "asa_sm100.cuh"
 #include <atomic>
 #include <mutex>
 #include <climits>
@@ -87,17 +88,22 @@ struct ProfScope {
 using asa::Shape;
 
 constexpr int kMaxDevices = 64;
-int* g_err_ptr[kMaxDevices];
+// Per-device addresses of device symbols, looked up once per device.  Host
+// threads may race on the first lookup; each writes the same value, and the
+// atomics make that race well defined.
+std::atomic<int*> g_err_ptr[kMaxDevices];
 
 int* error_word() {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
-    if (!g_err_ptr[dev]) {
+    int* w = g_err_ptr[dev].load(std::memory_order_relaxed);
+    if (!w) {
         void* p = nullptr;
         if (cudaGetSymbolAddress(&p, g_asa_error) != cudaSuccess) return nullptr;
-        g_err_ptr[dev] = (int*)p;
+        w = (int*)p;
+        g_err_ptr[dev].store(w, std::memory_order_relaxed);
     }
-    return g_err_ptr[dev];
+    return w;
 }
 
 size_t align16(size_t x) { return (x + 15) & ~size_t(15); }
@@ -178,6 +184,22 @@ size_t fwd_bytes(const Shape& s, int backend) {
 }
 
 thread_local cudaError_t g_last_cuda = cudaSuccess;
+
+// asa_wait_probe's kernel: lane 0 waits, with the kernels' bounded wait, on
+// phase 0 of a shared-memory mbarrier that expects one arrival nobody makes,
+// so the wait runs out after `spins` polls and records
+// ASA_ERR_DEVICE_TIMEOUT in the error word; then the barrier is completed by
+// the thread itself, so nothing is left pending when the block exits.
+__global__ void wait_probe_kernel(long long spins, int* err) {
+    __shared__ uint64_t bar;
+    if (threadIdx.x == 0) {
+        asa::sm100::mbar_init(&bar, 1);
+        asa::sm100::fence_barrier_init();
+        asa::sm100::mbar_wait(&bar, 0, spins, err, ASA_ERR_DEVICE_TIMEOUT);
+        asa::sm100::mbar_arrive(&bar);
+    }
+    __syncwarp();
+}
 int cuda_status(cudaError_t e) {
     if (e == cudaSuccess) return ASA_OK;
     g_last_cuda = e;
@@ -348,7 +370,7 @@ int asa_backward(const asa_params* p, const void* Q, const void* K, const void* 
 static __device__ __align__(256) unsigned char g_asa_noalloc_scratch[ASA_NOALLOC_SCRATCH_BYTES];
 
 namespace {
-void* g_noalloc_ptr[kMaxDevices];
+std::atomic<void*> g_noalloc_ptr[kMaxDevices];
 
 // Device address of g_asa_noalloc_scratch on the current device.  Host code
 // must not use the symbol itself (it names a host-side shadow); the address
@@ -359,13 +381,13 @@ int noalloc_scratch(void** out) {
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return cuda_status(e);
     if (dev < 0 || dev >= kMaxDevices) return ASA_ERR_UNSUPPORTED;
-    if (!g_noalloc_ptr[dev]) {
-        void* ptr = nullptr;
+    void* ptr = g_noalloc_ptr[dev].load(std::memory_order_relaxed);
+    if (!ptr) {
         e = cudaGetSymbolAddress(&ptr, g_asa_noalloc_scratch);
         if (e != cudaSuccess) return cuda_status(e);
-        g_noalloc_ptr[dev] = ptr;
+        g_noalloc_ptr[dev].store(ptr, std::memory_order_relaxed);
     }
-    *out = g_noalloc_ptr[dev];
+    *out = ptr;
     return ASA_OK;
 }
 }  // namespace
@@ -404,6 +426,23 @@ int asa_device_error(asa_stream_t stream, int* code) {
     if (e == cudaSuccess) e = cudaStreamSynchronize(st);
     *code = v;
     return cuda_status(e);
+}
+
+int asa_device_error_async(asa_stream_t stream, int* host_word) {
+    if (!host_word) return ASA_ERR_INVALID;
+    int* w = error_word();
+    if (!w) return ASA_ERR_CUDA;
+    return cuda_status(cudaMemcpyAsync(host_word, w, sizeof(int), cudaMemcpyDeviceToHost,
+                                       (cudaStream_t)stream));
+}
+
+int asa_wait_probe(long long spins, asa_stream_t stream) {
+    if (spins < 1) return ASA_ERR_INVALID;
+    int* w = error_word();
+    if (!w) return ASA_ERR_CUDA;
+    wait_probe_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(spins, w);
+    asa::note_launch();
+    return cuda_status(cudaGetLastError());
 }
 
 int asa_profile_begin(int enable) {

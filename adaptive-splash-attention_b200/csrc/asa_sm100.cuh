@@ -51,7 +51,9 @@ __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
 }
 // Bounded wait: returns false (and records `code` in *err) when the phase
 // with the given parity has not completed after `spins` polls.  Callers then
-// carry on without the data; the host sees the error word.
+// carry on without the data (the results are garbage, the host sees the error
+// word); before exiting, a CTA whose wait gave up drains its own outstanding
+// loads and MMAs (mbar_drain, drain_ring).
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, long long spins,
                                           int* err, int code) {
     if (mbar_try(bar, parity)) return true;
@@ -62,6 +64,28 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, long l
     }
     if (err) atomicCAS(err, 0, code);
     return false;
+}
+
+// Whether a wait anywhere has given up (the device error word is set).
+__device__ __forceinline__ bool error_set(const int* err) {
+    return err && *reinterpret_cast<const volatile int*>(err) != 0;
+}
+// Exit-time drain after a wait gave up: wait, bounded by a fixed poll count
+// that ignores the error word, for a phase of this CTA's own asynchronous
+// work (a TMA load or an MMA commit), so nothing is still in flight when the
+// CTA frees its TMEM and its shared memory.
+__device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
+    for (int i = 0; i < (1 << 20); ++i)
+        if (mbar_try(bar, parity)) return;
+}
+// Drain a ring of `stages` full barriers whose loads j = 0 .. count-1 went to
+// stage j % stages, phase (j / stages) & 1: waiting for each stage's last
+// phase covers the earlier ones (a barrier's phases complete in order).
+__device__ __forceinline__ void drain_ring(uint64_t* full, int stages, int count) {
+    for (int st = 0; st < stages && st < count; ++st) {
+        const int jl = st + ((count - 1 - st) / stages) * stages;
+        mbar_drain(&full[st], (uint32_t)(jl / stages) & 1u);
+    }
 }
 
 // ---- TMA ----------------------------------------------------------------------

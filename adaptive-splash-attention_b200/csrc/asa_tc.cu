@@ -1,30 +1,32 @@
 // asa_tc.cu -- tcgen05 / TMEM / TMA kernels for bf16 inputs, head dim 64 or
 // 128, 128x128 mask tiles.
 //
-// Kernels (one CTA per 128-row block, warp-specialised, 192 threads):
-//   tc_bounds   per-block min/max of the position indices (tile visibility)
-//   k1_tau_mask τ and block mask: S = Q·K^T over every visible tile into
-//               TMEM (double-buffered), 4 epilogue warps stream each score
-//               row through the reference top-k, then solve τ
-//               (reference build_mask_kernel :150-217)
-//   k3_forward  O = Σ p v / (Σ p + EPS) over the CSR tile list: S = Q·K^T,
-//               entmax p in the epilogue warps, P written to shared memory as
-//               a bf16 hi/lo pair, O += P_hi·V + P_lo·V in TMEM
-//               (reference splash_forward_sparse :244-341)
-//   k4_pre      D_q = O·dO per query (the acc·dO/n term of :487-491)
-//   k4_dq       dQ = Σ dS·K over the CSR list (query-major)
-//   k4_dkdv     dV = Σ P^T·dO/n, dK = Σ dS^T·Q over the transposed list
-//               (key-major; no atomics)
-//               (reference splash_backward_sparse :343-535)
+// Kernels (one CTA per 128-row block, warp-specialised):
+//   tc_bounds    per-block min/max of the position indices (tile visibility)
+//   k1_tau_mask  top-k and block mask: S = Q·K^T over every visible tile into
+//                TMEM (four buffers), epilogue warps stream each score row
+//                through the reference top-k (reference build_mask_kernel
+//                :150-217); k1_tau_solve then solves τ per row
+//   k3_forward   O = Σ p v / (Σ p + EPS) over the CSR tile list: S = Q·K^T,
+//                entmax p in the epilogue warps, P written back to TMEM as a
+//                bf16 hi/lo pair, O += P_hi·V + P_lo·V in TMEM
+//                (reference splash_forward_sparse :244-341)
+//   k4_pre       D_q = O·dO per query (the acc·dO/n term of :487-491)
+//   k4_dq        dQ = Σ dS·K over the CSR list (query-major)
+//   k4_dkdv      dV = Σ P^T·dO/n, dK = Σ dS^T·Q over the transposed list
+//                (key-major; no atomics)
+//                (reference splash_backward_sparse :343-535)
 //
-// Warp roles: warp 0 issues TMA loads, warp 1 owns TMEM and issues the MMAs
-// (lane 0) -- its 32 lanes also apply the reference's tile-load zeroing to
-// freshly loaded K/V tiles when a tile needs it -- and warps 2..5 are the
-// epilogue: thread (warp%4)*32+lane owns TMEM lane = tile row.
+// Warp roles: warp 0 issues the TMA loads, warp 1 owns TMEM and issues MMAs
+// (lane 0), in the forward and backward warp 2 issues the second MMA stream,
+// and the remaining warps are the epilogue: thread (warp%4)*32+lane owns
+// TMEM lane = tile row.  The epilogue warps also apply the reference's
+// tile-load zeroing to freshly loaded K/V tiles that need it.
 //
 // Every mbarrier wait is bounded (Shape::spins polls); when one runs out the
 // kernel records ASA_ERR_DEVICE_TIMEOUT in the device error word and carries
-// on without the data, so it always terminates.
+// on without the data, so it always terminates; before exiting, its TMA and
+// MMA issuers wait (with a fixed bound) for their own work still in flight.
 #include "asa_internal.h"
 #include "asa_sm100.cuh"
 #include <climits>
@@ -106,30 +108,6 @@ __device__ __forceinline__ bool needs_fix(const Shape& s, const Bounds& b, int b
     if (!s.ref_load || !s.causal) return false;   // bounds exist only for causal shapes
     return b.kmax[bh * s.nKB + kb] > b.qmin[bh * s.nQB + qb];
 }
-
-#ifdef ASA_EXP_TRACE
-__device__ unsigned long long g_trace[8][64][8];
-__device__ unsigned long long g_cnt[8];
-#define TRACE(role, j, ev) do { if (blockIdx.x == 0 && blockIdx.y == 0 && (j) < 64) g_trace[role][j][ev] = clock64(); } while (0)
-#else
-#define TRACE(role, j, ev) do {} while (0)
-#endif
-#ifdef ASA_EXP_CTA
-__device__ unsigned long long g_cta[4][4096][16];
-__device__ __forceinline__ unsigned long long gtimer() {
-    unsigned long long t; asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t)); return t;
-}
-#define CTA_MARK(k, ev) do { if (threadIdx.x == 0) { const int c_ = blockIdx.y * gridDim.x + blockIdx.x; \
-    if (c_ < 4096) { g_cta[k][c_][ev] = gtimer(); if ((ev) == 0) { unsigned sm_; asm("mov.u32 %0, %smid;" : "=r"(sm_)); g_cta[k][c_][15] = sm_; } } } } while (0)
-#define CTA_MARK_T(k, ev) do { const int c_ = blockIdx.y * gridDim.x + blockIdx.x; \
-    if (c_ < 4096) g_cta[k][c_][ev] = gtimer(); } while (0)
-#define g_cta_n(k, n) do { const int c_ = blockIdx.y * gridDim.x + blockIdx.x; \
-    if (c_ < 4096) g_cta[k][c_][14] = (n); } while (0)
-#else
-#define CTA_MARK(k, ev) do {} while (0)
-#define CTA_MARK_T(k, ev) do {} while (0)
-#define g_cta_n(k, n) do {} while (0)
-#endif
 
 // ---- per-CTA tile schedule ----------------------------------------------------
 // Each CTA stages its tile sequence in shared memory once, so no role chases
@@ -506,6 +484,7 @@ k1_tau_mask(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
     uint64_t* s_full = bars + 1 + 2 * S;      // [NB]
     uint64_t* s_free = s_full + NB;           // [NB]
     uint64_t* fixed = s_free + NB;            // K of a tile-load-zeroing tile fixed
+    uint64_t* drain = fixed + 1;              // exit-time MMA drain (after a timed-out wait)
     uint32_t* holder = reinterpret_cast<uint32_t*>(bars + 24);
     int* qidx_blk = reinterpret_cast<int*>(holder + 4);      // [128]
     int* misc = qidx_blk + TILE;                             // [8] warp counts, tile count, fix run
@@ -518,13 +497,13 @@ k1_tau_mask(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
     const int bh = blockIdx.y;
     const int qb = s.causal ? (int)(gridDim.x - 1 - blockIdx.x) : (int)blockIdx.x;
     const int32_t* Kidx_bh = Kidx + (size_t)bh * s.NK;
-    CTA_MARK(0, 0);
 
     if (threadIdx.x == 0) {
         mbar_init(q_full, 1);
         for (int i = 0; i < S; ++i) { mbar_init(&k_full[i], 1); mbar_init(&k_empty[i], 1); }
         for (int i = 0; i < NB; ++i) { mbar_init(&s_full[i], 1); mbar_init(&s_free[i], NE / 32); }
         mbar_init(fixed, 4);
+        mbar_init(drain, 1);
         fence_barrier_init();
         // Q does not depend on the schedule built below: issue it now
         tma_prefetch_desc(&tmQ);
@@ -553,7 +532,6 @@ k1_tau_mask(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
     const uint32_t tbase = *holder;
     const int qmin_blk = s.causal ? bd.qmin[bh * s.nQB + qb] : INT_MIN;
     const int T = misc[8];
-    CTA_MARK(0, 1);
 
     if (warp == 0) {
         if (lane == 0 && T > 0) {
@@ -561,40 +539,43 @@ k1_tau_mask(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
                 const int kb = (int)(sched[j] & SCHED_IDX);
                 const int st = j % S;
                 mbar_wait(&k_empty[st], ((j / S) & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
-                TRACE(4, j, 0);
                 mbar_expect_tx(&k_full[st], TB);
                 for (int bx = 0; bx < D / BOX; ++bx)
                     tma_load_3d(sK + st * TB + bx * BOX_BYTES, &tmK, &k_full[st], bx * BOX, kb * TILE, bh);
             }
         }
+        if (lane == 0 && error_set(err)) {   // a wait gave up: let this CTA's loads land
+            mbar_drain(q_full, 0);
+            drain_ring(k_full, S, T);
+        }
     } else if (warp == 1) {
         constexpr uint32_t idesc = idesc_bf16(128, 128, 0, 0);
         mbar_wait(q_full, 0, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);   // issued at set-up even when T = 0
-        if (lane == 0) CTA_MARK_T(0, 6);
         int nfix = 0;
         for (int j = 0; j < T; ++j) {
             const uint32_t e = sched[j];
             const int st = j % S, b = j % NB;
             uint8_t* kt = sK + st * TB;
             mbar_wait(&k_full[st], (j / S) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
-            if (lane == 0) TRACE(5, j, 0);
             if (e & SCHED_FIX)     // four epilogue warps zero K of this tile
                 mbar_wait(fixed, (nfix++) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
             __syncwarp();
             mbar_wait(&s_free[b], ((j / NB) & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
-            if (lane == 0) TRACE(5, j, 1);
             tc_fence_after();
             if (lane == 0) {
 #pragma unroll
                 for (int kk = 0; kk < D / 16; ++kk)
                     mma_bf16_ss(tbase + b * 128, kdesc(sQ, kk), kdesc(kt, kk), idesc, kk > 0);
-                TRACE(5, j, 2);
                 mma_commit(&s_full[b]);
                 mma_commit(&k_empty[st]);
-                if (j == 0) CTA_MARK_T(0, 7);
             }
             __syncwarp();
         }
+        if (lane == 0 && error_set(err)) {   // a wait gave up: let this CTA's MMAs finish
+            mma_commit(drain);
+            mbar_drain(drain, 0);
+        }
+        __syncwarp();
     } else {
         const int row = (warp & 3) * 32 + lane;
         const int et = threadIdx.x - EPI0;
@@ -642,8 +623,6 @@ k1_tau_mask(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
                 lim = fmaxf(lim, fmaxf(m1, NW > 2 ? y2 : neg_inf()));
             }
             mbar_wait(&s_full[b], (j / NB) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
-            if (j == 0 && et == 0) CTA_MARK_T(0, 8);
-            if (et == 0) TRACE(6, j, 0);
             tc_fence_after();
             uint32_t r2[CP][32];
 #pragma unroll
@@ -651,7 +630,6 @@ k1_tau_mask(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
             tmem_ld_wait();
             tc_fence_before();
             epi_arrive(&s_free[b]);          // S is in registers: release the buffer
-            if (et == 0) TRACE(6, j, 1);
             uint32_t vis[CP];
 #pragma unroll
             for (int cc = 0; cc < CP; ++cc) {
@@ -733,10 +711,7 @@ k1_tau_mask(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
                 t[NW * TILE] = v1;
                 t[2 * NW * TILE] = v2;
             }
-            if (et == 0) TRACE(6, j, 2);
-            if (j == 0 && et == 0) CTA_MARK_T(0, 2);
         }
-        if (et == 0) CTA_MARK_T(0, 3);
         // Merge: one thread per row walks the NW sorted lists (64-bit keys
         // ordered like (score desc, key index asc); identical keys -- the
         // -1e6 seeds -- go by list number) and emits the row's top-k in
@@ -745,7 +720,6 @@ k1_tau_mask(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
 #pragma unroll
         for (int i = 0; i < KM; ++i) lists[(h * KM + i) * TILE + row] = order_key(tk.v[i], tk.i[i]);
         asm volatile("bar.sync 2, %0;" ::"n"(NE) : "memory");
-        if (et == 0) CTA_MARK_T(0, 9);
         if (h == 0 && qv) {
             int pos[NW];
             unsigned long long cur[NW];
@@ -772,17 +746,12 @@ k1_tau_mask(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
                     }
             }
         }
-        if (et == 0) CTA_MARK_T(0, 10);
         asm volatile("bar.sync 2, %0;" ::"n"(NE) : "memory");
-        if (et == 0) CTA_MARK_T(0, 13);
         uint8_t* Mrow = M + ((size_t)bh * s.nQB + qb) * s.nKB;
         for (int i = et; i < s.nKB; i += NE) Mrow[i] = flags[i];
-        if (et == 0) CTA_MARK_T(0, 4);
     }
     tc_fence_before();
     __syncthreads();
-    CTA_MARK(0, 5);
-    if (threadIdx.x == 0) g_cta_n(0, T);
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tbase, 512);
@@ -850,17 +819,11 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
            const int32_t* __restrict__ Kidx, Bounds bd, const float* __restrict__ tau,
            const int32_t* __restrict__ ptr, const int32_t* __restrict__ idx, TO* __restrict__ O,
            float* __restrict__ O32, float* __restrict__ rownorm, int split, int* err) {
-#ifdef ASA_EXP_F_S2V3
-    constexpr int S = 2;                      // K stages
-    constexpr int SV = 3;                     // V stages
-#else
     constexpr int S = 3;                      // K stages
     constexpr int SV = 2;                     // V stages
-#endif
     constexpr int NB = 3;                     // S / P buffers in TMEM
     constexpr int TB = D * TILE * 2;
     extern __shared__ uint8_t smem_raw[];
-    CTA_MARK(1, 0);
     uint8_t* base = align1024(smem_raw, err);
     uint8_t* sQ = base;
     uint8_t* sK = base + TB;                  // S stages
@@ -876,6 +839,7 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
     uint64_t* p_full = s_free + NB;           // [NB]
     uint64_t* o_full = p_full + NB;
     uint64_t* fixed = o_full + 1;             // K/V of a tile-load-zeroing tile fixed
+    uint64_t* drain = fixed + 1;              // [2] exit-time MMA drains (after a timed-out wait)
     uint32_t* holder = reinterpret_cast<uint32_t*>(bars + 24);
     float* nsum = reinterpret_cast<float*>(holder + 4);     // [NWG][128]
     int* qidx_blk = reinterpret_cast<int*>(nsum + NWG * TILE);    // [128]
@@ -898,6 +862,8 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
         }
         mbar_init(o_full, 1);
         mbar_init(fixed, EPI_WARPS);
+        mbar_init(&drain[0], 1);
+        mbar_init(&drain[1], 1);
         fence_barrier_init();
         if (T > 0) {
             // Q and the first K/V tiles do not depend on the schedule being
@@ -925,7 +891,6 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
     }
     tc_fence_before();
     __syncthreads();
-    CTA_MARK(1, 1);
     tc_fence_after();
     const uint32_t tbase = *holder;
     constexpr uint32_t tO = 384;
@@ -937,37 +902,27 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
                 const int kb = (int)(sched[j] & SCHED_IDX);
                 const int st = j % S;
                 mbar_wait(&k_empty[st], ((j / S) & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
-                TRACE(0, j, 0);
                 mbar_expect_tx(&k_full[st], TB);
                 for (int bx = 0; bx < D / BOX; ++bx)
                     tma_load_3d(sK + st * TB + bx * BOX_BYTES, &tmK, &k_full[st], bx * BOX, kb * TILE, bh);
             }
-        }
-#ifdef ASA_EXP_TRACE
-        else if (lane == 2 && blockIdx.x == 0 && blockIdx.y == 0) {
-            for (int j = 0; j < T && j < 64; ++j) {
-                mbar_wait(&k_full[j % S], (j / S) & 1, s.spins, nullptr, 0);
-                TRACE(3, j, 0);
-            }
-        } else if (lane == 3 && blockIdx.x == 0 && blockIdx.y == 0) {
-            for (int j = 0; j < T && j < 64; ++j) {
-                mbar_wait(&v_full[j % SV], (j / SV) & 1, s.spins, nullptr, 0);
-                TRACE(3, j, 1);
-            }
-        }
-#endif
-        else if (lane == 1 && T > 0) {
+        } else if (lane == 1 && T > 0) {
             // V runs on its own thread: its ring (freed after P·V) must not
             // hold back the K ring (freed after S)
             for (int j = 1; j < T; ++j) {
                 const int kb = (int)(sched[j] & SCHED_IDX);
                 const int sv = j % SV;
                 mbar_wait(&v_empty[sv], ((j / SV) & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
-                TRACE(0, j, 1);
                 mbar_expect_tx(&v_full[sv], TB);
                 for (int bx = 0; bx < D / BOX; ++bx)
                     tma_load_3d(sV + sv * TB + bx * BOX_BYTES, &tmV, &v_full[sv], bx * BOX, kb * TILE, bh);
             }
+        }
+        __syncwarp();
+        if (lane == 0 && T > 0 && error_set(err)) {   // a wait gave up: let this CTA's loads land
+            mbar_drain(q_full, 0);
+            drain_ring(k_full, S, T);
+            drain_ring(v_full, SV, T);
         }
     } else if (warp == 1) {
         // S = Q·K^T issuer.  tcgen05.mma issue blocks at the tensor pipe's
@@ -983,7 +938,6 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
             const int st = n % S, b = n % NB;
             uint8_t* kt = sK + st * TB;
             mbar_wait(&k_full[st], (n / S) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
-            if (lane == 0) TRACE(1, n, 0);
             if (e & SCHED_FIX)     // the epilogue warps zero K and V of this tile
                 mbar_wait(fixed, (nfix++) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
             __syncwarp();
@@ -996,23 +950,26 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
                     mma_bf16_ss(tbase + b * 128, kdesc_step(dQ, kk), kdesc_step(dK, kk), idS, kk > 0);
                 mma_commit(&s_full[b]);
                 mma_commit(&k_empty[st]);
-                TRACE(1, n, 3);
             }
             __syncwarp();
         }
+        if (lane == 0 && error_set(err)) {   // a wait gave up: let this warp's MMAs finish
+            mma_commit(&drain[0]);
+            mbar_drain(&drain[0], 0);
+        }
+        __syncwarp();
     } else if (warp == 2) {
         // O += P·V issuer: P·V(m) needs its V tile and the epilogue's P.
+        // P·V(m) needs no wait on `fixed`: p_full(m) completes only after
+        // every epilogue warp's arrival, and the warps that zero V of a
+        // tile-load-zeroing tile arrive after that zeroing and its proxy fence.
         constexpr uint32_t idPV = idesc_bf16(128, D, 0, 1);
-        int nfix = 0;
         for (int m = 0; m < T; ++m) {
-            const uint32_t e = sched[m];
             const int b = m % NB, sv = m % SV;
             uint8_t* vt = sV + sv * TB;
             mbar_wait(&v_full[sv], (m / SV) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
-            if (e & SCHED_FIX) mbar_wait(fixed, (nfix++) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
             __syncwarp();
             mbar_wait(&p_full[b], (m / NB) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
-            if (lane == 0) TRACE(1, m, 2);
             tc_fence_after();
             if (lane == 0) {
                 const uint32_t pb = tbase + b * 128;
@@ -1027,11 +984,14 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
                 }
                 mma_commit(&s_free[b]);
                 mma_commit(&v_empty[sv]);
-                TRACE(1, m, 4);
             }
             __syncwarp();
         }
         if (lane == 0) mma_commit(o_full);
+        if (lane == 0 && error_set(err)) {   // a wait gave up: let this warp's MMAs finish
+            mma_commit(&drain[1]);
+            mbar_drain(&drain[1], 0);
+        }
         __syncwarp();
     } else {
         const int row = (warp & 3) * 32 + lane;
@@ -1074,12 +1034,7 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
                 epi_arrive(fixed);
             }
             mbar_wait(&s_full[b], (j / NB) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
-            if (et == 0 && j == 0) CTA_MARK_T(1, 3);
-            if (et == 0) TRACE(2, j, 0);
             tc_fence_after();
-#ifdef ASA_EXP_F_NOEPI
-            if (true) { tc_fence_before(); epi_arrive(&p_full[b]); continue; }
-#endif
             if (kPacked && packed_row) {
                 // both chunks loaded at once, packed math; on partially
                 // visible tiles invisible keys are masked to p = 0
@@ -1111,9 +1066,7 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
                         tmem_st8(col + g * 16 + 8, lo);
                     }
                 }
-                if (et == 0) TRACE(2, j, 1);
                 tmem_st_wait();
-                if (et == 0) TRACE(2, j, 3);
                 tc_fence_before();
                 epi_arrive(&p_full[b]);
                 continue;
@@ -1158,9 +1111,7 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
                     if (split) tmem_st8(tl + b * 128 + c * 32 + g * 16 + 8, lo);
                 }
             }
-            if (et == 0) TRACE(2, j, 1);
             tmem_st_wait();
-            if (et == 0) TRACE(2, j, 3);
             tc_fence_before();
             epi_arrive(&p_full[b]);
         }
@@ -1175,9 +1126,7 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
         }
         epi_bar();
         n = nsum[row];
-        if (et == 0) CTA_MARK_T(1, 4);
         mbar_wait(o_full, 0, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
-        if (et == 0) CTA_MARK_T(1, 5);
         tc_fence_after();
         const float inv = __fdiv_rn(1.0f, __fadd_rn(n, ASA_EPS));
         // every MMA is done: the K stages are free for the store staging
@@ -1200,12 +1149,9 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
             if (O32) warp_store_rows<float>(O32 + row0 * D, D, nrows, c * 32, o, stage, lane);
             if (sizeof(TO) == 2 || (void*)O != (void*)O32) warp_store_rows<TO>(O + row0 * D, D, nrows, c * 32, o, stage, lane);
         }
-        if (et == 0) CTA_MARK_T(1, 6);
     }
     tc_fence_before();
     __syncthreads();
-    CTA_MARK(1, 2);
-    if (threadIdx.x == 0) g_cta_n(1, T);
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tbase, 512);
@@ -1233,7 +1179,6 @@ k4_dq(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
     constexpr int SK = 3;
     constexpr int TB = D * TILE * 2;
     extern __shared__ uint8_t smem_raw[];
-    CTA_MARK(2, 0);
     uint8_t* base = align1024(smem_raw, err);
     uint8_t* sQ = base;
     uint8_t* sdO = base + TB;
@@ -1251,6 +1196,7 @@ k4_dq(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
     uint64_t* ds_free = ds_full + 1;
     uint64_t* dq_full = ds_free + 1;
     uint64_t* fixed = dq_full + 1;            // K/V of a tile-load-zeroing tile fixed
+    uint64_t* drain = fixed + 1;              // [2] exit-time MMA drains (after a timed-out wait)
     uint32_t* holder = reinterpret_cast<uint32_t*>(bars + 24);
     int* qidx_blk = reinterpret_cast<int*>(holder + 4);
     uint32_t* sched = reinterpret_cast<uint32_t*>(qidx_blk + TILE);   // [T]
@@ -1273,6 +1219,8 @@ k4_dq(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
         mbar_init(ds_free, 1);
         mbar_init(dq_full, 1);
         mbar_init(fixed, 8);
+        mbar_init(&drain[0], 1);
+        mbar_init(&drain[1], 1);
         fence_barrier_init();
         if (T > 0) {
             // Q, dO and the first K/V tiles do not depend on the schedule
@@ -1298,7 +1246,6 @@ k4_dq(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
     }
     tc_fence_before();
     __syncthreads();
-    CTA_MARK(2, 1);
     tc_fence_after();
     const uint32_t tbase = *holder;
     constexpr uint32_t tS = 0, tP = 128, tQ = 256, tDh = 384, tDl = 448;
@@ -1310,7 +1257,6 @@ k4_dq(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
                 const int kb = (int)(sched[j] & SCHED_IDX);
                 const int st = j % SK;
                 mbar_wait(&k_empty[st], ((j / SK) & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
-                TRACE(4, j, 0);
                 mbar_expect_tx(&k_full[st], TB);
                 for (int bx = 0; bx < D / BOX; ++bx)
                     tma_load_3d(sK + st * TB + bx * BOX_BYTES, &tmK, &k_full[st], bx * BOX, kb * TILE, bh);
@@ -1321,11 +1267,16 @@ k4_dq(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
                 const int kb = (int)(sched[j] & SCHED_IDX);
                 const int st = j % SV;
                 mbar_wait(&v_empty[st], ((j / SV) & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
-                TRACE(4, j, 1);
                 mbar_expect_tx(&v_full[st], TB);
                 for (int bx = 0; bx < D / BOX; ++bx)
                     tma_load_3d(sV + st * TB + bx * BOX_BYTES, &tmV, &v_full[st], bx * BOX, kb * TILE, bh);
             }
+        }
+        __syncwarp();
+        if (lane == 0 && T > 0 && error_set(err)) {   // a wait gave up: let this CTA's loads land
+            mbar_drain(q_full, 0);
+            drain_ring(k_full, SK, T);
+            drain_ring(v_full, SV, T);
         }
     } else if (warp == 1) {
         // S = Q·K^T and dP = dO·V^T issuer.  dQ comes from warp 2, so the
@@ -1347,7 +1298,6 @@ k4_dq(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
                 mbar_wait(fixed, (nfix++) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
             __syncwarp();
             mbar_wait(sd_free, (j & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
-            if (lane == 0) TRACE(5, j, 0);
             tc_fence_after();
             if (lane == 0) {
                 const uint64_t dK = kdesc(kt, 0), dV = kdesc(vt, 0);
@@ -1358,10 +1308,14 @@ k4_dq(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
                 }
                 mma_commit(sd_full);
                 mma_commit(&v_empty[sv]);
-                TRACE(5, j, 1);
             }
             __syncwarp();
         }
+        if (lane == 0 && error_set(err)) {   // a wait gave up: let this warp's MMAs finish
+            mma_commit(&drain[0]);
+            mbar_drain(&drain[0], 0);
+        }
+        __syncwarp();
     } else if (warp == 2) {
         // dQ += dS·K issuer (in tile order: a deterministic sum)
         constexpr uint32_t idQ = idesc_bf16(128, D, 0, 1);
@@ -1369,7 +1323,6 @@ k4_dq(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
             const int st = i % SK;
             const uint8_t* kt = sK + st * TB;
             mbar_wait(ds_full, i & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
-            if (lane == 0) TRACE(5, i, 2);
             tc_fence_after();
             if (lane == 0) {
                 const uint64_t dK = mndesc(kt, 0);
@@ -1383,11 +1336,14 @@ k4_dq(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
                 }
                 mma_commit(ds_free);
                 mma_commit(&k_empty[st]);
-                TRACE(5, i, 3);
             }
             __syncwarp();
         }
         if (lane == 0) mma_commit(dq_full);
+        if (lane == 0 && error_set(err)) {   // a wait gave up: let this warp's MMAs finish
+            mma_commit(&drain[1]);
+            mbar_drain(&drain[1], 0);
+        }
         __syncwarp();
     } else {
         // DQ_NW warpgroups; warpgroup h owns the 32-column chunk h of every
@@ -1432,7 +1388,6 @@ k4_dq(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
                 epi_arrive(fixed);
             }
             mbar_wait(sd_full, j & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
-            if (et == 0) TRACE(6, j, 0);
             tc_fence_after();
             uint32_t rs[32], rp[32];
             tmem_ld32(tl + tS + h * 32, rs);
@@ -1472,16 +1427,13 @@ k4_dq(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
                 }
                 split_pack(g, hi, lo);
             }
-            if (et == 0) TRACE(6, j, 1);
             mbar_wait(ds_free, (j & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
-            if (et == 0) TRACE(6, j, 2);
             tc_fence_after();
             tmem_st16(tl + tDh + h * 16, hi);
             if (split) tmem_st16(tl + tDl + h * 16, lo);
             tmem_st_wait();
             tc_fence_before();
             epi_arrive(ds_full);
-            if (et == 0) TRACE(6, j, 3);
         }
         mbar_wait(dq_full, 0, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
         tc_fence_after();
@@ -1507,8 +1459,6 @@ k4_dq(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
     }
     tc_fence_before();
     __syncthreads();
-    CTA_MARK(2, 2);
-    if (threadIdx.x == 0) g_cta_n(2, T);
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tbase, 512);
@@ -1547,7 +1497,6 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
     constexpr int TB = D * TILE * 2;
     constexpr int HQ = TILE / 2;              // queries per half
     extern __shared__ uint8_t smem_raw[];
-    CTA_MARK(3, 0);
     uint8_t* base = align1024(smem_raw, err);
     uint8_t* sK = base;
     uint8_t* sV = base + TB;
@@ -1563,6 +1512,7 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
     uint64_t* out_full = pd_free + 2;
     uint64_t* kv_ready = out_full + 1;        // pristine K/V and block positions in place
     uint64_t* fixed = kv_ready + 1;           // ... and zeroed by the epilogue warps
+    uint64_t* drain = fixed + 1;              // [2] exit-time MMA drains (after a timed-out wait)
     uint32_t* holder = reinterpret_cast<uint32_t*>(bars + 16);
     // per query of the current (and next) block: query pairs as float4
     // (-τ, -τ', max(lo, 0), max(lo', 0)) and (hi, hi', 1/n, 1/n') with lo/hi
@@ -1589,6 +1539,8 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
         mbar_init(out_full, 1);
         mbar_init(kv_ready, 1);
         mbar_init(fixed, 8);
+        mbar_init(&drain[0], 1);
+        mbar_init(&drain[1], 1);
         fence_barrier_init();
         if (T > 0) {
             // the first Q/dO tile does not depend on the schedule built below
@@ -1605,7 +1557,6 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
         sched_from_list(sched, list + e0, T, s, bd, bh, kb, true, threadIdx.x - DKV_EPI0);
     tc_fence_before();
     __syncthreads();
-    CTA_MARK(3, 1);
     tc_fence_after();
     const uint32_t tbase = *holder;
     // half buffer hb: S^T at 128*hb, dP^T at 128*hb + 64; then dV, dK
@@ -1624,6 +1575,7 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
                 }
             }
         }
+        if (lane == 0 && error_set(err)) drain_ring(q_full, SQ, T);   // a wait gave up: let loads land
     } else if (warp == 1) {
         // S^T = K·Q^T and dP^T = V·dO^T per half (N = 64 queries)
         constexpr uint32_t idS = idesc_bf16(128, HQ, 0, 0);
@@ -1671,7 +1623,6 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
 #pragma unroll 1
             for (int hb = 0; hb < 2; ++hb) {
                 mbar_wait(&pd_free[hb], (i & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
-                if (lane == 0 && hb == 0) TRACE(1, i, 1);
                 tc_fence_after();
                 if (lane == 0) {
                     const uint64_t dQh = kdesc(qt + hb * HQ * 128, 0), dOh = kdesc(ot + hb * HQ * 128, 0);
@@ -1681,11 +1632,16 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
                         mma_bf16_ss(tbase + 128 * hb + 64, kdesc_step(dVd, kk), kdesc_step(dOh, kk), idS, kk > 0);
                     }
                     mma_commit(&sd_full[hb]);
-                    if (hb == 1) TRACE(1, i, 2);
                 }
                 __syncwarp();
             }
         }
+        if (lane == 0 && error_set(err)) {   // a wait gave up: let this warp's loads and MMAs finish
+            if (loads > 0) mbar_drain(kv_full, (uint32_t)(loads - 1) & 1u);
+            mma_commit(&drain[0]);
+            mbar_drain(&drain[0], 0);
+        }
+        __syncwarp();
     } else if (warp == 2) {
         // dV += P^T·dO and dK += dS^T·Q per half (K = the half's 64 queries),
         // in tile order: deterministic sums
@@ -1698,7 +1654,6 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
 #pragma unroll 1
             for (int hb = 0; hb < 2; ++hb) {
                 mbar_wait(&pd_full[hb], i & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
-                if (lane == 0 && hb == 0) TRACE(1, i, 3);
                 tc_fence_after();
                 if (lane == 0) {
                     const uint32_t cS = tbase + 128 * hb, cP = cS + 64;
@@ -1718,12 +1673,16 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
                         }
                     }
                     mma_commit(&pd_free[hb]);
-                    if (hb == 1) { mma_commit(&q_empty[st]); TRACE(1, i, 4); }
+                    if (hb == 1) mma_commit(&q_empty[st]);
                 }
                 __syncwarp();
             }
         }
         if (lane == 0) mma_commit(out_full);
+        if (lane == 0 && error_set(err)) {   // a wait gave up: let this warp's MMAs finish
+            mma_commit(&drain[1]);
+            mbar_drain(&drain[1], 0);
+        }
         __syncwarp();
     } else {
         // DKV_NW warpgroups; in each half warpgroup h owns one 16-query group
@@ -1776,7 +1735,6 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
                 const int gq = hb * 4 + h;            // 16-query group of the tile
                 const uint32_t cS = 128 * hb, cP = cS + 64;
                 mbar_wait(&sd_full[hb], i & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
-                if (et == 0 && hb == 0) TRACE(2, i, 0);
                 tc_fence_after();
                 uint32_t rs[16], rp[16];
                 tmem_ld16(tl + cS + h * 16, rs);
@@ -1842,7 +1800,6 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
                 tmem_st_wait();
                 tc_fence_before();
                 epi_arrive(&pd_full[hb]);
-                if (et == 0 && hb == 1) TRACE(2, i, 1);
             }
         }
         if (T > 0) {
@@ -1879,8 +1836,6 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
     }
     tc_fence_before();
     __syncthreads();
-    CTA_MARK(3, 2);
-    if (threadIdx.x == 0) g_cta_n(3, T);
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tbase, 512);
@@ -2198,25 +2153,3 @@ cudaError_t tc_launch_dkdv(const Shape& s, const BwdArgs& a, cudaStream_t st) {
 
 }  // namespace asa
 
-#ifdef ASA_EXP_TRACE
-namespace asa {
-void* exp_trace_ptr_impl();
-}
-extern "C" void* asa_exp_trace_ptr() {
-    void* p = nullptr;
-    cudaGetSymbolAddress(&p, asa::g_trace);
-    return p;
-}
-extern "C" void* asa_exp_cnt_ptr() {
-    void* p = nullptr;
-    cudaGetSymbolAddress(&p, asa::g_cnt);
-    return p;
-}
-#endif
-#ifdef ASA_EXP_CTA
-extern "C" void* asa_exp_cta_ptr() {
-    void* p = nullptr;
-    cudaGetSymbolAddress(&p, asa::g_cta);
-    return p;
-}
-#endif

@@ -7,8 +7,7 @@ import ctypes
 import os
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-# ASA_LIBRARY selects another build of the same C ABI (e.g. an instrumented one).
-LIB_PATH = os.environ.get("ASA_LIBRARY") or os.path.join(HERE, "libasa.so")
+LIB_PATH = os.path.join(HERE, "libasa.so")
 
 ASA_OK, ASA_ERR_INVALID, ASA_ERR_UNSUPPORTED, ASA_ERR_WORKSPACE, ASA_ERR_CUDA, \
     ASA_ERR_DEVICE_TIMEOUT = range(6)
@@ -21,7 +20,8 @@ PRECISION = {"split": 0, "bf16": 1}
 SYMBOLS = ("asa_params_default", "asa_workspace_bytes", "asa_resolve_backend", "asa_tau_mask",
            "asa_forward", "asa_backward", "asa_scrub", "asa_device_error", "asa_status_string",
            "asa_version", "asa_profile_begin", "asa_profile_end", "asa_profile_get",
-           "asa_launch_count", "asa_last_cuda_error", "asa_tau_mask_noalloc")
+           "asa_launch_count", "asa_last_cuda_error", "asa_tau_mask_noalloc",
+           "asa_device_error_async", "asa_wait_probe")
 NOALLOC_SCRATCH_BYTES = 1 << 20
 
 
@@ -80,6 +80,8 @@ def lib():
         L.asa_launch_count.argtypes = []
         L.asa_launch_count.restype = ctypes.c_longlong
         L.asa_tau_mask_noalloc.argtypes = [pp, vp, vp, vp, vp, vp, vp, vp, vp, vp]
+        L.asa_device_error_async.argtypes = [vp, ctypes.POINTER(ctypes.c_int)]
+        L.asa_wait_probe.argtypes = [ctypes.c_longlong, vp]
         L.asa_last_cuda_error.argtypes = []
         L.asa_last_cuda_error.restype = ctypes.c_char_p
         for name in SYMBOLS:

@@ -176,10 +176,13 @@ def forward_saved(Q, K, V, Q_idx, K_idx, st: Settings, need_o32=True):
     s.params = (p, qi, ki)
     fwd, _ = _workspace(p, dev)
     ws = torch.empty(fwd, device=dev, dtype=torch.uint8)
+    check_device_errors(dev)
     L.check(L.lib().asa_forward(ctypes.byref(p), _ptr(Q), _ptr(K), _ptr(V), _ptr(qi), _ptr(ki),
                                 _ptr(O), _ptr(O32), _ptr(s.tau), _ptr(s.M), _ptr(s.csr_ptr),
                                 _ptr(s.csr_idx), _ptr(s.rownorm), _ptr(ws), fwd, _stream()),
             "asa_forward")
+    if not need_o32:   # no backward will follow: read the error word now
+        _poll_device_errors(dev)
     return O, s
 
 
@@ -195,11 +198,13 @@ def backward_saved(Q, K, V, dO, s: Saved):
     dV = torch.empty(V.shape, device=dev, dtype=out_dt)
     _, bwd = _workspace(p, dev)
     ws = torch.empty(bwd, device=dev, dtype=torch.uint8)
+    check_device_errors(dev)
     L.check(L.lib().asa_backward(ctypes.byref(p), _ptr(Q), _ptr(K), _ptr(V), _ptr(qi), _ptr(ki),
                                  _ptr(s.O32), _ptr(s.tau), _ptr(s.M), _ptr(s.csr_ptr),
                                  _ptr(s.csr_idx), _ptr(s.rownorm), _ptr(dO), _ptr(dQ), _ptr(dK),
                                  _ptr(dV), _ptr(ws), bwd, _stream()),
             "asa_backward")
+    _poll_device_errors(dev)
     return dQ, dK, dV
 
 
@@ -212,11 +217,55 @@ def scrub_(x):
 
 
 def device_error(device=None):
-    """Read and clear the device error word (bounded waits that ran out)."""
+    """Read and clear the device error word (bounded waits that ran out).
+    Synchronises the current stream."""
     code = ctypes.c_int()
     with torch.cuda.device(device):
         L.check(L.lib().asa_device_error(_stream(), ctypes.byref(code)), "asa_device_error")
     return code.value
+
+
+# Per device: a pinned host int that receives asynchronous copies of the
+# device error word after each backward (and each forward that saves nothing
+# for a backward).  A copy that has landed with a non-zero value makes the
+# next call raise -- the reference raises from CUDA_CHECK / TORCH_CHECK after
+# its synchronising launches (:24-27); here no call synchronises, so the
+# report comes one call later, or from device_error() at any time.
+_err_words = {}
+
+
+def _error_word(dev):
+    w = _err_words.get(dev)
+    if w is None:
+        w = torch.zeros(1, dtype=torch.int32, pin_memory=True)
+        _err_words[dev] = w
+    return w
+
+
+def check_device_errors(dev):
+    """Raise AsaError(ASA_ERR_DEVICE_TIMEOUT) if an earlier asynchronous
+    read of the device error word on `dev` saw a timed-out wait."""
+    w = _err_words.get(dev)
+    if w is not None and int(w[0]) != 0:
+        code = int(w[0])
+        w[0] = 0
+        with torch.cuda.device(dev):
+            device_error()          # clears the device word
+        raise L.AsaError(code, "a previous splash_attention call on this device")
+
+
+def _poll_device_errors(dev):
+    w = _error_word(dev)
+    code = ctypes.c_int.from_address(w.data_ptr())
+    L.check(L.lib().asa_device_error_async(_stream(), ctypes.byref(code)),
+            "asa_device_error_async")
+
+
+def wait_probe(spins=1000):
+    """Launch the library's device-timeout self-test on the current stream:
+    a wait that nothing completes gives up after `spins` polls and records
+    ASA_ERR_DEVICE_TIMEOUT in the device error word."""
+    L.check(L.lib().asa_wait_probe(int(spins), _stream()), "asa_wait_probe")
 
 
 class profile:

@@ -48,9 +48,20 @@ def sharded_attention(Q, K, V, Q_idx, K_idx, rank=None, world=None, **kw):
     if world is None:
         world = int(os.environ.get("WORLD_SIZE", 1))
     q, k, v = (local_heads(x, rank, world) for x in (Q, K, V))
-    qi = local_heads(Q_idx, rank, world) if Q_idx is not None and Q_idx.dim() == 2 else Q_idx
-    ki = local_heads(K_idx, rank, world) if K_idx is not None and K_idx.dim() == 2 else K_idx
-    return splash_attention(q, k, v, qi, ki, **kw)
+    return splash_attention(q, k, v, _local_positions(Q_idx, Q, rank, world),
+                            _local_positions(K_idx, K, rank, world), **kw)
+
+
+def _local_positions(idx, X, rank, world):
+    """This rank's rows of a position tensor: [N] broadcasts to every head;
+    [B*H, N] and [B, H, N] are flattened to heads and sliced."""
+    if idx is None or idx.dim() == 1:
+        return idx
+    B, H, N = X.shape[0], X.shape[1], X.shape[2]
+    if idx.dim() not in (2, 3) or idx.numel() != B * H * N:
+        raise ValueError(f"sharded_attention: positions must be [N], [B*H, N] or [B, H, N] "
+                         f"with B*H = {B * H} and N = {N}; got {tuple(idx.shape)}")
+    return local_heads(idx.reshape(B * H, N), rank, world)
 
 
 def gather_heads(local, world, group=None):

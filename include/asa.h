@@ -156,6 +156,21 @@ int asa_scrub(int dtype, void* x, size_t n, void* ws, asa_stream_t stream);
  * wait runs out.  Synchronises the stream.  *code is 0 when no error. */
 int asa_device_error(asa_stream_t stream, int* code);
 
+/* Enqueues on `stream` a copy of the device error word into *host_word
+ * (pinned host memory, for the copy to stay asynchronous) without clearing
+ * it or synchronising: a caller checks the value after a later
+ * synchronisation point and then reads and clears the word with
+ * asa_device_error.  No counterpart in the reference, whose host launchers
+ * synchronise and raise after every call (CUDA_CHECK, :24-27). */
+int asa_device_error_async(asa_stream_t stream, int* host_word);
+
+/* Self-test of the device-side timeout path: launches one block whose wait
+ * on a barrier phase that nothing completes gives up after `spins` polls and
+ * records ASA_ERR_DEVICE_TIMEOUT in the device error word (read it with
+ * asa_device_error).  The kernel returns on its own and leaves no work in
+ * flight.  No counterpart in the reference. */
+int asa_wait_probe(long long spins, asa_stream_t stream);
+
 /* Per-launch timing for benchmarks and tracing (no counterpart in the
  * reference, which only wall-clocks whole calls, nb:1791-1796).
  * asa_profile_begin(1) makes every entry point record a CUDA event before

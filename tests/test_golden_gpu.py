@@ -48,5 +48,5 @@ def test_engine_matches_reference_kernels(cuda, name):
         rk = r[k]
         if k in ("O", "dQ"):
             gk, rk = gk[:, :full], rk[:, :full]
-        e = np.abs(rk - gk).max() / max(1.0, np.abs(gk).max())
-        assert e <= 1e-5, f"{k}: scaled max-abs {e:.3g}"
+        e = np.abs(rk - gk).max()
+        assert e <= 1e-5, f"{k}: max-abs {e:.3g} (unscaled bound 1e-5)"

@@ -46,10 +46,14 @@ def test_oracle_matches_reference_kernels(name):
     err = np.abs(r["tau"][:, :full] - g["tau"][:, :full]) - (
         TAU_ATOL + TAU_RTOL * np.abs(g["tau"][:, :full]))
     assert (err <= 0).all(), f"τ differs: worst excess {err.max():.3g}"
-    # fp32 inputs: 1e-5 max-abs, scaled by max(1, max|ref|); the reference's
-    # dK/dV come from unordered fp32 atomics and its powf is CUDA's.
+    # fp32 inputs: 1e-5 max-abs.  Where α makes the exponents non-integral
+    # (α = 1.3) both sides call powf -- the oracle libm's, the reference
+    # CUDA's, which differ by up to an ulp -- so there the bound is scaled by
+    # max(1, max|ref|) (measured: dQ 1.2e-5 at |dQ| <= 4.1).  The reference's
+    # dK/dV also come from unordered fp32 atomics.
     for k in ("O", "dQ") + (() if partial else ("dK", "dV")):
         gk = g[k].reshape(r[k].shape)[:, :full] if k in ("O", "dQ") else g[k].reshape(r[k].shape)
         rk = r[k][:, :full] if k in ("O", "dQ") else r[k]
-        e = np.abs(rk - gk).max() / max(1.0, np.abs(gk).max())
-        assert e <= 1e-5, f"{k}: scaled max-abs {e:.3g}"
+        scale = max(1.0, np.abs(gk).max()) if s["alpha"] not in (1.25, 1.5, 2.0) else 1.0
+        e = np.abs(rk - gk).max()
+        assert e <= 1e-5 * scale, f"{k}: max-abs {e:.3g} > {1e-5 * scale:.3g}"

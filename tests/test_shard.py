@@ -30,3 +30,26 @@ def test_two_ranks_gloo_equal_single_process():
 def test_failed_rank_is_reported():
     with pytest.raises(RuntimeError, match="rank 1 failed.*injected failure"):
         launch(shard_workers.fails_on_rank1, 2, backend="gloo", port=29562, timeout=120)
+
+
+@pytest.mark.parametrize("shape", [(2, 3, 40), (6, 40), (40,)])
+def test_local_positions_accepts_every_position_layout(shape):
+    import torch
+    from splash_attention.shard import _local_positions, partition
+    X = torch.zeros(2, 3, 40, 8)
+    idx = torch.arange(2 * 3 * 40).reshape(6, 40) if len(shape) > 1 else torch.arange(40)
+    idx = idx.reshape(shape)
+    for rank in range(4):
+        got = _local_positions(idx, X, rank, 4)
+        if len(shape) == 1:
+            assert got is idx
+            continue
+        s, e = partition(6, 4)[rank]
+        assert torch.equal(got, idx.reshape(6, 40)[s:e])
+
+
+def test_local_positions_rejects_mismatched_shapes():
+    import torch
+    from splash_attention.shard import _local_positions
+    with pytest.raises(ValueError, match="positions must be"):
+        _local_positions(torch.zeros(5, 40), torch.zeros(2, 3, 40, 8), 0, 2)
