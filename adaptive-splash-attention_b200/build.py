@@ -4,7 +4,8 @@
 
 Objects go to adaptive-splash-attention_b200/_build/; the library lands in
 adaptive-splash-attention_b200/splash_attention/libasa.so, next to the
-Python package that loads it.
+Python package that loads it, and the PyTorch operator library over it in
+splash_attention/_torch_ops.so.
 """
 import concurrent.futures as cf
 import os
@@ -26,7 +27,8 @@ TC_PARTS = [("asa_tc.cu", part) for part in (1, 2, 3, 4)]
 
 
 def _deps():
-    return [os.path.join(CSRC, f) for f in os.listdir(CSRC)] + [
+    return [os.path.join(CSRC, f) for f in os.listdir(CSRC)
+            if f.endswith((".cu", ".cuh", ".h"))] + [
         os.path.join(HERE, "..", "include", "asa.h")]
 
 
@@ -65,5 +67,36 @@ def build(force: bool = False) -> str:
     return LIB
 
 
+TORCH_OPS = os.path.join(HERE, "splash_attention", "_torch_ops.so")
+
+
+def build_torch_ops(force: bool = False) -> str:
+    """The TORCH_LIBRARY operators (csrc/torch_ops.cpp): host C++ against
+    PyTorch's headers, linked to libasa.so (found next to it at run time)."""
+    import torch
+    import torch.utils.cpp_extension as ce
+    src = os.path.join(CSRC, "torch_ops.cpp")
+    deps = [src, os.path.join(HERE, "..", "include", "asa.h"), LIB]
+    if (not force and os.path.exists(TORCH_OPS)
+            and os.path.getmtime(TORCH_OPS) >= max(os.path.getmtime(p) for p in deps)):
+        return TORCH_OPS
+    cuda_home = os.path.dirname(os.path.dirname(NVCC))
+    abi = int(torch._C._GLIBCXX_USE_CXX11_ABI)
+    cmd = ["g++", "-O2", "-std=c++17", "-fPIC", "-shared", f"-D_GLIBCXX_USE_CXX11_ABI={abi}",
+           src, "-o", TORCH_OPS + ".tmp", "-I", os.path.join(cuda_home, "include")]
+    for p in ce.include_paths():
+        cmd += ["-isystem", p]
+    for p in ce.library_paths():
+        cmd += ["-L", p, f"-Wl,-rpath,{p}"]
+    cmd += ["-L", os.path.dirname(LIB), "-l:libasa.so", "-Wl,-rpath,$ORIGIN",
+            "-lc10", "-lc10_cuda", "-ltorch_cpu", "-ltorch_cuda", "-ltorch"]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"g++ failed for torch_ops.cpp:\n{r.stdout}\n{r.stderr}")
+    os.replace(TORCH_OPS + ".tmp", TORCH_OPS)
+    return TORCH_OPS
+
+
 if __name__ == "__main__":
     print(build(force="--force" in sys.argv))
+    print(build_torch_ops(force="--force" in sys.argv))

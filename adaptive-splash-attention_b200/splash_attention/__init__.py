@@ -16,14 +16,23 @@ Drop-in surface of mvideet/Adaptive-Splash-Attention:
 Every computation runs in hand-written CUDA kernels for sm_100a behind the C
 ABI of include/asa.h (libasa.so).  There is no CPU fallback.
 """
+import os
+
 import torch
 
 from . import _lib
 from .ops import Settings, forward_saved, backward_saved, tau_mask, scrub_, device_error, \
-    resolved_backend, make_params
+    resolved_backend, make_params, _index, _check_inputs
 from .streamed import forward_backward_host
 
 _lib.lib()  # fail at import time if the native library is missing
+
+_TORCH_OPS = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_torch_ops.so")
+if not os.path.exists(_TORCH_OPS):
+    raise ImportError(f"splash_attention: {_TORCH_OPS} is missing; build it with "
+                      "`python adaptive-splash-attention_b200/build.py` (no fallback path exists)")
+torch.ops.load_library(_TORCH_OPS)
+_ops = torch.ops.splash_attention
 
 __all__ = ["AdaptiveSplashAttention", "splash_attention", "forward", "backward", "tau_mask",
            "Settings", "device_error", "forward_backward_host"]
@@ -32,21 +41,35 @@ __all__ = ["AdaptiveSplashAttention", "splash_attention", "forward", "backward",
 REF_BLOCK_M, REF_BLOCK_N, REF_K_KEEP = 32, 64, 8
 
 
-class _SplashFn(torch.autograd.Function):
-    @staticmethod
-    def forward(ctx, Q, K, V, Q_idx, K_idx, st):
-        O, saved = forward_saved(Q, K, V, Q_idx, K_idx, st,
-                                 need_o32=any(ctx.needs_input_grad[:3]))
-        ctx.saved = saved
-        ctx.save_for_backward(Q, K, V)
-        return O
+def _op_config(Q, st: Settings):
+    """The scalar arguments of splash_attention::forward / ::backward."""
+    out_dt = st.out_dtype if st.out_dtype is not None else Q.dtype
+    if out_dt not in (torch.float32, torch.bfloat16):
+        raise TypeError(f"splash_attention: unsupported out_dtype {out_dt}")
+    sm_scale = st.sm_scale if st.sm_scale is not None else Q.shape[-1] ** -0.5
+    return (float(st.alpha), float(sm_scale), int(st.k_keep), int(st.block_m), int(st.block_n),
+            bool(st.causal), _lib.BACKEND[st.backend], _lib.PRECISION[st.precision],
+            out_dt == torch.float32, bool(st.ref_tile_load))
 
-    @staticmethod
-    def backward(ctx, dO):
-        Q, K, V = ctx.saved_tensors
-        dQ, dK, dV = backward_saved(Q, K, V, dO, ctx.saved)
-        dQ, dK, dV = (g.to(t.dtype) for g, t in zip((dQ, dK, dV), (Q, K, V)))
-        return dQ, dK, dV, None, None, None
+
+def _setup_context(ctx, inputs, output):
+    Q, K, V, Qi, Ki = inputs[:5]
+    O, O32, tau, M, ptr, idx, rown = output
+    ctx.mark_non_differentiable(O32, tau, M, ptr, idx, rown)
+    ctx.save_for_backward(Q, K, V, Qi, Ki, O32 if O32.numel() else O, tau, M, ptr, idx, rown)
+    ctx.cfg = tuple(inputs[5:-1])      # everything but need_o32
+
+
+def _backward(ctx, dO, *_unused):
+    Q, K, V, Qi, Ki, O32, tau, M, ptr, idx, rown = ctx.saved_tensors
+    if dO is None:
+        return (None,) * 16
+    dQ, dK, dV = _ops.backward(Q, K, V, Qi, Ki, O32, tau, M, ptr, idx, rown, dO, *ctx.cfg)
+    return (dQ.to(Q.dtype), dK.to(K.dtype), dV.to(V.dtype)) + (None,) * 13
+
+
+torch.library.register_autograd("splash_attention::forward", _backward,
+                                setup_context=_setup_context)
 
 
 def splash_attention(Q, K, V, Q_idx=None, K_idx=None, *, alpha=1.5, sm_scale=None, k_keep=8,
@@ -57,6 +80,10 @@ def splash_attention(Q, K, V, Q_idx=None, K_idx=None, *, alpha=1.5, sm_scale=Non
     integer dtype; [N] broadcasts).  Key k is visible to query q iff
     K_idx[k] <= Q_idx[q] (causal=False: every key).
 
+    Runs the registered operator splash_attention::forward (C++ over the C
+    ABI; traceable through its Meta kernel), whose autograd formula calls
+    splash_attention::backward.
+
     ref_tile_load=True reproduces the reference kernels' tile staging, in
     which a visible key's K/V elements are zeroed when the reference thread
     that loads them serves a query that cannot see the key; False reads every
@@ -64,7 +91,13 @@ def splash_attention(Q, K, V, Q_idx=None, K_idx=None, *, alpha=1.5, sm_scale=Non
     st = Settings(alpha=alpha, sm_scale=sm_scale, k_keep=k_keep, block_m=block_m,
                   block_n=block_n, causal=causal, backend=backend, precision=precision,
                   out_dtype=out_dtype, ref_tile_load=ref_tile_load)
-    return _SplashFn.apply(Q, K, V, Q_idx, K_idx, st)
+    if Q.device.type != "meta":
+        _check_inputs(Q, K, V)
+    BH = Q.shape[0] * Q.shape[1]
+    qi = _index(Q_idx, BH, Q.shape[2], Q.device, "Q_idx") if causal else None
+    ki = _index(K_idx, BH, K.shape[2], Q.device, "K_idx") if causal else None
+    need_o32 = torch.is_grad_enabled() and any(t.requires_grad for t in (Q, K, V))
+    return _ops.forward(Q, K, V, qi, ki, *_op_config(Q, st), need_o32)[0]
 
 
 class AdaptiveSplashAttention(torch.nn.Module):

@@ -378,8 +378,9 @@ def measure(a, c, name, rank, world, dev, scaling, dist, with_extras=True):
                        "peak_kind": f"{peak_kind} bf16 burst (of measured)",
                        "kernels_ms": {k_: round(v_[0], 4) for k_, v_ in kern.items()}}
     if "tau_mask" in kern:
-        # the τ/mask pass: compulsory HBM bytes (Q and K read once, τ and M written)
-        tm_ms = kern["tau_mask"][0] / max(kern["tau_mask"][1], 1)
+        # the τ/mask pass (all its launches: bounds, top-k + mask, τ solve):
+        # compulsory HBM bytes (Q and K read once, τ and M written)
+        tm_ms = kern["tau_mask"][0]
         elt = 4 if c["dtype"] == "f32" else 2
         tm_bytes = h_local * (2 * N * c["d"] * elt + N * 4 + nqb * nkb)
         rec["tau_mask"] = {"ms": tm_ms, "hbm_gbs": tm_bytes / (tm_ms * 1e-3) / 1e9,
@@ -410,10 +411,15 @@ def measure(a, c, name, rank, world, dev, scaling, dist, with_extras=True):
             h2d = sum(x.numel() * x.element_size() for x in (hQ, hK, hV, hdO))
             d2h = sum(x.numel() * x.element_size() for x in outs)
 
+            # chunks of at least 16 MiB of inputs: small heads in tiny chunks
+            # leave the GPU idle between copies
+            head_bytes = 4 * N * c["d"] * Q.element_size()
+            chunk = max(a.e2e_chunk, -(-(16 << 20) // head_bytes))
+
             def e2e_step():
                 sa.forward_backward_host(hQ, hK, hV, hdO, hidx, hidx, out=outs,
-                                         heads_per_chunk=a.e2e_chunk, synchronize=False, **st)
-            api = (f"splash_attention.forward_backward_host (pinned host in/out, {a.e2e_chunk} "
+                                         heads_per_chunk=chunk, synchronize=False, **st)
+            api = (f"splash_attention.forward_backward_host (pinned host in/out, {chunk} "
                    "heads per chunk, copies overlapped with kernels)")
         for _ in range(2):
             e2e_step()
