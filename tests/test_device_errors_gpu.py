@@ -29,10 +29,9 @@ def test_python_surface_raises_after_a_timeout(cuda):
     with torch.no_grad():   # enqueues the asynchronous read of the error word
         splash_attention(q, q, q, idx, idx, block_m=64, block_n=64)
     torch.cuda.synchronize()
-    with pytest.raises(RuntimeError, match="timed out") as ei:
+    with pytest.raises(RuntimeError, match=r"timed out \(asa_status 5\)"):
         with torch.no_grad():
             splash_attention(q, q, q, idx, idx, block_m=64, block_n=64)
-    assert ei.value.code == L.ASA_ERR_DEVICE_TIMEOUT
     assert ops.device_error() == 0          # the raise cleared the word
     with torch.no_grad():                   # and the context is still usable
         out = splash_attention(q, q, q, idx, idx, block_m=64, block_n=64)
