@@ -24,6 +24,9 @@ size_t tc_bwd_workspace(const Shape& s);
 cudaError_t tc_tau_mask(const Shape& s, const void* Q, const void* K, const int32_t* Qidx,
                         const int32_t* Kidx, float* tau, uint8_t* M, void* ws, int* err,
                         cudaStream_t st);
+cudaError_t tc_exact_tau(const Shape& s, const void* Q, const void* K, const int32_t* Qidx,
+                         const int32_t* Kidx, float* tau, uint8_t* M, void* ws, int* err,
+                         cudaStream_t st);
 cudaError_t tc_forward(const Shape& s, const void* Q, const void* K, const void* V,
                        const int32_t* Qidx, const int32_t* Kidx, const float* tau,
                        const int32_t* ptr, const int32_t* idx, void* O, float* O32,
@@ -119,6 +122,8 @@ int check_params(const asa_params* p) {
         return ASA_ERR_INVALID;
     if (p->backend < ASA_BACKEND_AUTO || p->backend > ASA_BACKEND_TC) return ASA_ERR_INVALID;
     if (p->precision != ASA_PREC_SPLIT && p->precision != ASA_PREC_BF16) return ASA_ERR_INVALID;
+    if (p->tau_mode != ASA_TAU_REFERENCE && p->tau_mode != ASA_TAU_EXACT) return ASA_ERR_INVALID;
+    if (p->grad_mode != ASA_GRAD_REFERENCE && p->grad_mode != ASA_GRAD_JACOBIAN) return ASA_ERR_INVALID;
     if (p->d > 128) return ASA_ERR_UNSUPPORTED;        // reference D_MAX (:14-16)
     if (p->k_keep > 32) return ASA_ERR_UNSUPPORTED;
     const long long BH = (long long)p->B * p->H;
@@ -148,7 +153,10 @@ Shape make_shape(const asa_params* p) {
     s.spins = p->timeout_spins > 0 ? p->timeout_spins : (1LL << 22);
     s.in_dtype = p->in_dtype;
     s.out_dtype = p->out_dtype;
-    s.ref_load = (p->ref_tile_load && p->causal) ? 1 : 0;
+    s.exact_tau = p->tau_mode == ASA_TAU_EXACT ? 1 : 0;
+    s.jacobian = p->grad_mode == ASA_GRAD_JACOBIAN ? 1 : 0;
+    // the exact threshold is a property of the rows as given: no tile-load zeroing
+    s.ref_load = (p->ref_tile_load && p->causal && !s.exact_tau) ? 1 : 0;
     s.split = p->precision == ASA_PREC_SPLIT ? 1 : 0;
     return s;
 }
@@ -223,6 +231,8 @@ void asa_params_default(asa_params* p) {
     p->backend = ASA_BACKEND_AUTO;
     p->precision = ASA_PREC_SPLIT;
     p->ref_tile_load = 1;
+    p->tau_mode = ASA_TAU_REFERENCE;
+    p->grad_mode = ASA_GRAD_REFERENCE;
 }
 
 int asa_resolve_backend(const asa_params* p) {
@@ -258,7 +268,10 @@ int asa_tau_mask(const asa_params* p, const void* Q, const void* K, const int32_
     cudaError_t e;
     {
         ProfScope ps("tau_mask", st);
-        if (b == ASA_BACKEND_TC)
+        if (s.exact_tau)
+            e = b == ASA_BACKEND_TC ? asa::tc_exact_tau(s, Q, K, Qidx, Kidx, tau, M, ws, error_word(), st)
+                                    : asa::simt_exact_tau(s, Q, K, Qidx, Kidx, tau, M, st);
+        else if (b == ASA_BACKEND_TC)
             e = asa::tc_tau_mask(s, Q, K, Qidx, Kidx, tau, M, ws, error_word(), st);
         else
             e = asa::simt_tau_mask(s, Q, K, Qidx, Kidx, tau, M, st);
@@ -346,7 +359,9 @@ int asa_backward(const asa_params* p, const void* Q, const void* K, const void* 
     }
     {
         ProfScope ps("bwd_rowstats", st);
-        e = asa::simt_rowstats(s, Q, K, V, Qidx, Kidx, tau, csr_ptr, csr_idx, dO, invN, accdO, st);
+        e = s.jacobian
+                ? asa::simt_jacobian_stats(s, Q, K, V, Qidx, Kidx, tau, csr_ptr, csr_idx, dO, invN, accdO, st)
+                : asa::simt_rowstats(s, Q, K, V, Qidx, Kidx, tau, csr_ptr, csr_idx, dO, invN, accdO, st);
     }
     if (e == cudaSuccess) {
         ProfScope ps("bwd_dq", st);
@@ -508,6 +523,6 @@ const char* asa_status_string(int status) {
     }
 }
 
-int asa_version(void) { return 100; }
+int asa_version(void) { return 200; }
 
 }  // extern "C"

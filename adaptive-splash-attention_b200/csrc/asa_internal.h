@@ -24,7 +24,14 @@ struct Shape {
     int in_dtype, out_dtype;
     int ref_load;    // reproduce the reference's tile-load zeroing (causal only)
     int split;       // tcgen05 path: P and dS enter the MMAs as bf16 hi+lo pairs
+    int exact_tau;   // asa_tau_mode ASA_TAU_EXACT
+    int jacobian;    // asa_grad_mode ASA_GRAD_JACOBIAN
 };
+
+// Passes of the exact-τ solve: one for the row maximum, then Newton steps
+// (bisection-safeguarded) on Σ u_+^{1/(α-1)} = 1 from the left end of the
+// bracket [(α-1)s_max - 1, (α-1)s_max].
+constexpr int kExactPasses = 10;
 
 // Whether element `t` of key row `kn` survives the reference's tile staging
 // for consumers in query block `qb`: the reference thread that stages it
@@ -62,6 +69,13 @@ cudaError_t simt_dkdv(const Shape& s, const void* Q, const void* K, const void* 
                       const int32_t* cptr, const int32_t* cidx, const void* dO,
                       const float* invN, const float* accdO, void* dK, void* dV,
                       cudaStream_t st);
+
+cudaError_t simt_exact_tau(const Shape& s, const void* Q, const void* K, const int32_t* Qidx,
+                           const int32_t* Kidx, float* tau, uint8_t* M, cudaStream_t st);
+cudaError_t simt_jacobian_stats(const Shape& s, const void* Q, const void* K, const void* V,
+                                const int32_t* Qidx, const int32_t* Kidx, const float* tau,
+                                const int32_t* ptr, const int32_t* idx, const void* dO,
+                                float* invN, float* accdO, cudaStream_t st);
 
 // ---- tile lists (asa_compact.cu) --------------------------------------------
 // CSR of M in the reference's format (build_lookup_kernel :219-242), and the

@@ -147,9 +147,107 @@ simt_tau_mask_kernel(Shape sh, const T* __restrict__ Q, const T* __restrict__ K,
 
 
 // ---------------------------------------------------------------------------
+// Exact α-entmax threshold (asa_tau_mode ASA_TAU_EXACT): τ with
+// Σ_j [(α-1)s_j - τ]_+^{1/(α-1)} = 1 over every visible key of the row.  One
+// thread per query, kExactPasses passes over the keys: the first finds the
+// row maximum s_max, which brackets τ in [(α-1)s_max - 1, (α-1)s_max]; each
+// later pass evaluates F(τ) = Σ u_+^{1/(α-1)} and Σ u_+^{(2-α)/(α-1)} and
+// takes a Newton step (F is convex and decreasing, so from the bracket's
+// left end the steps climb monotonically), falling back to bisection when a
+// step leaves the bracket.  The last pass also sets M for every tile that
+// holds a positive weight at the bracket's left end, which bounds the final
+// τ from below: a superset of the tiles the final τ leaves weight in.
+// No counterpart in the reference (whose τ comes from the top-k only,
+// :51-148); K is staged without the reference's tile-load zeroing.
+// ---------------------------------------------------------------------------
+template <typename T, int DM>
+__global__ void __launch_bounds__(QTHREADS)
+simt_exact_tau_kernel(Shape sh, const T* __restrict__ Q, const T* __restrict__ K,
+                      const int32_t* __restrict__ Qidx, const int32_t* __restrict__ Kidx,
+                      float* __restrict__ tau, uint8_t* __restrict__ M) {
+    __shared__ float Ks[KT][DM];
+    __shared__ int Kp[KT];
+    __shared__ int red[QTHREADS / 32];
+    const int QT = blockDim.x;
+    const int tid = threadIdx.x;
+    const int bh = blockIdx.y;
+    const int subs = (sh.BM + QT - 1) / QT;
+    const int qb = blockIdx.x / subs;
+    const int inblk = (blockIdx.x % subs) * QT + tid;
+    const int q = qb * sh.BM + inblk;
+    const bool qv = inblk < sh.BM && q < sh.NQ;
+    const int d = sh.d;
+    const size_t qrow = (size_t)bh * sh.NQ + (qv ? q : 0);
+
+    float qr[DM];
+#pragma unroll
+    for (int t = 0; t < DM; ++t) qr[t] = (qv && t < d) ? to_f(Q[qrow * d + t]) : 0.0f;
+    const int qpos = !qv ? INT_MIN : (sh.causal ? Qidx[qrow] : INT_MAX);
+    const int cta_max = block_qmax(qpos, red);
+    const float inv = __fdiv_rn(1.0f, sh.am1);
+    float smax = -INFINITY, tq = 0.0f, lo = 0.0f, hi = 0.0f;
+    uint8_t* Mrow = M + ((size_t)bh * sh.nQB + qb) * sh.nKB;
+    for (int pass = 0; pass < kExactPasses; ++pass) {
+        const bool last = pass == kExactPasses - 1;
+        float F = 0.0f, Dd = 0.0f;
+        for (int start = 0; start < sh.NK; start += KT) {
+            int any = 0;
+            if (tid < KT) {
+                const int kn = start + tid;
+                const int kp = kn < sh.NK ? (sh.causal ? Kidx[(size_t)bh * sh.NK + kn] : INT_MIN) : INT_MAX;
+                Kp[tid] = kp;
+                any = (kn < sh.NK) && kp <= cta_max;
+            }
+            if (!__syncthreads_or(any)) continue;
+            for (int x = tid; x < KT * DM; x += QT) {
+                const int j = x / DM, t = x % DM, kn = start + j;
+                Ks[j][t] = (kn < sh.NK && t < d) ? to_f(K[((size_t)bh * sh.NK + kn) * d + t]) : 0.0f;
+            }
+            __syncthreads();
+            if (qv) {
+                for (int j = 0; j < KT; ++j) {
+                    const int kn = start + j;
+                    if (kn >= sh.NK || !(Kp[j] <= qpos)) continue;
+                    float a = 0.0f;
+#pragma unroll
+                    for (int t = 0; t < DM; ++t)
+                        if (t < d) a = __fmaf_rn(qr[t], Ks[j][t], a);
+                    const float sc = clamp_score(a, sh.scale);
+                    if (pass == 0) { smax = fmaxf(smax, sc); continue; }
+                    const float u = __fmaf_rn(sh.am1, sc, -tq);
+                    if (u > 0.0f) {
+                        const float p = pow_exact(u, sh.pinv), w = pow_exact(u, sh.pe2);
+                        if (isfinite(p)) F += p;
+                        if (isfinite(w)) Dd += w;
+                    }
+                    if (last && __fmaf_rn(sh.am1, sc, -lo) > 0.0f) Mrow[kn / sh.BN] = 1;
+                }
+            }
+            __syncthreads();
+        }
+        if (pass == 0) {
+            if (!(smax > -INFINITY)) smax = 0.0f;     // no visible key: no weight anywhere
+            hi = __fmul_rn(sh.am1, smax);
+            lo = __fadd_rn(hi, -1.0f);
+            tq = lo;
+            continue;
+        }
+        const float g = F - 1.0f;
+        if (g >= 0.0f) lo = tq; else hi = tq;
+        float tn = (Dd > 0.0f) ? tq + g / (inv * Dd) : tq;
+        if (!(tn >= lo && tn <= hi)) tn = 0.5f * (lo + hi);
+        tq = tn;
+    }
+    if (qv) tau[qrow] = tq;
+}
+
+// ---------------------------------------------------------------------------
 // Query-major walk over a query block's active tiles (CSR order, keys
 // ascending), shared by the forward (MODE 0), the backward's row statistics
-// (MODE 1) and dQ (MODE 2).  Each thread owns one query row; its q (and dO)
+// (MODE 1), dQ (MODE 2) and the row statistics of the Jacobian gradient
+// (MODE 3: accdO = (n + EPS)·Σ_j w_j (v_j·dO) / Σ_j w_j with
+// w = u^{(2-α)/(α-1)}, so that dQ/dK/dV's "accdO·invN" term becomes the
+// w-weighted mean of v·dO).  Each thread owns one query row; its q (and dO)
 // row sits in padded shared memory, K/V chunks are read as broadcasts.
 // References: splash_forward_sparse :244-341, splash_backward_sparse pass 1
 // :395-437 and pass 2's dQ part :439-534.
@@ -176,8 +274,9 @@ simt_rows_kernel(Shape sh, const T* __restrict__ Q, const T* __restrict__ K,
     const size_t qrow = (size_t)bh * sh.NQ + (qv ? q : 0);
     constexpr int LD = DM + 1;
     float* qs = smem;                          // [QT][DM+1]
-    float* gs_ = qs + QT * LD;                 // [QT][DM+1] dO rows (MODE 2)
-    float* Ks = gs_ + (MODE == 2 ? QT * LD : 0);
+    constexpr bool kDO = MODE >= 2;            // dO rows staged (MODE 2 and 3)
+    float* gs_ = qs + QT * LD;                 // [QT][DM+1] dO rows
+    float* Ks = gs_ + (kDO ? QT * LD : 0);
     float* Vs = Ks + KT * DM;
     __shared__ int Kp[KT];
     __shared__ int red[QTHREADS / 32];
@@ -186,7 +285,7 @@ simt_rows_kernel(Shape sh, const T* __restrict__ Q, const T* __restrict__ K,
 
     for (int t = 0; t < DM; ++t) {
         qs[tid * LD + t] = (qv && t < d) ? to_f(Q[qrow * d + t]) : 0.0f;
-        if (MODE == 2) gs_[tid * LD + t] = (qv && t < d) ? to_f(dO[qrow * d + t]) : 0.0f;
+        if (kDO) gs_[tid * LD + t] = (qv && t < d) ? to_f(dO[qrow * d + t]) : 0.0f;
     }
     const int qpos = !qv ? INT_MIN : (sh.causal ? Qidx[qrow] : INT_MAX);
     const float tq = qv ? tau[qrow] : 0.0f;
@@ -198,6 +297,7 @@ simt_rows_kernel(Shape sh, const T* __restrict__ Q, const T* __restrict__ K,
 #pragma unroll
     for (int t = 0; t < DM; ++t) acc[t] = 0.0f;
     float n = 0.0f;
+    float wA = 0.0f, wB = 0.0f;                // MODE 3: Σ w·(v·dO), Σ w
 
     const int32_t* p = ptr + (size_t)bh * (sh.nQB + 1);
     const int32_t* ix = idx + (size_t)bh * sh.nQB * sh.nKB;
@@ -232,7 +332,20 @@ simt_rows_kernel(Shape sh, const T* __restrict__ Q, const T* __restrict__ K,
                 const float s = clamp_score(a, sh.scale);
                 float u;
                 const float pr = entmax_p(s, sh.am1, tq, sh.pinv, &u);
-                if (MODE != 2) {
+                if (MODE == 3) {
+                    n = __fadd_rn(n, pr);
+                    if (u > ASA_EPS) {
+                        const float w = pow_exact(fmaxf(u, ASA_EPS), sh.pe2);
+                        if (isfinite(w)) {
+                            float vd = 0.0f;
+#pragma unroll
+                            for (int t = 0; t < DM; ++t)
+                                if (t < d) vd = __fmaf_rn(Vs[j * DM + t], gs_[tid * LD + t], vd);
+                            wA = __fmaf_rn(w, vd, wA);
+                            wB = __fadd_rn(wB, w);
+                        }
+                    }
+                } else if (MODE != 2) {
                     n = __fadd_rn(n, pr);
 #pragma unroll
                     for (int t = 0; t < DM; ++t)
@@ -282,6 +395,10 @@ simt_rows_kernel(Shape sh, const T* __restrict__ Q, const T* __restrict__ K,
             if (t < d) ad = __fmaf_rn(acc[t], to_f(dO[qrow * d + t]), ad);  // :487-490
         r0[qrow] = __fdiv_rn(1.0f, __fadd_rn(n, ASA_EPS));                 // :435
         r1[qrow] = ad;
+    } else if (MODE == 3) {
+        const float np = __fadd_rn(n, ASA_EPS);
+        r0[qrow] = __fdiv_rn(1.0f, np);
+        r1[qrow] = wB > 0.0f ? __fmul_rn(__fdiv_rn(wA, wB), np) : 0.0f;
     } else {
 #pragma unroll
         for (int t = 0; t < DM; ++t) {
@@ -474,7 +591,7 @@ cudaError_t launch_rows(const Shape& s, const void* Q, const void* K, const void
                         float* r0, float* r1, cudaStream_t st) {
     const int QT = qthreads(s.BM);
     const int subs = (s.BM + QT - 1) / QT;
-    const size_t smem = sizeof(float) * ((size_t)QT * (DM + 1) * (MODE == 2 ? 2 : 1) + 2 * KT * DM);
+    const size_t smem = sizeof(float) * ((size_t)QT * (DM + 1) * (MODE >= 2 ? 2 : 1) + 2 * KT * DM);
     auto kern = simt_rows_kernel<T, TO, DM, MODE>;
     cudaError_t e = set_smem(kern, smem);
     if (e != cudaSuccess) return e;
@@ -535,6 +652,31 @@ cudaError_t simt_rowstats(const Shape& s, const void* Q, const void* K, const vo
                           float* invN, float* accdO, cudaStream_t st) {
     ASA_DISPATCH_T(s.in_dtype, T, ASA_DISPATCH_DM(s.d, DM, {
         return launch_rows<T, float, DM, 1>(s, Q, K, V, Qidx, Kidx, tau, ptr, idx, dO, nullptr,
+                                            nullptr, nullptr, nullptr, invN, accdO, st);
+    }));
+    return cudaErrorInvalidValue;
+}
+
+cudaError_t simt_exact_tau(const Shape& s, const void* Q, const void* K, const int32_t* Qidx,
+                           const int32_t* Kidx, float* tau, uint8_t* M, cudaStream_t st) {
+    cudaError_t e = cudaMemsetAsync(M, 0, (size_t)s.BH * s.nQB * s.nKB, st);
+    if (e != cudaSuccess) return e;
+    ASA_DISPATCH_T(s.in_dtype, T, ASA_DISPATCH_DM(s.d, DM, {
+        const int QT = qthreads(s.BM);
+        dim3 grid(s.nQB * ((s.BM + QT - 1) / QT), s.BH);
+        simt_exact_tau_kernel<T, DM><<<grid, QT, 0, st>>>(s, (const T*)Q, (const T*)K, Qidx, Kidx, tau, M);
+        note_launch();
+        return cudaGetLastError();
+    }));
+    return cudaErrorInvalidValue;
+}
+
+cudaError_t simt_jacobian_stats(const Shape& s, const void* Q, const void* K, const void* V,
+                                const int32_t* Qidx, const int32_t* Kidx, const float* tau,
+                                const int32_t* ptr, const int32_t* idx, const void* dO,
+                                float* invN, float* accdO, cudaStream_t st) {
+    ASA_DISPATCH_T(s.in_dtype, T, ASA_DISPATCH_DM(s.d, DM, {
+        return launch_rows<T, float, DM, 3>(s, Q, K, V, Qidx, Kidx, tau, ptr, idx, dO, nullptr,
                                             nullptr, nullptr, nullptr, invN, accdO, st);
     }));
     return cudaErrorInvalidValue;

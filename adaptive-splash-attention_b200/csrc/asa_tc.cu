@@ -758,6 +758,213 @@ k1_tau_mask(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
     }
 }
 
+// ===========================================================================
+// K1 exact: the exact α-entmax threshold (asa_tau_mode ASA_TAU_EXACT) and the
+// "tile max vs τ" mask, no counterpart in the reference.  τ solves
+// Σ_j [(α-1)s_j - τ]_+^{1/(α-1)} = 1 over every visible key of the row (s the
+// clamped score).  kExactPasses passes over the row's visible tiles, S =
+// Q·K^T on the tensor cores each time: the first finds the row maximum,
+// which brackets τ in [(α-1)s_max - 1, (α-1)s_max]; each later pass sums
+// F(τ) = Σ u_+^{1/(α-1)} and Σ u_+^{(2-α)/(α-1)} and takes a Newton step (F
+// is convex and decreasing, so from the left end the steps climb
+// monotonically), falling back to bisection when a step leaves the bracket.
+// The row's NW threads (one per column slice) add their partial sums in a
+// fixed order between passes, so every thread of a row holds the same τ.
+// The last pass marks each tile holding a positive weight at the bracket's
+// left end, which bounds the final τ from below: a superset of the tiles the
+// final τ leaves weight in.
+// ===========================================================================
+template <int D, int NW, int PINV, int PE2>
+__global__ void __launch_bounds__(64 + 128 * NW, 1)
+k1_exact(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK, Shape s,
+         const int32_t* __restrict__ Qidx, const int32_t* __restrict__ Kidx, Bounds bd,
+         float* __restrict__ tau, uint8_t* __restrict__ M, int* err) {
+    constexpr int NE = 128 * NW;              // epilogue threads
+    constexpr int CP = 4 / NW;                // 32-column chunks per thread per tile
+    constexpr int S = 4;                      // K stages
+    constexpr int NB = 4;                     // S buffers in TMEM (128 columns each)
+    constexpr int TB = D * TILE * 2;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* base = align1024(smem_raw, err);
+    uint8_t* sQ = base;
+    uint8_t* sK = base + TB;
+    float* red = reinterpret_cast<float*>(sK + S * TB);    // [2 parities][2][NW][128] partial sums
+    uint64_t* bars = reinterpret_cast<uint64_t*>(red + 4 * NW * TILE);
+    uint64_t* q_full = bars;
+    uint64_t* k_full = bars + 1;
+    uint64_t* k_empty = k_full + S;
+    uint64_t* s_full = k_empty + S;           // [NB]
+    uint64_t* s_free = s_full + NB;           // [NB]
+    uint64_t* drain = s_free + NB;            // exit-time MMA drain (after a timed-out wait)
+    uint32_t* holder = reinterpret_cast<uint32_t*>(bars + 24);
+    int* misc = reinterpret_cast<int*>(holder + 4);        // [8] warp counts, tile count
+    uint32_t* sched = reinterpret_cast<uint32_t*>(misc + 16);   // [nKB]
+    uint8_t* flags = reinterpret_cast<uint8_t*>(sched + s.nKB);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int bh = blockIdx.y;
+    const int qb = s.causal ? (int)(gridDim.x - 1 - blockIdx.x) : (int)blockIdx.x;
+    const int32_t* Kidx_bh = Kidx + (size_t)bh * s.NK;
+
+    if (threadIdx.x == 0) {
+        mbar_init(q_full, 1);
+        for (int i = 0; i < S; ++i) { mbar_init(&k_full[i], 1); mbar_init(&k_empty[i], 1); }
+        for (int i = 0; i < NB; ++i) { mbar_init(&s_full[i], 1); mbar_init(&s_free[i], NE / 32); }
+        mbar_init(drain, 1);
+        fence_barrier_init();
+        tma_prefetch_desc(&tmQ);
+        tma_prefetch_desc(&tmK);
+        mbar_expect_tx(q_full, TB);
+        for (int bx = 0; bx < D / BOX; ++bx)
+            tma_load_3d(sQ + bx * BOX_BYTES, &tmQ, q_full, bx * BOX, qb * TILE, bh);
+    }
+    if (warp == 1) { tmem_alloc(holder, 512); tmem_relinquish(); }
+    if (threadIdx.x >= EPI0) {
+        const int r = threadIdx.x - EPI0;
+        for (int i = r; i < s.nKB; i += NE) flags[i] = 0;
+        if (r < NEPI) {                       // the schedule builders' barrier counts NEPI threads
+            const int n = sched_visible(sched, misc, s, bd, bh, qb, r);
+            if (r == 0) misc[8] = n;
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tbase = *holder;
+    const int T = misc[8];
+    const int TP = kExactPasses * T;          // every pass: tile jj % T
+
+    if (warp == 0) {
+        if (lane == 0) {
+            for (int j = 0; j < TP; ++j) {
+                const int kb = (int)(sched[j % T] & SCHED_IDX);
+                const int st = j % S;
+                mbar_wait(&k_empty[st], ((j / S) & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+                mbar_expect_tx(&k_full[st], TB);
+                for (int bx = 0; bx < D / BOX; ++bx)
+                    tma_load_3d(sK + st * TB + bx * BOX_BYTES, &tmK, &k_full[st], bx * BOX, kb * TILE, bh);
+            }
+        }
+        if (lane == 0 && error_set(err)) {   // a wait gave up: let this CTA's loads land
+            mbar_drain(q_full, 0);
+            drain_ring(k_full, S, TP);
+        }
+    } else if (warp == 1) {
+        constexpr uint32_t idesc = idesc_bf16(128, 128, 0, 0);
+        mbar_wait(q_full, 0, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);   // issued at set-up even when T = 0
+        const uint64_t dQd = kdesc(sQ, 0);
+        for (int j = 0; j < TP; ++j) {
+            const int st = j % S, b = j % NB;
+            mbar_wait(&k_full[st], (j / S) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+            mbar_wait(&s_free[b], ((j / NB) & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+            tc_fence_after();
+            if (lane == 0) {
+                const uint64_t dK = kdesc(sK + st * TB, 0);
+#pragma unroll
+                for (int kk = 0; kk < D / 16; ++kk)
+                    mma_bf16_ss(tbase + b * 128, kdesc_step(dQd, kk), kdesc_step(dK, kk), idesc, kk > 0);
+                mma_commit(&s_full[b]);
+                mma_commit(&k_empty[st]);
+            }
+            __syncwarp();
+        }
+        if (lane == 0 && error_set(err)) {   // a wait gave up: let this CTA's MMAs finish
+            mma_commit(drain);
+            mbar_drain(drain, 0);
+        }
+        __syncwarp();
+    } else {
+        const int row = (warp & 3) * 32 + lane;
+        const int et = threadIdx.x - EPI0;
+        const int h = et / TILE;                  // column slice of each tile
+        const int q = qb * TILE + row;
+        const bool qv = q < s.NQ;
+        const int qpos = !qv ? INT_MIN : (s.causal ? Qidx[(size_t)bh * s.NQ + q] : INT_MAX);
+        const uint32_t tl = tmem_lane_base(tbase, warp);
+        const float inv = __fdiv_rn(1.0f, s.am1);
+        float tq = 0.0f, lo = 0.0f, hi = 0.0f;    // τ and its bracket (identical in the row's threads)
+        float a0 = neg_inf(), a1 = 0.0f;          // this pass's partials: max, or F and Σ w
+        // add the row's partial sums (fixed order: deterministic), then step τ
+        auto combine = [&](int pass) {
+            float* rp = red + (pass & 1) * 2 * NW * TILE;
+            rp[h * TILE + row] = a0;
+            rp[(NW + h) * TILE + row] = a1;
+            asm volatile("bar.sync 2, %0;" ::"n"(NE) : "memory");
+            if (pass == 0) {
+                float m = neg_inf();
+#pragma unroll
+                for (int g = 0; g < NW; ++g) m = fmaxf(m, rp[g * TILE + row]);
+                if (!(m > neg_inf())) m = 0.0f;       // no visible key: no weight anywhere
+                hi = __fmul_rn(s.am1, clamp_score(m, s.scale));
+                lo = __fadd_rn(hi, -1.0f);
+                tq = lo;
+            } else {
+                float F = 0.0f, W = 0.0f;
+#pragma unroll
+                for (int g = 0; g < NW; ++g) {
+                    F += rp[g * TILE + row];
+                    W += rp[(NW + g) * TILE + row];
+                }
+                const float gF = F - 1.0f;
+                if (gF >= 0.0f) lo = tq; else hi = tq;
+                float tn = W > 0.0f ? tq + gF / (inv * W) : tq;
+                if (!(tn >= lo && tn <= hi)) tn = 0.5f * (lo + hi);
+                tq = tn;
+            }
+            a0 = 0.0f;
+            a1 = 0.0f;
+        };
+        for (int jj = 0; jj < TP; ++jj) {
+            const int pass = jj / T;
+            if (jj > 0 && jj % T == 0) combine(pass - 1);
+            const bool last = pass == kExactPasses - 1;
+            const uint32_t e = sched[jj % T];
+            const int kb = (int)(e & SCHED_IDX);
+            const int b = jj % NB;
+            const bool all = (e & SCHED_ALL) != 0;
+            mbar_wait(&s_full[b], (jj / NB) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+            tc_fence_after();
+            uint32_t r2[CP][32];
+#pragma unroll
+            for (int cc = 0; cc < CP; ++cc) tmem_ld32(tl + b * 128 + (h * CP + cc) * 32, r2[cc]);
+            tmem_ld_wait();
+            tc_fence_before();
+            epi_arrive(&s_free[b]);          // S is in registers: release the buffer
+            bool hit = false;
+#pragma unroll
+            for (int cc = 0; cc < CP; ++cc) {
+                const uint32_t vis = all ? 0xffffffffu
+                                         : vis_mask32(Kidx_bh, kb * TILE + (h * CP + cc) * 32, s.NK, s.causal, qpos);
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                    if (!((vis >> i) & 1u)) continue;
+                    const float sc = clamp_score(__uint_as_float(r2[cc][i]), s.scale);
+                    if (pass == 0) { a0 = fmaxf(a0, sc); continue; }
+                    const float u = __fmaf_rn(s.am1, sc, -tq);
+                    if (u > 0.0f) {
+                        const float p = powk<PINV>(u, s.pinv.e), w = powk<PE2>(u, s.pe2.e);
+                        if (isfinite(p)) a0 += p;
+                        if (isfinite(w)) a1 += w;
+                    }
+                    if (last) hit |= __fmaf_rn(s.am1, sc, -lo) > 0.0f;
+                }
+            }
+            if (hit) flags[kb] = 1;
+        }
+        if (T > 0) combine(kExactPasses - 1);
+        if (h == 0 && qv) tau[(size_t)bh * s.NQ + q] = T > 0 ? tq : 0.0f;
+        asm volatile("bar.sync 2, %0;" ::"n"(NE) : "memory");
+        uint8_t* Mrow = M + ((size_t)bh * s.nQB + qb) * s.nKB;
+        for (int i = et; i < s.nKB; i += NE) Mrow[i] = flags[i];
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tbase, 512);
+    }
+}
+
 // Coalesced store of a warp's 32 rows x 32 columns (lane i holds row i's
 // values o[0..31]) through 4 KB of shared staging: row-per-lane stores write
 // 32 different lines per instruction, partial sectors that cost more than
@@ -1843,6 +2050,213 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
 }
 
 // ===========================================================================
+// K4 jac: the row statistic of the Jacobian gradient (asa_grad_mode
+// ASA_GRAD_JACOBIAN), no counterpart in the reference.  Over the CSR tile
+// list: S = Q·K^T and dP = dO·V^T into TMEM (two buffers), and per query
+// R = Σ_j w_j dP_j / Σ_j w_j, w = u^{(2-α)/(α-1)} for u > EPS (the weights
+// the gradient kernels apply).  R replaces D = O·dO, so dQ and dK/dV then
+// compute g = w (dP - R) / n.  Each of the DQ_NW epilogue warpgroups owns
+// one 32-key chunk of every tile; the row's partial sums are added in a
+// fixed order at the end.
+// ===========================================================================
+template <int D, int PE2>
+__global__ void __launch_bounds__(DQ_THREADS, 1)
+k4_jac(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+       const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO, Shape s,
+       const int32_t* __restrict__ Qidx, const int32_t* __restrict__ Kidx, Bounds bd,
+       const float* __restrict__ tau, const int32_t* __restrict__ ptr, const int32_t* __restrict__ idx,
+       float* __restrict__ Rq, int* err) {
+    constexpr int SK = 2, SV = 2;             // K / V stages (both released after S/dP)
+    constexpr int NB = 2;                     // S/dP buffer pairs in TMEM
+    constexpr int TB = D * TILE * 2;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* base = align1024(smem_raw, err);
+    uint8_t* sQ = base;
+    uint8_t* sdO = base + TB;
+    uint8_t* sK = base + 2 * TB;              // SK stages
+    uint8_t* sV = sK + SK * TB;               // SV stages
+    float* red = reinterpret_cast<float*>(sV + SV * TB);    // [2][DQ_NW][128] partial sums
+    uint64_t* bars = reinterpret_cast<uint64_t*>(red + 2 * DQ_NW * TILE);
+    uint64_t* q_full = bars;
+    uint64_t* k_full = bars + 1;
+    uint64_t* k_empty = k_full + SK;
+    uint64_t* v_full = k_empty + SK;
+    uint64_t* v_empty = v_full + SV;
+    uint64_t* sd_full = v_empty + SV;         // [NB]
+    uint64_t* sd_free = sd_full + NB;         // [NB]
+    uint64_t* fixed = sd_free + NB;           // K/V of a tile-load-zeroing tile fixed
+    uint64_t* drain = fixed + 1;              // exit-time MMA drain (after a timed-out wait)
+    uint32_t* holder = reinterpret_cast<uint32_t*>(bars + 24);
+    int* qidx_blk = reinterpret_cast<int*>(holder + 4);
+    uint32_t* sched = reinterpret_cast<uint32_t*>(qidx_blk + TILE);   // [T]
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int bh = blockIdx.y;
+    const int qb = s.causal ? (int)(gridDim.x - 1 - blockIdx.x) : (int)blockIdx.x;
+    const int32_t* Kidx_bh = Kidx + (size_t)bh * s.NK;
+    const int32_t* list = idx + (size_t)bh * s.nQB * s.nKB;
+    const int e0 = ptr[(size_t)bh * (s.nQB + 1) + qb];
+    const int T = ptr[(size_t)bh * (s.nQB + 1) + qb + 1] - e0;
+
+    if (threadIdx.x == 0) {
+        mbar_init(q_full, 1);
+        for (int i = 0; i < SK; ++i) { mbar_init(&k_full[i], 1); mbar_init(&k_empty[i], 1); }
+        for (int i = 0; i < SV; ++i) { mbar_init(&v_full[i], 1); mbar_init(&v_empty[i], 1); }
+        for (int i = 0; i < NB; ++i) { mbar_init(&sd_full[i], 1); mbar_init(&sd_free[i], DQ_NE / 32); }
+        mbar_init(fixed, 8);
+        mbar_init(drain, 1);
+        fence_barrier_init();
+        if (T > 0) {
+            mbar_expect_tx(q_full, 2 * TB);
+            for (int bx = 0; bx < D / BOX; ++bx) {
+                tma_load_3d(sQ + bx * BOX_BYTES, &tmQ, q_full, bx * BOX, qb * TILE, bh);
+                tma_load_3d(sdO + bx * BOX_BYTES, &tmdO, q_full, bx * BOX, qb * TILE, bh);
+            }
+        }
+    }
+    if (warp == 1) { tmem_alloc(holder, 512); tmem_relinquish(); }
+    if (threadIdx.x >= DQ_EPI0) {
+        const int r = threadIdx.x - DQ_EPI0;
+        const int q = qb * TILE + r;
+        if (r < TILE) qidx_blk[r] = (q < s.NQ && s.causal) ? Qidx[(size_t)bh * s.NQ + q] : INT_MAX;
+        if (r < NEPI) sched_from_list(sched, list + e0, T, s, bd, bh, qb, false, r);
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tbase = *holder;
+    const int qmin_blk = s.causal ? bd.qmin[bh * s.nQB + qb] : INT_MIN;
+
+    if (warp == 0) {
+        if (lane < 2 && T > 0) {
+            // lane 0 streams K, lane 1 streams V
+            uint64_t* full = lane == 0 ? k_full : v_full;
+            uint64_t* empty = lane == 0 ? k_empty : v_empty;
+            uint8_t* ring = lane == 0 ? sK : sV;
+            const CUtensorMap* tm = lane == 0 ? &tmK : &tmV;
+            for (int j = 0; j < T; ++j) {
+                const int kb = (int)(sched[j] & SCHED_IDX);
+                const int st = j % 2;
+                mbar_wait(&empty[st], ((j / 2) & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+                mbar_expect_tx(&full[st], TB);
+                for (int bx = 0; bx < D / BOX; ++bx)
+                    tma_load_3d(ring + st * TB + bx * BOX_BYTES, tm, &full[st], bx * BOX, kb * TILE, bh);
+            }
+        }
+        __syncwarp();
+        if (lane == 0 && T > 0 && error_set(err)) {   // a wait gave up: let this CTA's loads land
+            mbar_drain(q_full, 0);
+            drain_ring(k_full, SK, T);
+            drain_ring(v_full, SV, T);
+        }
+    } else if (warp == 1) {
+        constexpr uint32_t idS = idesc_bf16(128, 128, 0, 0);
+        if (T > 0) mbar_wait(q_full, 0, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+        const uint64_t dQd = kdesc(sQ, 0), dOd = kdesc(sdO, 0);
+        int nfix = 0;
+        for (int j = 0; j < T; ++j) {
+            const int st = j % 2, b = j % NB;
+            mbar_wait(&k_full[st], (j / 2) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+            mbar_wait(&v_full[st], (j / 2) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+            if (sched[j] & SCHED_FIX)      // the epilogue warps zero K and V of this tile
+                mbar_wait(fixed, (nfix++) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+            __syncwarp();
+            mbar_wait(&sd_free[b], ((j / NB) & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+            tc_fence_after();
+            if (lane == 0) {
+                const uint64_t dK = kdesc(sK + st * TB, 0), dV = kdesc(sV + st * TB, 0);
+                const uint32_t cS = tbase + b * 256, cP = cS + 128;
+#pragma unroll
+                for (int kk = 0; kk < D / 16; ++kk) {
+                    mma_bf16_ss(cS, kdesc_step(dQd, kk), kdesc_step(dK, kk), idS, kk > 0);
+                    mma_bf16_ss(cP, kdesc_step(dOd, kk), kdesc_step(dV, kk), idS, kk > 0);
+                }
+                mma_commit(&sd_full[b]);
+                mma_commit(&k_empty[st]);
+                mma_commit(&v_empty[st]);
+            }
+            __syncwarp();
+        }
+        if (lane == 0 && error_set(err)) {   // a wait gave up: let this warp's MMAs finish
+            mma_commit(drain);
+            mbar_drain(drain, 0);
+        }
+        __syncwarp();
+    } else if (warp >= DQ_EPI0 / 32) {
+        const int row = (warp & 3) * 32 + lane;
+        const int et = threadIdx.x - DQ_EPI0;
+        const int h = et / TILE;                  // 32-key chunk of every tile
+        const int q = qb * TILE + row;
+        const bool qv = q < s.NQ;
+        const size_t qrow = (size_t)bh * s.NQ + (qv ? q : 0);
+        const int qpos = !qv ? INT_MIN : (s.causal ? Qidx[qrow] : INT_MAX);
+        const float tq = qv ? tau[qrow] : 0.0f;
+        const uint32_t tl = tmem_lane_base(tbase, warp);
+        float A = 0.0f, B = 0.0f;
+        for (int j = 0; j < T; ++j) {
+            const uint32_t e = sched[j];
+            const int kb = (int)(e & SCHED_IDX);
+            const int b = j % NB;
+            const bool all = qv && (e & SCHED_ALL) != 0;
+            if ((e & SCHED_FIX) && et < 8 * 32) {
+                // the reference's tile-load zeroing of K and V, by eight
+                // epilogue warps (32 rows each of K or V); S/dP waits for it
+                const int ew = et >> 5;
+                uint8_t* tile;
+                if (ew < 4) {
+                    mbar_wait(&k_full[j % 2], (j / 2) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+                    tile = sK + (j % 2) * TB;
+                } else {
+                    mbar_wait(&v_full[j % 2], (j / 2) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+                    tile = sV + (j % 2) * TB;
+                }
+                fix_tile<D, 1>(tile, qidx_blk, qmin_blk, Kidx_bh, kb, s.NK, lane, 32 * (ew & 3));
+                fence_async_smem();
+                epi_arrive(fixed);
+            }
+            mbar_wait(&sd_full[b], (j / NB) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+            tc_fence_after();
+            uint32_t rs[32], rp[32];
+            tmem_ld32(tl + b * 256 + h * 32, rs);
+            tmem_ld32(tl + b * 256 + 128 + h * 32, rp);
+            tmem_ld_wait();
+            tc_fence_before();
+            epi_arrive(&sd_free[b]);
+            const uint32_t vis = all ? 0xffffffffu
+                                     : (qv ? vis_mask32(Kidx_bh, kb * TILE + h * 32, s.NK, s.causal, qpos) : 0u);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+                if (!((vis >> i) & 1u)) continue;
+                const float u = __fmaf_rn(s.am1, clamp_score(__uint_as_float(rs[i]), s.scale), -tq);
+                if (!(u > ASA_EPS)) continue;
+                const float w = powk<PE2>(fmaxf(u, ASA_EPS), s.pe2.e);
+                if (!isfinite(w)) continue;
+                A = fmaf(w, __uint_as_float(rp[i]), A);
+                B += w;
+            }
+        }
+        red[h * TILE + row] = A;
+        red[(DQ_NW + h) * TILE + row] = B;
+        asm volatile("bar.sync 2, %0;" ::"n"(DQ_NE) : "memory");
+        if (h == 0 && qv) {
+            float a = 0.0f, bs = 0.0f;
+#pragma unroll
+            for (int g = 0; g < DQ_NW; ++g) {
+                a += red[g * TILE + row];
+                bs += red[(DQ_NW + g) * TILE + row];
+            }
+            Rq[qrow] = bs > 0.0f ? a / bs : 0.0f;
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tbase, 512);
+    }
+}
+
+// ===========================================================================
 // K4 pre: D_q = Σ_t O_t · dO_t (fp32 O, bf16 dO) and 1/(n+EPS), one warp per row.
 // ===========================================================================
 template <int D>
@@ -2018,6 +2432,34 @@ cudaError_t tc_tau_mask(const Shape& s, const void* Q, const void* K, const int3
     return go(k1_tau_mask<64, 32, 2>, k1_tau_solve<32>, 64, 2);
 }
 
+// τ and the mask by the exact α-entmax threshold (asa_tau_mode ASA_TAU_EXACT).
+cudaError_t tc_exact_tau(const Shape& s, const void* Q, const void* K, const int32_t* Qidx,
+                         const int32_t* Kidx, float* tau, uint8_t* M, void* ws, int* err,
+                         cudaStream_t st) {
+    cudaError_t e = launch_bounds(s, Qidx, Kidx, ws, st);
+    if (e != cudaSuccess) return e;
+    CUtensorMap mQ, mK;
+    if (!make_map(&mQ, Q, s.BH, s.NQ, s.d) || !make_map(&mK, K, s.BH, s.NK, s.d)) return cudaErrorInvalidValue;
+    Bounds bd = bounds_at(s, ws);
+    dim3 grid(s.nQB, s.BH);
+    return with_alpha(s, [&](auto ac) -> cudaError_t {
+        constexpr int PI = decltype(ac)::pinv, PE = decltype(ac)::pe2;
+        auto go = [&](auto kern, int D) -> cudaError_t {
+            // Q + four K stages, partial sums, barriers + TMEM holder, counts,
+            // the tile schedule and the mask flags, alignment slack
+            const size_t smem = (size_t)D * TILE * 2 * 5 + (size_t)4 * 4 * TILE * 4 + 24 * 8 + 16 + 64 +
+                                (size_t)s.nKB * 5 + 64;
+            cudaError_t r = prep(kern, smem);
+            if (r != cudaSuccess) return r;
+            kern<<<grid, 64 + 128 * 4, smem, st>>>(mQ, mK, s, Qidx, Kidx, bd, tau, M, err);
+            note_launch();
+            return cudaGetLastError();
+        };
+        if (s.d == 128) return go(k1_exact<128, 4, PI, PE>, 128);
+        return go(k1_exact<64, 4, PI, PE>, 64);
+    });
+}
+
 #endif  // part 1
 
 #if ASA_PART(2)
@@ -2102,6 +2544,9 @@ cudaError_t tc_backward(const Shape& s, const void* Q, const void* K, const void
     const size_t rows = (size_t)s.BH * s.NQ;
     float* invNv = Dq + rows;
     cudaError_t e = cudaSuccess;
+    const bool maps = make_map(&a.mQ, Q, s.BH, s.NQ, s.d) && make_map(&a.mK, K, s.BH, s.NK, s.d) &&
+                      make_map(&a.mV, V, s.BH, s.NK, s.d) && make_map(&a.mdO, dO, s.BH, s.NQ, s.d);
+    if (!maps && (stages & 6 || s.jacobian)) return cudaErrorInvalidValue;
     if (stages & 1) {
         e = launch_bounds(s, Qidx, Kidx, ws, st);
         if (e != cudaSuccess) return e;
@@ -2114,11 +2559,27 @@ cudaError_t tc_backward(const Shape& s, const void* Q, const void* K, const void
         note_launch();
         e = cudaGetLastError();
         if (e != cudaSuccess) return e;
+        if (s.jacobian) {
+            // the Jacobian's row statistic replaces D = O·dO
+            const Bounds bd = bounds_at(s, ws);
+            e = with_alpha(s, [&](auto ac) -> cudaError_t {
+                auto go = [&](auto kern, int D) -> cudaError_t {
+                    const size_t smem = (size_t)D * TILE * 2 * 6 + (size_t)2 * DQ_NW * TILE * 4 + 24 * 8 + 16 +
+                                        TILE * 4 + (size_t)s.nKB * 4 + 64;
+                    cudaError_t r = prep(kern, smem);
+                    if (r != cudaSuccess) return r;
+                    kern<<<dim3(s.nQB, s.BH), DQ_THREADS, smem, st>>>(a.mQ, a.mK, a.mV, a.mdO, s, Qidx, Kidx, bd,
+                                                                     tau, ptr, idx, Dq, err);
+                    note_launch();
+                    return cudaGetLastError();
+                };
+                if (s.d == 128) return go(k4_jac<128, decltype(ac)::pe2>, 128);
+                return go(k4_jac<64, decltype(ac)::pe2>, 64);
+            });
+            if (e != cudaSuccess) return e;
+        }
     }
     if (!(stages & 6)) return cudaSuccess;
-    if (!make_map(&a.mQ, Q, s.BH, s.NQ, s.d) || !make_map(&a.mK, K, s.BH, s.NK, s.d) ||
-        !make_map(&a.mV, V, s.BH, s.NK, s.d) || !make_map(&a.mdO, dO, s.BH, s.NQ, s.d))
-        return cudaErrorInvalidValue;
     a.Qidx = Qidx; a.Kidx = Kidx; a.ptr = ptr; a.idx = idx; a.cptr = cptr; a.cidx = cidx;
     a.tau = tau; a.invNv = invNv; a.Dq = Dq; a.dQ = dQ; a.dK = dK; a.dV = dV; a.err = err;
     if (stages & 2) {

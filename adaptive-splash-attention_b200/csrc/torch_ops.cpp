@@ -10,10 +10,11 @@
 //
 //   splash_attention::forward(Q, K, V, Q_idx?, K_idx?, alpha, sm_scale, k_keep,
 //       block_m, block_n, causal, backend, precision, out_f32, ref_tile_load,
-//       need_o32) -> (O, O32, tau, M, csr_ptr, csr_idx, rownorm)
+//       tau_mode, grad_mode, need_o32) -> (O, O32, tau, M, csr_ptr, csr_idx, rownorm)
 //   splash_attention::backward(Q, K, V, Q_idx?, K_idx?, O32, tau, M, csr_ptr,
 //       csr_idx, rownorm, dO, alpha, sm_scale, k_keep, block_m, block_n,
-//       causal, backend, precision, out_f32, ref_tile_load) -> (dQ, dK, dV)
+//       causal, backend, precision, out_f32, ref_tile_load, tau_mode,
+//       grad_mode) -> (dQ, dK, dV)
 //
 // O32 is the fp32 copy of O the backward reads; it is empty when need_o32 is
 // false (no backward will follow) and when O itself is fp32 (the backward
@@ -54,6 +55,7 @@ struct Cfg {
     bool causal;
     int64_t backend, precision;
     bool out_f32, ref_tile_load;
+    int64_t tau_mode, grad_mode;
 };
 
 asa_params make_params(const Tensor& Q, const Tensor& K, const Cfg& c) {
@@ -78,6 +80,8 @@ asa_params make_params(const Tensor& Q, const Tensor& K, const Cfg& c) {
     p.backend = (int)c.backend;
     p.precision = (int)c.precision;
     p.ref_tile_load = c.ref_tile_load ? 1 : 0;
+    p.tau_mode = (int)c.tau_mode;
+    p.grad_mode = (int)c.grad_mode;
     return p;
 }
 
@@ -157,16 +161,18 @@ FwdOut forward_shapes(const Tensor& Q, const Tensor& K, const Cfg& c, bool need_
 }
 
 Cfg cfg_of(double alpha, double sm_scale, int64_t k_keep, int64_t block_m, int64_t block_n,
-           bool causal, int64_t backend, int64_t precision, bool out_f32, bool ref_tile_load) {
+           bool causal, int64_t backend, int64_t precision, bool out_f32, bool ref_tile_load,
+           int64_t tau_mode, int64_t grad_mode) {
     return Cfg{alpha, sm_scale, k_keep, block_m, block_n, causal, backend, precision, out_f32,
-               ref_tile_load};
+               ref_tile_load, tau_mode, grad_mode};
 }
 
 FwdOut forward_cuda(const Tensor& Q_, const Tensor& K_, const Tensor& V_,
                     const c10::optional<Tensor>& Qidx, const c10::optional<Tensor>& Kidx,
                     double alpha, double sm_scale, int64_t k_keep, int64_t block_m,
                     int64_t block_n, bool causal, int64_t backend, int64_t precision,
-                    bool out_f32, bool ref_tile_load, bool need_o32) {
+                    bool out_f32, bool ref_tile_load, int64_t tau_mode, int64_t grad_mode,
+                    bool need_o32) {
     TORCH_CHECK(Q_.is_cuda() && K_.is_cuda() && V_.is_cuda(),
                 "splash_attention: tensors must be on a CUDA device");   // reference :543
     TORCH_CHECK(V_.sizes() == K_.sizes() && V_.scalar_type() == Q_.scalar_type() &&
@@ -175,7 +181,7 @@ FwdOut forward_cuda(const Tensor& Q_, const Tensor& K_, const Tensor& V_,
     c10::cuda::CUDAGuard guard(Q_.device());
     const Tensor Q = Q_.contiguous(), K = K_.contiguous(), V = V_.contiguous();
     const Cfg c = cfg_of(alpha, sm_scale, k_keep, block_m, block_n, causal, backend, precision,
-                         out_f32, ref_tile_load);
+                         out_f32, ref_tile_load, tau_mode, grad_mode);
     asa_params p = make_params(Q, K, c);
     check_positions(Qidx, (int64_t)p.B * p.H, p.NQ, "Q_idx", causal);
     check_positions(Kidx, (int64_t)p.B * p.H, p.NK, "K_idx", causal);
@@ -203,9 +209,10 @@ FwdOut forward_meta(const Tensor& Q, const Tensor& K, const Tensor& V,
                     const c10::optional<Tensor>& Qidx, const c10::optional<Tensor>& Kidx,
                     double alpha, double sm_scale, int64_t k_keep, int64_t block_m,
                     int64_t block_n, bool causal, int64_t backend, int64_t precision,
-                    bool out_f32, bool ref_tile_load, bool need_o32) {
+                    bool out_f32, bool ref_tile_load, int64_t tau_mode, int64_t grad_mode,
+                    bool need_o32) {
     const Cfg c = cfg_of(alpha, sm_scale, k_keep, block_m, block_n, causal, backend, precision,
-                         out_f32, ref_tile_load);
+                         out_f32, ref_tile_load, tau_mode, grad_mode);
     return forward_shapes(Q, K, c, need_o32, Q.options());
 }
 
@@ -214,12 +221,13 @@ std::tuple<Tensor, Tensor, Tensor> backward_cuda(
     const c10::optional<Tensor>& Kidx, const Tensor& O32, const Tensor& tau, const Tensor& M,
     const Tensor& csr_ptr, const Tensor& csr_idx, const Tensor& rownorm, const Tensor& dO_,
     double alpha, double sm_scale, int64_t k_keep, int64_t block_m, int64_t block_n, bool causal,
-    int64_t backend, int64_t precision, bool out_f32, bool ref_tile_load) {
+    int64_t backend, int64_t precision, bool out_f32, bool ref_tile_load, int64_t tau_mode,
+    int64_t grad_mode) {
     c10::cuda::CUDAGuard guard(Q_.device());
     const Tensor Q = Q_.contiguous(), K = K_.contiguous(), V = V_.contiguous();
     const Tensor dO = dO_.to(Q.scalar_type()).contiguous();
     const Cfg c = cfg_of(alpha, sm_scale, k_keep, block_m, block_n, causal, backend, precision,
-                         out_f32, ref_tile_load);
+                         out_f32, ref_tile_load, tau_mode, grad_mode);
     asa_params p = make_params(Q, K, c);
     TORCH_CHECK(O32.numel() == Q.numel() && O32.scalar_type() == at::kFloat,
                 "splash_attention::backward: the forward did not keep its fp32 output");
@@ -249,7 +257,8 @@ std::tuple<Tensor, Tensor, Tensor> backward_meta(
     const c10::optional<Tensor>& Kidx, const Tensor& O32, const Tensor& tau, const Tensor& M,
     const Tensor& csr_ptr, const Tensor& csr_idx, const Tensor& rownorm, const Tensor& dO,
     double alpha, double sm_scale, int64_t k_keep, int64_t block_m, int64_t block_n, bool causal,
-    int64_t backend, int64_t precision, bool out_f32, bool ref_tile_load) {
+    int64_t backend, int64_t precision, bool out_f32, bool ref_tile_load, int64_t tau_mode,
+    int64_t grad_mode) {
     const auto ot = out_f32 ? at::kFloat : Q.scalar_type();
     return {at::empty(Q.sizes(), Q.options().dtype(ot)), at::empty(K.sizes(), K.options().dtype(ot)),
             at::empty(K.sizes(), K.options().dtype(ot))};
@@ -261,13 +270,15 @@ TORCH_LIBRARY(splash_attention, m) {
     m.def(
         "forward(Tensor Q, Tensor K, Tensor V, Tensor? Q_idx, Tensor? K_idx, float alpha, "
         "float sm_scale, int k_keep, int block_m, int block_n, bool causal, int backend, "
-        "int precision, bool out_f32, bool ref_tile_load, bool need_o32) -> "
+        "int precision, bool out_f32, bool ref_tile_load, int tau_mode, int grad_mode, "
+        "bool need_o32) -> "
         "(Tensor, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor)");
     m.def(
         "backward(Tensor Q, Tensor K, Tensor V, Tensor? Q_idx, Tensor? K_idx, Tensor O32, "
         "Tensor tau, Tensor M, Tensor csr_ptr, Tensor csr_idx, Tensor rownorm, Tensor dO, "
         "float alpha, float sm_scale, int k_keep, int block_m, int block_n, bool causal, "
-        "int backend, int precision, bool out_f32, bool ref_tile_load) -> (Tensor, Tensor, Tensor)");
+        "int backend, int precision, bool out_f32, bool ref_tile_load, int tau_mode, int grad_mode) "
+        "-> (Tensor, Tensor, Tensor)");
 }
 
 TORCH_LIBRARY_IMPL(splash_attention, CUDA, m) {

@@ -47,9 +47,13 @@ def _op_config(Q, st: Settings):
     if out_dt not in (torch.float32, torch.bfloat16):
         raise TypeError(f"splash_attention: unsupported out_dtype {out_dt}")
     sm_scale = st.sm_scale if st.sm_scale is not None else Q.shape[-1] ** -0.5
+    if st.tau_mode not in _lib.TAU_MODE or st.grad_mode not in _lib.GRAD_MODE:
+        raise ValueError(f"splash_attention: tau_mode in {tuple(_lib.TAU_MODE)}, "
+                         f"grad_mode in {tuple(_lib.GRAD_MODE)}")
     return (float(st.alpha), float(sm_scale), int(st.k_keep), int(st.block_m), int(st.block_n),
             bool(st.causal), _lib.BACKEND[st.backend], _lib.PRECISION[st.precision],
-            out_dt == torch.float32, bool(st.ref_tile_load))
+            out_dt == torch.float32, bool(st.ref_tile_load), _lib.TAU_MODE[st.tau_mode],
+            _lib.GRAD_MODE[st.grad_mode])
 
 
 def _setup_context(ctx, inputs, output):
@@ -63,9 +67,9 @@ def _setup_context(ctx, inputs, output):
 def _backward(ctx, dO, *_unused):
     Q, K, V, Qi, Ki, O32, tau, M, ptr, idx, rown = ctx.saved_tensors
     if dO is None:
-        return (None,) * 16
+        return (None,) * 18
     dQ, dK, dV = _ops.backward(Q, K, V, Qi, Ki, O32, tau, M, ptr, idx, rown, dO, *ctx.cfg)
-    return (dQ.to(Q.dtype), dK.to(K.dtype), dV.to(V.dtype)) + (None,) * 13
+    return (dQ.to(Q.dtype), dK.to(K.dtype), dV.to(V.dtype)) + (None,) * 15
 
 
 torch.library.register_autograd("splash_attention::forward", _backward,
@@ -74,7 +78,7 @@ torch.library.register_autograd("splash_attention::forward", _backward,
 
 def splash_attention(Q, K, V, Q_idx=None, K_idx=None, *, alpha=1.5, sm_scale=None, k_keep=8,
                      block_m=128, block_n=128, causal=True, backend="auto", precision="split",
-                     out_dtype=None, ref_tile_load=True):
+                     out_dtype=None, ref_tile_load=True, tau_mode="reference", grad_mode="reference"):
     """α-entmax block-sparse attention with autograd.  Q, K, V: [B, H, N, d]
     float32 or bfloat16 on CUDA; Q_idx / K_idx: positions [B*H, N] (any
     integer dtype; [N] broadcasts).  Key k is visible to query q iff
@@ -87,10 +91,17 @@ def splash_attention(Q, K, V, Q_idx=None, K_idx=None, *, alpha=1.5, sm_scale=Non
     ref_tile_load=True reproduces the reference kernels' tile staging, in
     which a visible key's K/V elements are zeroed when the reference thread
     that loads them serves a query that cannot see the key; False reads every
-    visible key in full."""
+    visible key in full.
+
+    tau_mode="exact" replaces the reference's top-k threshold by the exact
+    α-entmax threshold over every visible key (and the mask by every tile
+    holding a positive weight); grad_mode="jacobian" replaces the fixed-τ
+    gradient by the α-entmax Jacobian.  Both together give exact α-entmax
+    attention and its exact gradient."""
     st = Settings(alpha=alpha, sm_scale=sm_scale, k_keep=k_keep, block_m=block_m,
                   block_n=block_n, causal=causal, backend=backend, precision=precision,
-                  out_dtype=out_dtype, ref_tile_load=ref_tile_load)
+                  out_dtype=out_dtype, ref_tile_load=ref_tile_load, tau_mode=tau_mode,
+                  grad_mode=grad_mode)
     if Q.device.type != "meta":
         _check_inputs(Q, K, V)
     BH = Q.shape[0] * Q.shape[1]
@@ -110,7 +121,7 @@ class AdaptiveSplashAttention(torch.nn.Module):
 
     def __init__(self, head_dim, alpha=1.5, k_keep=8, adaptive_threshold=True, sm_scale=None,
                  block_m=128, block_n=128, causal=True, backend="auto", precision="split",
-                 out_dtype=None, ref_tile_load=True):
+                 out_dtype=None, ref_tile_load=True, tau_mode="reference", grad_mode="reference"):
         super().__init__()
         if not adaptive_threshold:
             raise ValueError("AdaptiveSplashAttention: adaptive_threshold=False has no "
@@ -126,6 +137,7 @@ class AdaptiveSplashAttention(torch.nn.Module):
         self.causal = causal
         self.backend, self.precision, self.out_dtype = backend, precision, out_dtype
         self.ref_tile_load = ref_tile_load
+        self.tau_mode, self.grad_mode = tau_mode, grad_mode
 
     def forward(self, Q, K, V, Q_idx=None, K_idx=None):
         if Q.shape[-1] != self.head_dim:
@@ -134,12 +146,14 @@ class AdaptiveSplashAttention(torch.nn.Module):
                                 k_keep=self.k_keep, block_m=self.block_m,
                                 block_n=self.block_n, causal=self.causal, backend=self.backend,
                                 precision=self.precision, out_dtype=self.out_dtype,
-                                ref_tile_load=self.ref_tile_load)
+                                ref_tile_load=self.ref_tile_load, tau_mode=self.tau_mode,
+                                grad_mode=self.grad_mode)
 
     def extra_repr(self):
         return (f"head_dim={self.head_dim}, alpha={self.alpha}, k_keep={self.k_keep}, "
                 f"sm_scale={self.sm_scale}, block=({self.block_m},{self.block_n}), "
-                f"causal={self.causal}, backend={self.backend}, precision={self.precision}")
+                f"causal={self.causal}, backend={self.backend}, precision={self.precision}, "
+                f"tau_mode={self.tau_mode}, grad_mode={self.grad_mode}")
 
 
 def _ref_settings(sm_scale, alpha):

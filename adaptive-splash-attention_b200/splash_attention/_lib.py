@@ -15,6 +15,8 @@ DTYPE_F32, DTYPE_BF16 = 0, 1
 BACKEND = {"auto": 0, "simt": 1, "tc": 2}
 BACKEND_NAME = {v: k for k, v in BACKEND.items()}
 PRECISION = {"split": 0, "bf16": 1}
+TAU_MODE = {"reference": 0, "exact": 1}
+GRAD_MODE = {"reference": 0, "jacobian": 1}
 
 #: the exported symbols include/asa.h declares
 SYMBOLS = ("asa_params_default", "asa_workspace_bytes", "asa_resolve_backend", "asa_tau_mask",
@@ -33,7 +35,8 @@ class Params(ctypes.Structure):
                 ("sm_scale", ctypes.c_float), ("causal", ctypes.c_int),
                 ("in_dtype", ctypes.c_int), ("out_dtype", ctypes.c_int),
                 ("backend", ctypes.c_int), ("precision", ctypes.c_int),
-                ("timeout_spins", ctypes.c_longlong), ("ref_tile_load", ctypes.c_int)]
+                ("timeout_spins", ctypes.c_longlong), ("ref_tile_load", ctypes.c_int),
+                ("tau_mode", ctypes.c_int), ("grad_mode", ctypes.c_int)]
 
 
 class AsaError(RuntimeError):

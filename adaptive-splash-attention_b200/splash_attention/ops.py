@@ -49,6 +49,11 @@ class Settings:
     timeout_spins: int = 0
     # reproduce the reference's tile-load zeroing (include/asa.h ref_tile_load)
     ref_tile_load: bool = True
+    # "reference": τ from the row's top-k (the reference); "exact": the exact
+    # α-entmax threshold over all visible keys, mask = tiles with weight
+    tau_mode: str = "reference"
+    # "reference": the fixed-τ gradient; "jacobian": the α-entmax Jacobian
+    grad_mode: str = "reference"
 
 
 def make_params(Q, K, st: Settings):
@@ -71,6 +76,11 @@ def make_params(Q, K, st: Settings):
     p.precision = L.PRECISION[st.precision]
     p.timeout_spins = int(st.timeout_spins)
     p.ref_tile_load = 1 if st.ref_tile_load else 0
+    if st.tau_mode not in L.TAU_MODE or st.grad_mode not in L.GRAD_MODE:
+        raise ValueError(f"splash_attention: tau_mode in {tuple(L.TAU_MODE)}, "
+                         f"grad_mode in {tuple(L.GRAD_MODE)}")
+    p.tau_mode = L.TAU_MODE[st.tau_mode]
+    p.grad_mode = L.GRAD_MODE[st.grad_mode]
     return p
 
 

@@ -57,6 +57,23 @@ enum asa_backend {
     ASA_BACKEND_TC = 2     /* tcgen05 / TMEM / TMA kernels (bf16, d in {64,128}, 128x128 tiles) */
 };
 
+enum asa_tau_mode {
+    ASA_TAU_REFERENCE = 0, /* the reference's τ: five Halley steps over the row's top-k, and   */
+                           /* the mask = union of the block's top-k key blocks (:150-217)       */
+    ASA_TAU_EXACT = 1      /* the exact α-entmax threshold over all of the row's visible keys */
+                           /* (Σ [(α-1)s - τ]_+^{1/(α-1)} = 1), and the mask = every tile in   */
+                           /* which some row of the block has a positive weight ("tile max vs */
+                           /* τ"); the reference's tile-load zeroing does not apply           */
+};
+
+enum asa_grad_mode {
+    ASA_GRAD_REFERENCE = 0, /* the reference's fixed-τ gradient (:481-507)                     */
+    ASA_GRAD_JACOBIAN = 1   /* the α-entmax Jacobian: τ moves with the scores so that the row  */
+                            /* mass Σp is held fixed -- g_i = w_i (dP_i - Σ_j w_j dP_j / Σ_j w_j) */
+                            /* / Σp, w = ((α-1)s - τ)_+^{(2-α)/(α-1)}; with ASA_TAU_EXACT this */
+                            /* is the exact gradient of α-entmax attention                    */
+};
+
 enum asa_precision {
     ASA_PREC_SPLIT = 0,    /* P and dS enter the tensor cores as bf16 hi+lo pairs (parity) */
     ASA_PREC_BF16 = 1      /* single bf16 P and dS (FlashAttention-style rounding)          */
@@ -81,10 +98,13 @@ typedef struct asa_params {
                            /* qb*block_m + (col*d + dim) % block_m) cannot see    */
                            /* that key (:176-183, :285-294, :398-406, :442-450);  */
                            /* 0: every visible key is read in full.              */
+    int tau_mode;          /* asa_tau_mode (default ASA_TAU_REFERENCE)            */
+    int grad_mode;         /* asa_grad_mode (default ASA_GRAD_REFERENCE)          */
 } asa_params;
 
 /* Defaults: block 128x128, k_keep 8, α 1.5, sm_scale 0 (set it), causal,
- * bf16 in / bf16 out, AUTO backend, SPLIT precision, ref_tile_load 1. */
+ * bf16 in / bf16 out, AUTO backend, SPLIT precision, ref_tile_load 1,
+ * reference τ and gradient. */
 void asa_params_default(asa_params* p);
 
 /* Workspace each call needs, in bytes (16-byte multiples).
