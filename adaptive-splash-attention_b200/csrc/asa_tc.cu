@@ -320,6 +320,86 @@ __device__ __forceinline__ float powk(float x, float e) {
     else return powf(x, e);
 }
 
+// Maximum of three floats in one instruction (PTX max.f32 with three
+// operands, sm_100); NaN operands are ignored as fmaxf ignores them.
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+    float r;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+    return r;
+}
+// Largest of 32 raw scores (as bit patterns), 16 three-input maxima; m
+// receives the maxima of the groups {3g, 3g+1, 3g+2} (g < 10) and {30, 31}.
+__device__ __forceinline__ float chunk_max(const uint32_t (&r)[32], float (&m)[11]) {
+#pragma unroll
+    for (int g = 0; g < 10; ++g)
+        m[g] = max3f(__uint_as_float(r[3 * g]), __uint_as_float(r[3 * g + 1]), __uint_as_float(r[3 * g + 2]));
+    m[10] = fmaxf(__uint_as_float(r[30]), __uint_as_float(r[31]));
+    const float a = max3f(m[0], m[1], m[2]), b = max3f(m[3], m[4], m[5]), c = max3f(m[6], m[7], m[8]);
+    return fmaxf(max3f(a, b, c), fmaxf(m[9], m[10]));
+}
+
+// x^e for two values at once, exponent class PK in {1, 2, 3, 4, 5} (5: x^0).
+template <int PK>
+__device__ __forceinline__ float2 powk2(float2 x) {
+    if constexpr (PK == 1) return x;
+    else if constexpr (PK == 2) return __fmul2_rn(x, x);
+    else if constexpr (PK == 3) return __fmul2_rn(__fmul2_rn(x, x), x);
+    else if constexpr (PK == 4) { const float2 y = __fmul2_rn(x, x); return __fmul2_rn(y, y); }
+    else return make_float2(1.0f, 1.0f);
+}
+
+// Sums over one 32-key chunk for the exact-τ solve: F += Σ u_+^{1/(α-1)},
+// W += Σ u_+^{(2-α)/(α-1)} with u = (α-1)·clamp(raw·scale) - τ over the
+// visible keys (bit i of vis), and hit |= any visible u > 0 at τ = tlo.
+// Packed two-lane arithmetic for the exponent classes of α = 1.25, 1.5, 2
+// (scale > 0); powf otherwise.
+template <int PINV, int PE2>
+__device__ __forceinline__ void exact_sums(const uint32_t (&r)[32], uint32_t vis, const Shape& s, float tq,
+                                           float tlo, bool last, float& F, float& W, bool& hit) {
+    constexpr bool kPacked = (PINV == 1 || PINV == 2 || PINV == 4) && (PE2 == 1 || PE2 == 3 || PE2 == 5);
+    if (kPacked && s.scale > 0.0f) {
+        const float c = __fmul_rn(s.am1, s.scale);
+        const float2 c1 = make_float2(c, c), mt = make_float2(-tq, -tq), ml = make_float2(-tlo, -tlo);
+        // the score clamp, as bounds on u
+        const float uhi = __fmaf_rn(s.am1, 10.0f, -tq), ulo = __fmaf_rn(s.am1, -10.0f, -tq);
+        const float lhi = __fmaf_rn(s.am1, 10.0f, -tlo), llo = __fmaf_rn(s.am1, -10.0f, -tlo);
+        float2 f2 = make_float2(0.0f, 0.0f), w2 = make_float2(0.0f, 0.0f);
+        bool h = false;
+#pragma unroll
+        for (int m = 0; m < 16; ++m) {
+            const float2 x = make_float2(__uint_as_float(r[2 * m]), __uint_as_float(r[2 * m + 1]));
+            const bool v0 = (vis >> (2 * m)) & 1u, v1 = (vis >> (2 * m + 1)) & 1u;
+            float2 u = __ffma2_rn(x, c1, mt);
+            u.x = v0 ? fminf(fmaxf(u.x, ulo), uhi) : 0.0f;
+            u.y = v1 ? fminf(fmaxf(u.y, ulo), uhi) : 0.0f;
+            const float2 up = make_float2(fmaxf(u.x, 0.0f), fmaxf(u.y, 0.0f));
+            f2 = __fadd2_rn(f2, powk2<PINV>(up));
+            if constexpr (PE2 == 5) w2 = __fadd2_rn(w2, make_float2(u.x > 0.0f ? 1.0f : 0.0f, u.y > 0.0f ? 1.0f : 0.0f));
+            else w2 = __fadd2_rn(w2, powk2<PE2>(up));
+            if (last) {
+                const float2 ul = __ffma2_rn(x, c1, ml);
+                h |= (v0 && fminf(fmaxf(ul.x, llo), lhi) > 0.0f) || (v1 && fminf(fmaxf(ul.y, llo), lhi) > 0.0f);
+            }
+        }
+        F += f2.x + f2.y;
+        W += w2.x + w2.y;
+        hit |= h;
+        return;
+    }
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+        if (!((vis >> i) & 1u)) continue;
+        const float sc = clamp_score(__uint_as_float(r[i]), s.scale);
+        const float u = __fmaf_rn(s.am1, sc, -tq);
+        if (u > 0.0f) {
+            const float p = powk<PINV>(u, s.pinv.e), w = powk<PE2>(u, s.pe2.e);
+            if (isfinite(p)) F += p;
+            if (isfinite(w)) W += w;
+        }
+        if (last) hit |= __fmaf_rn(s.am1, sc, -tlo) > 0.0f;
+    }
+}
+
 // Entmax weight of one score (reference :311-316) for a known exponent class.
 template <int PK>
 __device__ __forceinline__ float entmax_pk(float u, float e) {
@@ -895,7 +975,7 @@ k1_exact(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtens
 #pragma unroll
                 for (int g = 0; g < NW; ++g) m = fmaxf(m, rp[g * TILE + row]);
                 if (!(m > neg_inf())) m = 0.0f;       // no visible key: no weight anywhere
-                hi = __fmul_rn(s.am1, clamp_score(m, s.scale));
+                hi = __fmul_rn(s.am1, m);             // m is a clamped score
                 lo = __fadd_rn(hi, -1.0f);
                 tq = lo;
             } else {
@@ -935,19 +1015,24 @@ k1_exact(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtens
             for (int cc = 0; cc < CP; ++cc) {
                 const uint32_t vis = all ? 0xffffffffu
                                          : vis_mask32(Kidx_bh, kb * TILE + (h * CP + cc) * 32, s.NK, s.causal, qpos);
+                if (pass == 0) {
+                    // the clamp is monotone for scale > 0: clamp the chunk's
+                    // largest raw score; otherwise clamp each
+                    if (s.scale > 0.0f) {
+                        uint32_t r[32];
 #pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    if (!((vis >> i) & 1u)) continue;
-                    const float sc = clamp_score(__uint_as_float(r2[cc][i]), s.scale);
-                    if (pass == 0) { a0 = fmaxf(a0, sc); continue; }
-                    const float u = __fmaf_rn(s.am1, sc, -tq);
-                    if (u > 0.0f) {
-                        const float p = powk<PINV>(u, s.pinv.e), w = powk<PE2>(u, s.pe2.e);
-                        if (isfinite(p)) a0 += p;
-                        if (isfinite(w)) a1 += w;
+                        for (int i = 0; i < 32; ++i) r[i] = ((vis >> i) & 1u) ? r2[cc][i] : 0xff800000u;
+                        float gm[11];
+                        const float cm = chunk_max(r, gm);
+                        if (cm > neg_inf()) a0 = fmaxf(a0, clamp_score(cm, s.scale));
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 32; ++i)
+                            if ((vis >> i) & 1u) a0 = fmaxf(a0, clamp_score(__uint_as_float(r2[cc][i]), s.scale));
                     }
-                    if (last) hit |= __fmaf_rn(s.am1, sc, -lo) > 0.0f;
+                    continue;
                 }
+                exact_sums<PINV, PE2>(r2[cc], vis, s, tq, lo, last, a0, a1, hit);
             }
             if (hit) flags[kb] = 1;
         }
@@ -2193,6 +2278,13 @@ k4_jac(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensor
         const float tq = qv ? tau[qrow] : 0.0f;
         const uint32_t tl = tmem_lane_base(tbase, warp);
         float A = 0.0f, B = 0.0f;
+        // packed path: u = min(raw·(α-1)·scale - τ, (α-1)·10 - τ); the clamp
+        // at -10 can only meet u <= 0, where the weight is 0
+        constexpr bool kPacked = PE2 == 1 || PE2 == 3 || PE2 == 5;
+        const bool packed_row = kPacked && qv && s.scale > 0.0f && __fmaf_rn(s.am1, -10.0f, -tq) <= 0.0f;
+        const float c1s = __fmul_rn(s.am1, s.scale);
+        const float2 c1 = make_float2(c1s, c1s), mtau = make_float2(-tq, -tq);
+        const float uhi = __fmaf_rn(s.am1, 10.0f, -tq);
         for (int j = 0; j < T; ++j) {
             const uint32_t e = sched[j];
             const int kb = (int)(e & SCHED_IDX);
@@ -2224,6 +2316,26 @@ k4_jac(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensor
             epi_arrive(&sd_free[b]);
             const uint32_t vis = all ? 0xffffffffu
                                      : (qv ? vis_mask32(Kidx_bh, kb * TILE + h * 32, s.NK, s.causal, qpos) : 0u);
+            if (kPacked && packed_row) {
+                float2 a2 = make_float2(0.0f, 0.0f), b2 = make_float2(0.0f, 0.0f);
+#pragma unroll
+                for (int m = 0; m < 16; ++m) {
+                    float2 u = __ffma2_rn(make_float2(__uint_as_float(rs[2 * m]), __uint_as_float(rs[2 * m + 1])),
+                                          c1, mtau);
+                    u.x = fminf(u.x, uhi);
+                    u.y = fminf(u.y, uhi);
+                    const bool k0 = ((vis >> (2 * m)) & 1u) && u.x > ASA_EPS;
+                    const bool k1v = ((vis >> (2 * m + 1)) & 1u) && u.y > ASA_EPS;
+                    float2 w = powk2<PE2>(make_float2(fmaxf(u.x, ASA_EPS), fmaxf(u.y, ASA_EPS)));
+                    w.x = k0 ? w.x : 0.0f;
+                    w.y = k1v ? w.y : 0.0f;
+                    a2 = __ffma2_rn(w, make_float2(__uint_as_float(rp[2 * m]), __uint_as_float(rp[2 * m + 1])), a2);
+                    b2 = __fadd2_rn(b2, w);
+                }
+                A += a2.x + a2.y;
+                B += b2.x + b2.y;
+                continue;
+            }
 #pragma unroll
             for (int i = 0; i < 32; ++i) {
                 if (!((vis >> i) & 1u)) continue;
