@@ -20,7 +20,7 @@ NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 FLAGS = ["-O3", "-std=c++17", "-gencode", "arch=compute_100a,code=sm_100a", "-lineinfo",
          "-Xcompiler", "-fPIC", "-Xcompiler", "-ffp-contract=off", "--expt-relaxed-constexpr",
          "-Xptxas", "-v" if os.environ.get("ASA_PTXAS_V") else "-O3"]
-SOURCES = ["asa_capi.cu", "asa_simt.cu", "asa_compact.cu"]
+SOURCES = ["asa_capi.cu", "asa_simt.cu", "asa_compact.cu", "asa_stable.cu"]
 # asa_tc.cu is compiled as four objects (τ/mask, forward, dQ, dK/dV) so the
 # template instantiations build in parallel.
 TC_PARTS = [("asa_tc.cu", part) for part in (1, 2, 3, 4)]

@@ -23,7 +23,7 @@ size_t tc_fwd_workspace(const Shape& s);
 size_t tc_bwd_workspace(const Shape& s);
 cudaError_t tc_tau_mask(const Shape& s, const void* Q, const void* K, const int32_t* Qidx,
                         const int32_t* Kidx, float* tau, uint8_t* M, void* ws, int* err,
-                        cudaStream_t st);
+                        cudaStream_t st, float* topv_out = nullptr, int32_t* topi_out = nullptr);
 cudaError_t tc_exact_tau(const Shape& s, const void* Q, const void* K, const int32_t* Qidx,
                          const int32_t* Kidx, float* tau, uint8_t* M, void* ws, int* err,
                          cudaStream_t st);
@@ -421,6 +421,89 @@ int asa_tau_mask_noalloc(const asa_params* p, const void* Q, const void* K, cons
     // index bounds) before reading it, so nothing needs clearing here.
     return asa_tau_mask(p, Q, K, Qidx, Kidx, tau, M, csr_ptr, csr_idx, scratch,
                         ASA_NOALLOC_SCRATCH_BYTES, stream);
+}
+
+// ---- the top-k-only ("stable") operator ---------------------------------------
+namespace {
+// Forward workspace: [the τ/mask pass's workspace | M (unused by the operator)]
+struct StableLayout {
+    size_t mask, fwd, bwd;
+};
+StableLayout stable_layout(const Shape& s, int backend) {
+    StableLayout L;
+    L.mask = align16(fwd_bytes(s, backend));
+    L.fwd = align16(L.mask + (size_t)s.BH * s.nQB * s.nKB);
+    L.bwd = align16((size_t)2 * s.BH * s.NK * s.d * sizeof(float));   // fp32 dK, dV
+    return L;
+}
+Shape stable_shape(const asa_params* p) {
+    Shape s = make_shape(p);
+    s.ref_load = 0;          // the notebook kernel reads K rows directly
+    s.exact_tau = 0;
+    return s;
+}
+}  // namespace
+
+int asa_stable_workspace_bytes(const asa_params* p, size_t* fwd, size_t* bwd) {
+    int rc = check_params(p);
+    if (rc) return rc;
+    Shape s = stable_shape(p);
+    int b = resolve(p, s);
+    if (b < 0) return -b;
+    StableLayout L = stable_layout(s, b);
+    if (fwd) *fwd = L.fwd;
+    if (bwd) *bwd = L.bwd;
+    return ASA_OK;
+}
+
+int asa_stable_forward(const asa_params* p, const void* Q, const void* K, const void* V,
+                       const int32_t* Qidx, const int32_t* Kidx, void* O, float* top_val,
+                       int32_t* top_idx, float* weights, float* tau, float* tau_coef, void* ws,
+                       size_t ws_bytes, asa_stream_t stream) {
+    int rc = check_params(p);
+    if (rc) return rc;
+    Shape s = stable_shape(p);
+    int b = resolve(p, s);
+    if (b < 0) return -b;
+    if (s.NQ == 0) return ASA_OK;
+    if (!Q || !O || !top_val || !top_idx || !weights || !tau || !tau_coef) return ASA_ERR_INVALID;
+    if (s.NK && (!K || !V)) return ASA_ERR_INVALID;
+    if (p->causal && (!Qidx || (!Kidx && s.NK))) return ASA_ERR_INVALID;
+    StableLayout L = stable_layout(s, b);
+    if (!ws || ws_bytes < L.fwd) return ASA_ERR_WORKSPACE;
+    cudaStream_t st = (cudaStream_t)stream;
+    uint8_t* M = (uint8_t*)ws + L.mask;
+    cudaError_t e;
+    {
+        ProfScope ps("stable_topk", st);
+        e = b == ASA_BACKEND_TC
+                ? asa::tc_tau_mask(s, Q, K, Qidx, Kidx, nullptr, M, ws, error_word(), st, top_val, top_idx)
+                : asa::simt_tau_mask(s, Q, K, Qidx, Kidx, nullptr, M, st, top_val, top_idx);
+    }
+    if (e != cudaSuccess) return cuda_status(e);
+    ProfScope ps("stable_forward", st);
+    return cuda_status(asa::stable_forward(s, p->alpha, V, top_val, top_idx, O, tau, weights, tau_coef, st));
+}
+
+int asa_stable_backward(const asa_params* p, const void* Q, const void* K, const void* V,
+                        const float* top_val, const int32_t* top_idx, const float* weights,
+                        const float* tau, const float* tau_coef, const void* dO, void* dQ, void* dK,
+                        void* dV, void* ws, size_t ws_bytes, asa_stream_t stream) {
+    int rc = check_params(p);
+    if (rc) return rc;
+    Shape s = stable_shape(p);
+    int b = resolve(p, s);
+    if (b < 0) return -b;
+    StableLayout L = stable_layout(s, b);
+    if (!ws || ws_bytes < L.bwd) return ASA_ERR_WORKSPACE;
+    if (s.NQ && (!Q || !dO || !dQ || !top_val || !top_idx || !weights || !tau || !tau_coef))
+        return ASA_ERR_INVALID;
+    if (s.NK && (!K || !V || !dK || !dV)) return ASA_ERR_INVALID;
+    float* dK32 = (float*)ws;
+    float* dV32 = dK32 + (size_t)s.BH * s.NK * s.d;
+    ProfScope ps("stable_backward", (cudaStream_t)stream);
+    return cuda_status(asa::stable_backward(s, p->alpha, Q, K, V, dO, top_val, top_idx, weights, tau,
+                                            tau_coef, dQ, dK32, dV32, dK, dV, (cudaStream_t)stream));
 }
 
 int asa_scrub(int dtype, void* x, size_t n, void* ws, asa_stream_t stream) {

@@ -50,8 +50,10 @@ __device__ __forceinline__ bool ref_keep(const Shape& s, const int32_t* __restri
 void note_launch(int n = 1);
 
 // ---- SIMT kernels (asa_simt.cu) -------------------------------------------
+// topv / topi (optional): each row's top-k scores and keys in order.
 cudaError_t simt_tau_mask(const Shape& s, const void* Q, const void* K, const int32_t* Qidx,
-                          const int32_t* Kidx, float* tau, uint8_t* M, cudaStream_t st);
+                          const int32_t* Kidx, float* tau, uint8_t* M, cudaStream_t st,
+                          float* topv = nullptr, int32_t* topi = nullptr);
 cudaError_t simt_forward(const Shape& s, const void* Q, const void* K, const void* V,
                          const int32_t* Qidx, const int32_t* Kidx, const float* tau,
                          const int32_t* ptr, const int32_t* idx, void* O, float* O32,
@@ -76,6 +78,18 @@ cudaError_t simt_jacobian_stats(const Shape& s, const void* Q, const void* K, co
                                 const int32_t* Qidx, const int32_t* Kidx, const float* tau,
                                 const int32_t* ptr, const int32_t* idx, const void* dO,
                                 float* invN, float* accdO, cudaStream_t st);
+
+// ---- top-k-only ("stable") operator (asa_stable.cu) ---------------------------
+// From each row's top-k scores and keys (in order): τ by the five-step
+// bisection, the normalised weights, O = Σ_j w_j V[key_j]; and its gradient.
+cudaError_t stable_forward(const Shape& s, float alpha, const void* V, const float* topv,
+                           const int32_t* topi, void* O, float* tau, float* weights,
+                           float* tau_coef, cudaStream_t st);
+cudaError_t stable_backward(const Shape& s, float alpha, const void* Q, const void* K,
+                            const void* V, const void* dO, const float* topv,
+                            const int32_t* topi, const float* weights, const float* tau,
+                            const float* tau_coef, void* dQ, float* dK32, float* dV32,
+                            void* dK, void* dV, cudaStream_t st);
 
 // ---- tile lists (asa_compact.cu) --------------------------------------------
 // CSR of M in the reference's format (build_lookup_kernel :219-242), and the

@@ -70,7 +70,8 @@ template <typename T, int DM, int KM>
 __global__ void __launch_bounds__(QTHREADS)
 simt_tau_mask_kernel(Shape sh, const T* __restrict__ Q, const T* __restrict__ K,
                      const int32_t* __restrict__ Qidx, const int32_t* __restrict__ Kidx,
-                     float* __restrict__ tau, uint8_t* __restrict__ M) {
+                     float* __restrict__ tau, uint8_t* __restrict__ M, float* __restrict__ topv,
+                     int32_t* __restrict__ topi) {
     __shared__ float Ks[KT][DM];
     __shared__ int Kp[KT];
     __shared__ int red[QTHREADS / 32];
@@ -138,7 +139,15 @@ simt_tau_mask_kernel(Shape sh, const T* __restrict__ Q, const T* __restrict__ K,
         __syncthreads();
     }
     if (!qv) return;
-    tau[qrow] = ref_tau<KM>(tk.v, sh.k, sh.alpha);
+    if (topv) {   // the row's top-k in order (score desc, key asc)
+#pragma unroll
+        for (int j = 0; j < KM; ++j)
+            if (j >= KM - sh.k) {
+                topv[qrow * sh.k + j - (KM - sh.k)] = tk.v[j];
+                topi[qrow * sh.k + j - (KM - sh.k)] = tk.i[j];
+            }
+    }
+    if (tau) tau[qrow] = ref_tau<KM>(tk.v, sh.k, sh.alpha);
     const size_t base = ((size_t)bh * sh.nQB + qb) * sh.nKB;
 #pragma unroll
     for (int j = 0; j < KM; ++j)
@@ -574,11 +583,12 @@ cudaError_t set_smem(F* f, size_t bytes) {
 
 template <typename T, int DM, int KM>
 cudaError_t launch_tau_mask(const Shape& s, const void* Q, const void* K, const int32_t* Qidx,
-                            const int32_t* Kidx, float* tau, uint8_t* M, cudaStream_t st) {
+                            const int32_t* Kidx, float* tau, uint8_t* M, float* topv, int32_t* topi,
+                            cudaStream_t st) {
     const int QT = qthreads(s.BM);
     dim3 grid(s.nQB * ((s.BM + QT - 1) / QT), s.BH);
     simt_tau_mask_kernel<T, DM, KM><<<grid, QT, 0, st>>>(
-        s, (const T*)Q, (const T*)K, Qidx, Kidx, tau, M);
+        s, (const T*)Q, (const T*)K, Qidx, Kidx, tau, M, topv, topi);
     note_launch();
     return cudaGetLastError();
 }
@@ -624,13 +634,14 @@ cudaError_t launch_dkdv(const Shape& s, const void* Q, const void* K, const void
 }  // namespace
 
 cudaError_t simt_tau_mask(const Shape& s, const void* Q, const void* K, const int32_t* Qidx,
-                          const int32_t* Kidx, float* tau, uint8_t* M, cudaStream_t st) {
+                          const int32_t* Kidx, float* tau, uint8_t* M, cudaStream_t st, float* topv,
+                          int32_t* topi) {
     cudaError_t e = cudaMemsetAsync(M, 0, (size_t)s.BH * s.nQB * s.nKB, st);
     if (e != cudaSuccess) return e;
     ASA_DISPATCH_T(s.in_dtype, T, ASA_DISPATCH_DM(s.d, DM, {
-        if (s.k <= 8) return launch_tau_mask<T, DM, 8>(s, Q, K, Qidx, Kidx, tau, M, st);
-        if (s.k <= 16) return launch_tau_mask<T, DM, 16>(s, Q, K, Qidx, Kidx, tau, M, st);
-        return launch_tau_mask<T, DM, 32>(s, Q, K, Qidx, Kidx, tau, M, st);
+        if (s.k <= 8) return launch_tau_mask<T, DM, 8>(s, Q, K, Qidx, Kidx, tau, M, topv, topi, st);
+        if (s.k <= 16) return launch_tau_mask<T, DM, 16>(s, Q, K, Qidx, Kidx, tau, M, topv, topi, st);
+        return launch_tau_mask<T, DM, 32>(s, Q, K, Qidx, Kidx, tau, M, topv, topi, st);
     }));
     return cudaErrorInvalidValue;
 }

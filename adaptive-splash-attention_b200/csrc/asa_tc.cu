@@ -543,7 +543,7 @@ template <int D, int KM, int NW>
 __global__ void __launch_bounds__(64 + 128 * NW, 1)
 k1_tau_mask(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK, Shape s,
             const int32_t* __restrict__ Qidx, const int32_t* __restrict__ Kidx, Bounds bd,
-            float* __restrict__ topv, uint8_t* __restrict__ M, int* err) {
+            float* __restrict__ topv, int32_t* __restrict__ topi, uint8_t* __restrict__ M, int* err) {
     constexpr int NE = 128 * NW;              // epilogue threads
     constexpr int CP = 4 / NW;                // 32-column chunks per thread per tile
     constexpr int S = 3;                      // K stages
@@ -817,6 +817,7 @@ k1_tau_mask(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
                     if (cur[g] > best) { best = cur[g]; bg = g; }
                 out[rk] = order_value(best);
                 const int key = order_index(best);
+                if (topi) topi[((size_t)bh * s.NQ + q) * s.k + rk] = key;
                 if (key >= 0) flags[key / TILE] = 1;
 #pragma unroll
                 for (int g = 0; g < NW; ++g)
@@ -2511,14 +2512,16 @@ cudaError_t with_dtype_d(const Shape& s, F&& f) {
 #if ASA_PART(1)
 cudaError_t tc_tau_mask(const Shape& s, const void* Q, const void* K, const int32_t* Qidx,
                         const int32_t* Kidx, float* tau, uint8_t* M, void* ws, int* err,
-                        cudaStream_t st) {
+                        cudaStream_t st, float* topv_out, int32_t* topi_out) {
     cudaError_t e = launch_bounds(s, Qidx, Kidx, ws, st);
     if (e != cudaSuccess) return e;
     CUtensorMap mQ, mK;
     if (!make_map(&mQ, Q, s.BH, s.NQ, s.d) || !make_map(&mK, K, s.BH, s.NK, s.d)) return cudaErrorInvalidValue;
     Bounds bd = bounds_at(s, ws);
     dim3 grid(s.nQB, s.BH);
-    float* topv = (float*)((char*)ws + topv_offset(s));
+    // the rows' top-k scores (and keys) in order: the caller's buffers, or
+    // the workspace when only τ and the mask are wanted
+    float* topv = topv_out ? topv_out : (float*)((char*)ws + topv_offset(s));
     const size_t rows = (size_t)s.BH * s.NQ;
     auto go = [&](auto kern, auto solve, int D, int NW) -> cudaError_t {
         const int S = 3;
@@ -2526,10 +2529,10 @@ cudaError_t tc_tau_mask(const Shape& s, const void* Q, const void* K, const int3
                             24 * 8 + 16 + 2 * TILE * 4 + 64 + (size_t)s.nKB * 5 + 64;
         cudaError_t r = prep(kern, smem);
         if (r != cudaSuccess) return r;
-        kern<<<grid, 64 + 128 * NW, smem, st>>>(mQ, mK, s, Qidx, Kidx, bd, topv, M, err);
+        kern<<<grid, 64 + 128 * NW, smem, st>>>(mQ, mK, s, Qidx, Kidx, bd, topv, topi_out, M, err);
         note_launch();
         r = cudaGetLastError();
-        if (r != cudaSuccess) return r;
+        if (r != cudaSuccess || !tau) return r;
         solve<<<(unsigned)((rows + 127) / 128), 128, 0, st>>>(topv, tau, rows, s.k, s.alpha);
         note_launch();
         return cudaGetLastError();

@@ -22,7 +22,7 @@ import torch
 
 from . import _lib
 from .ops import Settings, forward_saved, backward_saved, tau_mask, scrub_, device_error, \
-    resolved_backend, make_params, _index, _check_inputs
+    resolved_backend, make_params, _index, _check_inputs, stable_forward_saved, stable_backward_saved
 from .streamed import forward_backward_host
 
 _lib.lib()  # fail at import time if the native library is missing
@@ -35,7 +35,8 @@ torch.ops.load_library(_TORCH_OPS)
 _ops = torch.ops.splash_attention
 
 __all__ = ["AdaptiveSplashAttention", "splash_attention", "forward", "backward", "tau_mask",
-           "Settings", "device_error", "forward_backward_host"]
+           "Settings", "device_error", "forward_backward_host", "stable_attention", "stable_forward",
+           "stable_backward"]
 
 # Reference compile-time defaults (adasplashattention.cu:8-19).
 REF_BLOCK_M, REF_BLOCK_N, REF_K_KEEP = 32, 64, 8
@@ -176,3 +177,49 @@ def backward(Q, K, V, Q_idx, K_idx, sm_scale, alpha, dOut):
     _, saved = forward_saved(Q, K, V, Q_idx, K_idx, st, need_o32=True)
     grads = backward_saved(Q, K, V, dOut, saved)
     return [scrub_(g) for g in grads]
+
+
+# ---- the notebook's top-k-only ("stable") operator -----------------------------
+class _StableFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, Q, K, V, Q_idx, K_idx, st):
+        O, saved = stable_forward_saved(Q, K, V, Q_idx, K_idx, st)
+        ctx.saved = saved
+        ctx.save_for_backward(Q, K, V)
+        return O
+
+    @staticmethod
+    def backward(ctx, dO):
+        Q, K, V = ctx.saved_tensors
+        dQ, dK, dV = stable_backward_saved(Q, K, V, dO, ctx.saved)
+        return dQ.to(Q.dtype), dK.to(K.dtype), dV.to(V.dtype), None, None, None
+
+
+def stable_attention(Q, K, V, Q_idx=None, K_idx=None, *, alpha=1.5, sm_scale=None, k_keep=8,
+                     causal=True, backend="auto", out_dtype=None):
+    """The reference notebook's top-k-only α-entmax attention
+    (AdaSplashNotebook.ipynb, stable_splash_kernel): each query attends to
+    its k_keep highest-scoring visible keys with bisection-τ α-entmax
+    weights, O = Σ_j w_j V[key_j].  Autograd gives the operator's gradient
+    (the notebook's backward returns zeros).  Q, K, V: [B, H, N, d] float32
+    or bfloat16 on CUDA."""
+    st = Settings(alpha=alpha, sm_scale=sm_scale, k_keep=k_keep, causal=causal, backend=backend,
+                  out_dtype=out_dtype, ref_tile_load=False)
+    return _StableFn.apply(Q, K, V, Q_idx, K_idx, st)
+
+
+def stable_forward(Q, K, V, Q_idx, K_idx, sm_scale, alpha):
+    """The notebook's stable module ``forward(Q, K, V, Q_idx, K_idx,
+    sm_scale, alpha)`` (K_KEEP = 8): returns O in Q's dtype."""
+    O, _ = stable_forward_saved(Q, K, V, Q_idx, K_idx,
+                                Settings(alpha=alpha, sm_scale=sm_scale, k_keep=REF_K_KEEP,
+                                         ref_tile_load=False))
+    return O
+
+
+def stable_backward(Q, K, V, Q_idx, K_idx, sm_scale, alpha, dOut):
+    """The notebook's stable module ``backward(...)`` signature with the
+    operator's gradient: returns [dQ, dK, dV]."""
+    st = Settings(alpha=alpha, sm_scale=sm_scale, k_keep=REF_K_KEEP, ref_tile_load=False)
+    _, saved = stable_forward_saved(Q, K, V, Q_idx, K_idx, st)
+    return list(stable_backward_saved(Q, K, V, dOut, saved))

@@ -23,7 +23,8 @@ SYMBOLS = ("asa_params_default", "asa_workspace_bytes", "asa_resolve_backend", "
            "asa_forward", "asa_backward", "asa_scrub", "asa_device_error", "asa_status_string",
            "asa_version", "asa_profile_begin", "asa_profile_end", "asa_profile_get",
            "asa_launch_count", "asa_last_cuda_error", "asa_tau_mask_noalloc",
-           "asa_device_error_async", "asa_wait_probe")
+           "asa_device_error_async", "asa_wait_probe", "asa_stable_workspace_bytes",
+           "asa_stable_forward", "asa_stable_backward")
 NOALLOC_SCRATCH_BYTES = 1 << 20
 
 
@@ -85,6 +86,9 @@ def lib():
         L.asa_tau_mask_noalloc.argtypes = [pp, vp, vp, vp, vp, vp, vp, vp, vp, vp]
         L.asa_device_error_async.argtypes = [vp, ctypes.POINTER(ctypes.c_int)]
         L.asa_wait_probe.argtypes = [ctypes.c_longlong, vp]
+        L.asa_stable_workspace_bytes.argtypes = [pp, ctypes.POINTER(sz), ctypes.POINTER(sz)]
+        L.asa_stable_forward.argtypes = [pp] + [vp] * 11 + [vp, sz, vp]
+        L.asa_stable_backward.argtypes = [pp] + [vp] * 12 + [vp, sz, vp]
         L.asa_last_cuda_error.argtypes = []
         L.asa_last_cuda_error.restype = ctypes.c_char_p
         for name in SYMBOLS:

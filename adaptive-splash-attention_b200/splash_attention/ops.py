@@ -300,3 +300,64 @@ class profile:
 
 def launch_count():
     return int(L.lib().asa_launch_count())
+
+
+class StableSaved:
+    """What the top-k-only operator's forward hands its backward."""
+    __slots__ = ("top_val", "top_idx", "weights", "tau", "tau_coef", "params")
+
+
+def stable_forward_saved(Q, K, V, Q_idx, K_idx, st: Settings):
+    """The notebook's top-k-only ("stable") operator (asa_stable_forward);
+    returns (O, StableSaved).  Q, K, V: [B, H, N, d]."""
+    _check_inputs(Q, K, V)
+    Q, K, V = Q.contiguous(), K.contiguous(), V.contiguous()
+    if V.shape != K.shape or V.dtype != Q.dtype or K.dtype != Q.dtype:
+        raise ValueError("stable_attention: V must match K in shape and Q in dtype")
+    p = make_params(Q, K, st)
+    BH = p.B * p.H
+    dev = Q.device
+    qi = _index(Q_idx, BH, p.NQ, dev, "Q_idx") if st.causal else None
+    ki = _index(K_idx, BH, p.NK, dev, "K_idx") if st.causal else None
+    O = torch.empty(p.B, p.H, p.NQ, p.d, device=dev, dtype=_torch_dtype(p.out_dtype))
+    s = StableSaved()
+    s.top_val = torch.empty(BH, p.NQ, p.k_keep, device=dev, dtype=torch.float32)
+    s.top_idx = torch.empty(BH, p.NQ, p.k_keep, device=dev, dtype=torch.int32)
+    s.weights = torch.empty(BH, p.NQ, p.k_keep, device=dev, dtype=torch.float32)
+    s.tau = torch.empty(BH, p.NQ, device=dev, dtype=torch.float32)
+    s.tau_coef = torch.empty(BH, p.NQ, device=dev, dtype=torch.float32)
+    s.params = p
+    fwd, bwd = ctypes.c_size_t(), ctypes.c_size_t()
+    L.check(L.lib().asa_stable_workspace_bytes(ctypes.byref(p), ctypes.byref(fwd), ctypes.byref(bwd)),
+            "asa_stable_workspace_bytes")
+    ws = torch.empty(fwd.value, device=dev, dtype=torch.uint8)
+    check_device_errors(dev)
+    L.check(L.lib().asa_stable_forward(ctypes.byref(p), _ptr(Q), _ptr(K), _ptr(V), _ptr(qi), _ptr(ki),
+                                       _ptr(O), _ptr(s.top_val), _ptr(s.top_idx), _ptr(s.weights),
+                                       _ptr(s.tau), _ptr(s.tau_coef), _ptr(ws), fwd.value, _stream()),
+            "asa_stable_forward")
+    return O, s
+
+
+def stable_backward_saved(Q, K, V, dO, s: StableSaved):
+    """Gradient of the top-k-only operator (asa_stable_backward)."""
+    p = s.params
+    Q, K, V = Q.contiguous(), K.contiguous(), V.contiguous()
+    dO = dO.to(Q.dtype).contiguous()
+    dev = Q.device
+    out_dt = _torch_dtype(p.out_dtype)
+    dQ = torch.empty(Q.shape, device=dev, dtype=out_dt)
+    dK = torch.empty(K.shape, device=dev, dtype=out_dt)
+    dV = torch.empty(V.shape, device=dev, dtype=out_dt)
+    fwd, bwd = ctypes.c_size_t(), ctypes.c_size_t()
+    L.check(L.lib().asa_stable_workspace_bytes(ctypes.byref(p), ctypes.byref(fwd), ctypes.byref(bwd)),
+            "asa_stable_workspace_bytes")
+    ws = torch.empty(bwd.value, device=dev, dtype=torch.uint8)
+    check_device_errors(dev)
+    L.check(L.lib().asa_stable_backward(ctypes.byref(p), _ptr(Q), _ptr(K), _ptr(V), _ptr(s.top_val),
+                                        _ptr(s.top_idx), _ptr(s.weights), _ptr(s.tau), _ptr(s.tau_coef),
+                                        _ptr(dO), _ptr(dQ), _ptr(dK), _ptr(dV), _ptr(ws), bwd.value,
+                                        _stream()),
+            "asa_stable_backward")
+    _poll_device_errors(dev)
+    return dQ, dK, dV

@@ -167,6 +167,34 @@ int asa_backward(const asa_params* p, const void* Q, const void* K, const void* 
                  const void* dO, void* dQ, void* dK, void* dV,
                  void* ws, size_t ws_bytes, asa_stream_t stream);
 
+/* The top-k-only ("stable") operator of the reference notebook
+ * (AdaSplashNotebook.ipynb file lines 303-450: stable_entmax_threshold,
+ * stable_splash_kernel, stable_forward): per query the top-k clamped scores
+ * of the visible keys (k_keep; the same top-k as asa_tau_mask, with no
+ * tile-load zeroing), τ by five bisection steps (α clamped to [1.01, 3]),
+ * the weights p_j / max(Σp, EPS) and O = Σ_j w_j V[key_j].  block_m/block_n
+ * only choose the kernels of the top-k pass (128x128 with bf16 and d in
+ * {64, 128}: tcgen05).  Outputs besides O, kept for the backward, are
+ * [B*H*NQ*k] top_val (clamped scores, descending) and top_idx (keys, -1 for
+ * a row with fewer visible keys), weights, and per row tau and tau_coef (the
+ * weight of the bisection's upper start in τ). */
+int asa_stable_workspace_bytes(const asa_params* p, size_t* fwd_bytes, size_t* bwd_bytes);
+int asa_stable_forward(const asa_params* p, const void* Q, const void* K, const void* V,
+                       const int32_t* Q_idx, const int32_t* K_idx, void* O, float* top_val,
+                       int32_t* top_idx, float* weights, float* tau, float* tau_coef,
+                       void* ws, size_t ws_bytes, asa_stream_t stream);
+
+/* Gradient of asa_stable_forward (the notebook's stable_backward returns
+ * zeros, nb:470-476): τ enters through the bisection's starting bracket,
+ * whose ends depend on the largest and smallest kept score; a clamped score
+ * passes no gradient.  dQ, dK, dV are out_dtype and fully overwritten; dK
+ * and dV are gathered with fp32 atomics, so their last bits can vary run to
+ * run. */
+int asa_stable_backward(const asa_params* p, const void* Q, const void* K, const void* V,
+                        const float* top_val, const int32_t* top_idx, const float* weights,
+                        const float* tau, const float* tau_coef, const void* dO, void* dQ,
+                        void* dK, void* dV, void* ws, size_t ws_bytes, asa_stream_t stream);
+
 /* The reference's host-side scrub done on the device: NaN -> 0, and if any
  * element is ±Inf the whole tensor is clamped to [-100, 100]
  * (:599-606, :684-697).  ws needs 16 bytes. */

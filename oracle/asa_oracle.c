@@ -423,3 +423,72 @@ void asa_oracle_backward(const asa_oracle_cfg* c, const float* Q, const float* K
         }
     free(invN); free(accdO); free(active);
 }
+
+/* The reference notebook's top-k-only "stable" operator
+ * (AdaSplashNotebook.ipynb file lines 303-375, stable_entmax_threshold, and
+ * 376-450, stable_splash_kernel), from each row's top-k lists as
+ * asa_oracle_tau_mask produces them (with ref_tile_load = 0: the notebook
+ * kernel reads K rows directly): α clamped to [1.01, 3]; τ by five
+ * bisection steps from [(α-1)s_min - 1, (α-1)s_max + 1] with the |f| < 1e-4
+ * exit and the τ clamp; p_j = u_j^{1/(α-1)} for u_j > EPS, normalised by
+ * max(Σp, EPS), a non-finite weight -> 1/k; O = Σ_j p_j V[key_j] in j order
+ * (one FMA per step), non-finite -> 0.  tau_coef receives the weight of the
+ * upper start (or of the upper τ clamp) in the final τ. */
+void asa_oracle_stable_forward(const asa_oracle_cfg* c, const float* V, const float* topv,
+                               const int32_t* topi, float* O, float* tau_out, float* weights,
+                               float* tau_coef) {
+    const int k = c->k_keep, d = c->d;
+    const float alpha = fmaxf(1.01f, fminf(c->alpha, 3.0f));
+    const float am1 = alpha - 1.0f;
+    const float inv = 1.0f / am1;
+    #pragma omp parallel for schedule(static)
+    for (long r = 0; r < (long)c->BH * c->NQ; ++r) {
+        const float* s = topv + (size_t)r * k;
+        const float s_max = s[0], s_min = s[k - 1];
+        float lo = fmaf(am1, s_min, -1.0f), hi = fmaf(am1, s_max, 1.0f);
+        float clo = 0.0f, chi = 1.0f;
+        float tau = 0.5f * (lo + hi), ct = 0.5f;
+        for (int it = 0; it < ASA_MAX_HALLEY; ++it) {
+            float f = -1.0f;
+            for (int j = 0; j < k; ++j) {
+                const float u = fmaf(am1, s[j], -tau);
+                if (u <= 0.0f) break;
+                float up = powf(fmaxf(u, ASA_EPS), inv);
+                if (isnan(up) || isinf(up)) up = 0.0f;
+                f += up;
+            }
+            if (fabsf(f) < 1e-4f) break;
+            if (f > 0.0f) { lo = tau; clo = ct; } else { hi = tau; chi = ct; }
+            tau = 0.5f * (lo + hi);
+            ct = 0.5f * (clo + chi);
+            const float tmin = fmaf(s_min, am1, -10.0f), tmax = fmaf(s_max, am1, 10.0f);
+            if (tau < tmin) { tau = tmin; ct = 0.0f; }
+            if (tau > tmax) { tau = tmax; ct = 1.0f; }
+        }
+        float p[ASA_KMAX], norm = 0.0f;
+        for (int j = 0; j < k; ++j) {
+            const float u = fmaf(am1, s[j], -tau);
+            float pj = (u > ASA_EPS) ? powf(u, inv) : 0.0f;
+            if (isnan(pj) || isinf(pj)) pj = 0.0f;
+            p[j] = pj;
+            norm += pj;
+        }
+        norm = fmaxf(norm, ASA_EPS);
+        for (int j = 0; j < k; ++j) {
+            p[j] /= norm;
+            if (isnan(p[j]) || isinf(p[j])) p[j] = 1.0f / k;
+            weights[(size_t)r * k + j] = p[j];
+        }
+        tau_out[r] = tau;
+        tau_coef[r] = ct;
+        const size_t bh = (size_t)r / c->NQ;
+        for (int t = 0; t < d; ++t) {
+            float acc = 0.0f;
+            for (int j = 0; j < k; ++j) {
+                const int key = topi[(size_t)r * k + j];
+                if (key >= 0) acc = fmaf(p[j], V[(bh * c->NK + key) * d + t], acc);
+            }
+            O[(size_t)r * d + t] = (isnan(acc) || isinf(acc)) ? 0.0f : acc;
+        }
+    }
+}

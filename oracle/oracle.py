@@ -43,6 +43,7 @@ def lib():
                                             f32p, ctypes.c_void_p]
         _lib.asa_oracle_backward.argtypes = [cfgp, f32p, f32p, f32p, i32p, i32p, f32p, i32p, i32p,
                                              f32p, f32p, f32p, f32p]
+        _lib.asa_oracle_stable_forward.argtypes = [cfgp, f32p, f32p, i32p, f32p, f32p, f32p, f32p]
     return _lib
 
 
@@ -148,3 +149,23 @@ def run_all(cfg, Q, K, V, Qidx, Kidx, dO=None):
     if dO is not None:
         out["dQ"], out["dK"], out["dV"] = backward(cfg, Q, K, V, Qidx, Kidx, tau, ptr, idx, dO)
     return out
+
+
+def stable_forward(cfg, Q, K, V, Qidx, Kidx):
+    """The notebook's top-k-only ("stable") operator: the top-k lists of
+    tau_mask (without the reference's tile-load zeroing, as the notebook
+    kernel reads K directly), then its bisection τ, weights and output."""
+    import copy
+    c0 = copy.copy(cfg)
+    c0.ref_tile_load = False
+    _, _, topv, topi = tau_mask(c0, Q, K, Qidx, Kidx, want_topk=True)
+    rows = cfg.BH * cfg.NQ
+    O = np.zeros((cfg.BH, cfg.NQ, cfg.d), np.float32)
+    tau = np.zeros(rows, np.float32)
+    coef = np.zeros(rows, np.float32)
+    w = np.zeros((rows, cfg.k_keep), np.float32)
+    c = c0.c()
+    lib().asa_oracle_stable_forward(ctypes.byref(c), _f32(V), np.ascontiguousarray(topv, np.float32),
+                                    np.ascontiguousarray(topi, np.int32), O, tau, w, coef)
+    return dict(O=O, tau=tau.reshape(cfg.BH, cfg.NQ), weights=w.reshape(cfg.BH, cfg.NQ, -1),
+                tau_coef=coef.reshape(cfg.BH, cfg.NQ), topv=topv, topi=topi)
