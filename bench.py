@@ -226,9 +226,17 @@ def cpu_baseline(c, heads=1, max_n=8192):
     return flops / t / 1e12, t, sample, threads
 
 
+def use_all_host_cores():
+    """The CPU arms use every core this process may run on: torchrun sets
+    OMP_NUM_THREADS=1 for its ranks, which would leave the OpenMP oracle on
+    one core.  Must run before the oracle library is first loaded."""
+    os.environ["OMP_NUM_THREADS"] = str(len(os.sched_getaffinity(0)))
+
+
 def run_reference_arm(a, c, rank, world):
     if rank != 0:
         return 0
+    use_all_host_cores()
     heads = c["B"] * c["H"] if a.config in ("C1", "C2") else 1
     for _ in range(a.warmup):
         cpu_baseline(c, heads)
@@ -440,6 +448,7 @@ def measure(a, c, name, rank, world, dev, scaling, dist, with_extras=True):
 
     rec["cpu_baseline"] = None
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        use_all_host_cores()
         heads = c["B"] * c["H"] if name in ("C1", "C2") else 1
         v_, t_, sample, threads = cpu_baseline(c, heads)
         rec["cpu_baseline"] = {"value": v_, "unit": "TFLOP/s", "cores": threads, "kind": "port",
