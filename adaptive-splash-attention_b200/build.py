@@ -21,9 +21,9 @@ FLAGS = ["-O3", "-std=c++17", "-gencode", "arch=compute_100a,code=sm_100a", "-li
          "-Xcompiler", "-fPIC", "-Xcompiler", "-ffp-contract=off", "--expt-relaxed-constexpr",
          "-Xptxas", "-v" if os.environ.get("ASA_PTXAS_V") else "-O3"]
 SOURCES = ["asa_capi.cu", "asa_simt.cu", "asa_compact.cu", "asa_stable.cu"]
-# asa_tc.cu is compiled as four objects (τ/mask, forward, dQ, dK/dV) so the
-# template instantiations build in parallel.
-TC_PARTS = [("asa_tc.cu", part) for part in (1, 2, 3, 4)]
+# asa_tc.cu is compiled as five objects (τ/mask, forward, dQ, dK/dV, fused
+# forward) so the template instantiations build in parallel.
+TC_PARTS = [("asa_tc.cu", part) for part in (1, 2, 3, 4, 5)]
 
 
 def _deps():

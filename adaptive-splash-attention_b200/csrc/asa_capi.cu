@@ -31,6 +31,10 @@ cudaError_t tc_forward(const Shape& s, const void* Q, const void* K, const void*
                        const int32_t* Qidx, const int32_t* Kidx, const float* tau,
                        const int32_t* ptr, const int32_t* idx, void* O, float* O32,
                        float* rownorm, void* ws, int* err, cudaStream_t st);
+bool tc_fused_supported(const Shape& s);
+cudaError_t tc_fused_forward(const Shape& s, const void* Q, const void* K, const void* V,
+                             const int32_t* Qidx, const int32_t* Kidx, float* tau, uint8_t* M,
+                             void* O, float* O32, float* rownorm, void* ws, int* err, cudaStream_t st);
 cudaError_t tc_backward(const Shape& s, const void* Q, const void* K, const void* V,
                         const int32_t* Qidx, const int32_t* Kidx, const float* O32,
                         const float* tau, const int32_t* ptr, const int32_t* idx,
@@ -124,6 +128,7 @@ int check_params(const asa_params* p) {
     if (p->precision != ASA_PREC_SPLIT && p->precision != ASA_PREC_BF16) return ASA_ERR_INVALID;
     if (p->tau_mode != ASA_TAU_REFERENCE && p->tau_mode != ASA_TAU_EXACT) return ASA_ERR_INVALID;
     if (p->grad_mode != ASA_GRAD_REFERENCE && p->grad_mode != ASA_GRAD_JACOBIAN) return ASA_ERR_INVALID;
+    if (p->fused_forward != 0 && p->fused_forward != 1) return ASA_ERR_INVALID;
     if (p->d > 128) return ASA_ERR_UNSUPPORTED;        // reference D_MAX (:14-16)
     if (p->k_keep > 32) return ASA_ERR_UNSUPPORTED;
     const long long BH = (long long)p->B * p->H;
@@ -233,6 +238,7 @@ void asa_params_default(asa_params* p) {
     p->ref_tile_load = 1;
     p->tau_mode = ASA_TAU_REFERENCE;
     p->grad_mode = ASA_GRAD_REFERENCE;
+    p->fused_forward = 1;
 }
 
 int asa_resolve_backend(const asa_params* p) {
@@ -296,10 +302,25 @@ int asa_forward(const asa_params* p, const void* Q, const void* K, const void* V
     if (s.NQ == 0) return ASA_OK;
     if (!O || !csr_ptr || !csr_idx || !rownorm) return ASA_ERR_INVALID;
     if (!V && s.NK) return ASA_ERR_INVALID;
-    rc = asa_tau_mask(p, Q, K, Qidx, Kidx, tau, M, csr_ptr, csr_idx, ws, ws_bytes, stream);
-    if (rc) return rc;
     cudaStream_t st = (cudaStream_t)stream;
     cudaError_t e;
+    if (b == ASA_BACKEND_TC && p->fused_forward && asa::tc_fused_supported(s)) {
+        // one kernel: τ / mask and the forward; the tile lists (an output the
+        // backward reads) follow from the mask
+        if (!Q || !K || !tau || !M || (p->causal && (!Qidx || !Kidx))) return ASA_ERR_INVALID;
+        if (ws_bytes < fwd_bytes(s, b) || !ws) return ASA_ERR_WORKSPACE;
+        {
+            ProfScope ps("forward_fused", st);
+            e = asa::tc_fused_forward(s, Q, K, V, Qidx, Kidx, tau, M, O, O32, rownorm, ws, error_word(), st);
+        }
+        if (e == cudaSuccess) {
+            ProfScope ps("tile_lists", st);
+            e = asa::build_lists(s, M, csr_ptr, csr_idx, nullptr, nullptr, st);
+        }
+        return cuda_status(e);
+    }
+    rc = asa_tau_mask(p, Q, K, Qidx, Kidx, tau, M, csr_ptr, csr_idx, ws, ws_bytes, stream);
+    if (rc) return rc;
     ProfScope ps("forward", st);
     if (b == ASA_BACKEND_TC)
         e = asa::tc_forward(s, Q, K, V, Qidx, Kidx, tau, csr_ptr, csr_idx, O, O32, rownorm, ws,

@@ -50,16 +50,9 @@ using namespace sm100;
 constexpr int TILE = 128;
 constexpr int BOX = 64;                    // bf16 elements per 128-byte swizzle row
 constexpr int BOX_BYTES = TILE * 128;      // one 64-column box of 128 rows
-#ifndef ASA_NWG
-#define ASA_NWG 2
-#endif
-constexpr int NWG = ASA_NWG;               // epilogue warpgroups (each owns 128/NWG columns of a tile)
-constexpr int CPT = 4 / NWG;               // 32-column chunks per epilogue thread per tile
-constexpr int NEPI = 128 * NWG;            // epilogue threads
-constexpr int NTHREADS = 64 + NEPI;        // + producer warp + MMA warp
-constexpr int EPI0 = 64;                   // first epilogue thread
+constexpr int NEPI = 256;                  // threads that build a CTA's tile schedule (epi_bar counts them)
+constexpr int EPI0 = 64;                   // τ / mask: first epilogue thread (producer and MMA warps first)
 constexpr int K3_EPI0 = 96;                // forward: producer, S-issuer and P·V-issuer warps first
-constexpr int K3_THREADS = K3_EPI0 + NEPI;
 constexpr int DQ_NW = 4;                   // dQ: epilogue warpgroups (one 32-column chunk each)
 constexpr int DQ_NE = 128 * DQ_NW;
 constexpr int DQ_EPI0 = 96;                // dQ: producer, S/dP-issuer and dQ-issuer warps first
@@ -85,10 +78,9 @@ __device__ __forceinline__ void epi_bar() {
 
 __device__ __forceinline__ float neg_inf() { return __int_as_float(0xff800000); }
 
-// One arrival per epilogue warp (barriers are initialised with EPI_WARPS):
-// the warp's prior writes and tcgen05 fences are ordered before lane 0's
-// arrive by __syncwarp.
-constexpr int EPI_WARPS = NEPI / 32;
+// One arrival per epilogue warp (barriers are initialised with the epilogue
+// warp count): the warp's prior writes and tcgen05 fences are ordered before
+// lane 0's arrive by __syncwarp.
 __device__ __forceinline__ void epi_arrive(uint64_t* bar) {
     __syncwarp();
     if ((threadIdx.x & 31) == 0) sm100::mbar_arrive(bar);
@@ -525,7 +517,7 @@ k1_tau_solve(const float* __restrict__ topv, float* __restrict__ tau, size_t row
 // epilogue warpgroups split every tile by columns (warpgroup h owns keys
 // [128h/NW, 128(h+1)/NW)) and keep one partial top-k list per row; the lists
 // are merged pairwise under (score desc, key asc) -- the order sequential
-// insertion produces -- and warpgroup 0 solves τ.
+// insertion produces.
 //
 // Filter.  A score can only enter the row's final list if it is >= lim, the
 // largest of the partial lists' k-th values (each is a lower bound of the
@@ -539,39 +531,325 @@ k1_tau_solve(const float* __restrict__ topv, float* __restrict__ tau, size_t row
 // reference's strict '>' rule, so the lists are those full insertion gives.
 // On the first tile, before any list holds k scores, lim is seeded with the
 // smallest of KM group maxima of the chunk (KM distinct scores of this row).
+//
+// The phase is written as role functions over a shared-memory view so the
+// stand-alone mask kernel and the fused forward run the same code.
+constexpr int MASK_S = 3;    // K stages
+constexpr int MASK_NB = 4;   // S buffers in TMEM (128 columns each)
+
+struct MaskPhase {
+    uint8_t* sQ;
+    uint8_t* sK;              // MASK_S stages
+    float4* cbuf;             // [NE][CP][8] chunk copies
+    float* thr_s;             // [3][NW][128] published bounds
+    float* seed_s;            // [NW][128] seed bounds
+    uint64_t* q_full;
+    uint64_t* k_full;         // [MASK_S]
+    uint64_t* k_empty;        // [MASK_S]
+    uint64_t* s_full;         // [MASK_NB]
+    uint64_t* s_free;         // [MASK_NB]
+    uint64_t* fixed;          // K of a tile-load-zeroing tile fixed
+    uint64_t* drain;          // exit-time MMA drain (after a timed-out wait)
+    const int* qidx_blk;      // [128] positions of the block's queries
+    const uint32_t* sched;    // [T] visible key blocks
+    uint8_t* flags;           // [nKB] key blocks holding a row's top-k key
+    int T;
+};
+
+// Shared memory the phase needs beyond Q and the K stages.
+template <int D, int NW>
+constexpr size_t mask_extra_bytes() {
+    return (size_t)128 * NW * (4 / NW) * 8 * 16 + (size_t)3 * NW * TILE * 4 + (size_t)NW * TILE * 4;
+}
+
+template <int NB_>
+__device__ __forceinline__ void mask_init_barriers(const MaskPhase& m, int ne) {
+    mbar_init(m.q_full, 1);
+    for (int i = 0; i < MASK_S; ++i) { mbar_init(&m.k_full[i], 1); mbar_init(&m.k_empty[i], 1); }
+    for (int i = 0; i < NB_; ++i) { mbar_init(&m.s_full[i], 1); mbar_init(&m.s_free[i], ne / 32); }
+    mbar_init(m.fixed, 4);
+    mbar_init(m.drain, 1);
+}
+
+// Producer (one thread): the K tiles of the schedule through the ring.
+template <int D>
+__device__ void mask_produce(const MaskPhase& m, const CUtensorMap* tmK, const Shape& s, int bh, int* err) {
+    constexpr int TB = D * TILE * 2;
+    for (int j = 0; j < m.T; ++j) {
+        const int kb = (int)(m.sched[j] & SCHED_IDX);
+        const int st = j % MASK_S;
+        mbar_wait(&m.k_empty[st], ((j / MASK_S) & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+        mbar_expect_tx(&m.k_full[st], TB);
+        for (int bx = 0; bx < D / BOX; ++bx)
+            tma_load_3d(m.sK + st * TB + bx * BOX_BYTES, tmK, &m.k_full[st], bx * BOX, kb * TILE, bh);
+    }
+    if (error_set(err)) {   // a wait gave up: let this CTA's loads land
+        mbar_drain(m.q_full, 0);
+        drain_ring(m.k_full, MASK_S, m.T);
+    }
+}
+
+// MMA issuer (one warp): S = Q·K^T of every scheduled tile into the TMEM
+// buffers, MASK_NB in flight.
+template <int D>
+__device__ void mask_mma(const MaskPhase& m, const Shape& s, uint32_t tbase, int lane, int* err) {
+    constexpr int TB = D * TILE * 2;
+    constexpr uint32_t idesc = idesc_bf16(128, 128, 0, 0);
+    mbar_wait(m.q_full, 0, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);   // issued at set-up even when T = 0
+    int nfix = 0;
+    for (int j = 0; j < m.T; ++j) {
+        const uint32_t e = m.sched[j];
+        const int st = j % MASK_S, b = j % MASK_NB;
+        uint8_t* kt = m.sK + st * TB;
+        mbar_wait(&m.k_full[st], (j / MASK_S) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+        if (e & SCHED_FIX)     // four epilogue warps zero K of this tile
+            mbar_wait(m.fixed, (nfix++) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+        __syncwarp();
+        mbar_wait(&m.s_free[b], ((j / MASK_NB) & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+        tc_fence_after();
+        if (lane == 0) {
+#pragma unroll
+            for (int kk = 0; kk < D / 16; ++kk)
+                mma_bf16_ss(tbase + b * 128, kdesc(m.sQ, kk), kdesc(kt, kk), idesc, kk > 0);
+            mma_commit(&m.s_full[b]);
+            mma_commit(&m.k_empty[st]);
+        }
+        __syncwarp();
+    }
+    if (lane == 0 && error_set(err)) {   // a wait gave up: let this CTA's MMAs finish
+        mma_commit(m.drain);
+        mbar_drain(m.drain, 0);
+    }
+    __syncwarp();
+}
+
+// Epilogue thread et (row = TMEM lane, column slice h = et / 128): streams
+// the row's scores of every scheduled tile through its partial top-k list.
+template <int D, int KM, int NW>
+__device__ void mask_epilogue(const MaskPhase& m, const Shape& s, const int32_t* __restrict__ Kidx_bh,
+                              int qmin_blk, uint32_t tbase, int warp, int lane, int et, int qpos,
+                              TopK<KM>& tk, int* err) {
+    constexpr int NE = 128 * NW;
+    constexpr int CP = 4 / NW;                // 32-column chunks per thread per tile
+    constexpr int TB = D * TILE * 2;
+    constexpr int GSZ = TILE / KM;            // seed group size: KM groups per tile row
+    const int row = (warp & 3) * 32 + lane;
+    const int h = et / TILE;
+    const uint32_t tl = tmem_lane_base(tbase, warp);
+    const bool scale_pos = s.scale > 0.0f;
+    const float inv_scale = scale_pos ? 1.0f / s.scale : 0.0f;
+    float4* my = m.cbuf + et * CP * 8;
+    const int sw = lane & 7;                  // 16-byte slot swizzle: conflict-free chunk stores
+    // Published bounds of the row's k-th score (each list holds distinct
+    // scores): b0 = this list's k-th; b1 = its ceil(k/NW)-th (the minimum
+    // over the NW lists bounds k scores); b2 = its ceil(k/2)-th (the
+    // second largest over the lists bounds k scores).
+    const int first = KM - s.k;
+    const int i1 = first + (s.k + NW - 1) / NW - 1, i2 = first + (s.k + 1) / 2 - 1;
+    tk.init(s.k);
+    for (int j = 0; j < m.T; ++j) {
+        const uint32_t e = m.sched[j];
+        const int kb = (int)(e & SCHED_IDX);
+        const int b = j % MASK_NB;
+        const bool all = (e & SCHED_ALL) != 0;
+        if ((e & SCHED_FIX) && et < 4 * 32) {
+            // the reference's tile-load zeroing of K, 32 rows per warp
+            mbar_wait(&m.k_full[j % MASK_S], (j / MASK_S) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+            fix_tile<D, 1>(m.sK + (j % MASK_S) * TB, m.qidx_blk, qmin_blk, Kidx_bh, kb, s.NK, lane,
+                           32 * (et >> 5));
+            fence_async_smem();
+            epi_arrive(m.fixed);
+        }
+        float lim = tk.threshold();
+        {
+            float m1 = __uint_as_float(0x7f800000u), x2 = neg_inf(), y2 = neg_inf();
+#pragma unroll
+            for (int g = 0; g < NW; ++g) {
+                const volatile float* t = m.thr_s + g * TILE + row;
+                if (g != h) lim = fmaxf(lim, t[0]);
+                m1 = fminf(m1, t[NW * TILE]);
+                const float c2 = t[2 * NW * TILE];
+                y2 = fmaxf(y2, fminf(x2, c2));
+                x2 = fmaxf(x2, c2);
+            }
+            lim = fmaxf(lim, fmaxf(m1, NW > 2 ? y2 : neg_inf()));
+        }
+        mbar_wait(&m.s_full[b], (j / MASK_NB) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+        tc_fence_after();
+        uint32_t r2[CP][32];
+#pragma unroll
+        for (int cc = 0; cc < CP; ++cc) tmem_ld32(tl + b * 128 + (h * CP + cc) * 32, r2[cc]);
+        tmem_ld_wait();
+        tc_fence_before();
+        epi_arrive(&m.s_free[b]);          // S is in registers: release the buffer
+        uint32_t vis[CP];
+#pragma unroll
+        for (int cc = 0; cc < CP; ++cc) {
+            vis[cc] = 0xffffffffu;
+            if (!all) {
+                vis[cc] = vis_mask32(Kidx_bh, kb * TILE + (h * CP + cc) * 32, s.NK, s.causal, qpos);
+#pragma unroll
+                for (int i = 0; i < 32; ++i)
+                    if (!((vis[cc] >> i) & 1u)) r2[cc][i] = 0xff800000u;   // -inf: never a candidate
+            }
+        }
+        if (j == 0 && all && scale_pos) {
+            // Seed on a fully visible first tile: the KM groups of GSZ
+            // consecutive scores of the row's 128 have KM distinct
+            // maxima, so the smallest bounds the row's k-th score.
+            float t0 = __uint_as_float(0x7f800000u);
+#pragma unroll
+            for (int g = 0; g < CP * 32 / GSZ; ++g) {
+                float mx = __uint_as_float(r2[(g * GSZ) / 32][(g * GSZ) % 32]);
+#pragma unroll
+                for (int i = 1; i < GSZ; ++i)
+                    mx = fmaxf(mx, __uint_as_float(r2[(g * GSZ + i) / 32][(g * GSZ + i) % 32]));
+                t0 = fminf(t0, mx);
+            }
+            m.seed_s[h * TILE + row] = t0;
+            asm volatile("bar.sync 2, %0;" ::"n"(NE) : "memory");   // uniform: same schedule everywhere
+#pragma unroll
+            for (int g = 0; g < NW; ++g) t0 = fminf(t0, m.seed_s[g * TILE + row]);
+            lim = fmaxf(lim, clamp_score(t0, s.scale));
+        }
+#pragma unroll
+        for (int cc = 0; cc < CP; ++cc) {
+            const int kn0 = kb * TILE + (h * CP + cc) * 32;
+            const uint32_t (&r)[32] = r2[cc];
+            // candidate mask: bit i set when score i may reach lim
+            uint32_t cand;
+            if (scale_pos && lim > -10.0f) {
+                const float rlo = (lim - fmaf(fabsf(lim), 0x1p-20f, 0x1p-100f)) * inv_scale;
+                const float2 lo2 = make_float2(rlo, rlo), m1 = make_float2(-1.0f, -1.0f);
+                uint32_t c4[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+                for (int i = 3; i >= 0; --i) {
+#pragma unroll
+                    for (int q4 = 0; q4 < 4; ++q4) {
+                        const int i0 = q4 * 8 + 2 * i;
+                        const float2 dlt = __ffma2_rn(make_float2(__uint_as_float(r[i0]),
+                                                                  __uint_as_float(r[i0 + 1])), m1, lo2);
+                        c4[q4] = __funnelshift_l(__float_as_uint(dlt.y), c4[q4], 1);
+                        c4[q4] = __funnelshift_l(__float_as_uint(dlt.x), c4[q4], 1);
+                    }
+                }
+                cand = (c4[0] | (c4[1] << 8) | (c4[2] << 16) | (c4[3] << 24)) & vis[cc];
+            } else {
+                cand = vis[cc];               // no bound above the clamp floor yet: every score
+            }
+            if (cand) {
+#pragma unroll
+                for (int q8 = 0; q8 < 8; ++q8)
+                    my[cc * 8 + (q8 ^ sw)] = make_float4(__uint_as_float(r[4 * q8]), __uint_as_float(r[4 * q8 + 1]),
+                                                         __uint_as_float(r[4 * q8 + 2]), __uint_as_float(r[4 * q8 + 3]));
+            }
+            const float* myf = reinterpret_cast<const float*>(my + cc * 8);
+            while (cand) {
+                const int i = __ffs(cand) - 1;
+                cand &= cand - 1;
+                const float v = clamp_score(myf[(((i >> 2) ^ sw) << 2) | (i & 3)], s.scale);
+                if (v > tk.threshold()) tk.insert(v, kn0 + i);   // keys ascend per thread
+            }
+        }
+        {
+            float v1 = tk.v[KM - 1], v2 = tk.v[KM - 1];
+#pragma unroll
+            for (int i = 0; i < KM; ++i) {
+                if (i == i1) v1 = tk.v[i];
+                if (i == i2) v2 = tk.v[i];
+            }
+            volatile float* t = m.thr_s + h * TILE + row;
+            t[0] = tk.threshold();
+            t[NW * TILE] = v1;
+            t[2 * NW * TILE] = v2;
+        }
+    }
+}
+
+// Merge: one thread per row walks the NW sorted lists (64-bit keys ordered
+// like (score desc, key index asc); identical keys -- the -1e6 seeds -- go
+// by list number) and emits the row's top-k in order: into topv / topi when
+// given, and into mv[KM] in TopK slot layout (live slots [KM-k, KM), +inf
+// before them) for a τ solve in the caller.  Marks the key blocks of the
+// emitted keys in m.flags.  Run by all NE epilogue threads; `lists` is NW*KM*128
+// 8-byte entries of shared memory no longer read by anyone.
+template <int KM, int NW>
+__device__ void mask_merge(const MaskPhase& m, const Shape& s, const TopK<KM>& tk, unsigned long long* lists,
+                           int row, int h, bool qv, size_t qrow, float* __restrict__ topv,
+                           int32_t* __restrict__ topi, float (&mv)[KM]) {
+    constexpr int NE = 128 * NW;
+    const int first = KM - s.k;
+    asm volatile("bar.sync 2, %0;" ::"n"(NE) : "memory");   // K stages no longer read
+#pragma unroll
+    for (int i = 0; i < KM; ++i) lists[(h * KM + i) * TILE + row] = order_key(tk.v[i], tk.i[i]);
+    asm volatile("bar.sync 2, %0;" ::"n"(NE) : "memory");
+#pragma unroll
+    for (int i = 0; i < KM; ++i) mv[i] = __int_as_float(0x7f800000);
+    if (h == 0 && qv) {
+        int pos[NW];
+        unsigned long long cur[NW];
+#pragma unroll
+        for (int g = 0; g < NW; ++g) {
+            pos[g] = first;
+            cur[g] = lists[(g * KM + first) * TILE + row];
+        }
+        for (int rk = 0; rk < s.k; ++rk) {
+            int bg = 0;
+            unsigned long long best = cur[0];
+#pragma unroll
+            for (int g = 1; g < NW; ++g)
+                if (cur[g] > best) { best = cur[g]; bg = g; }
+            const float v = order_value(best);
+            const int key = order_index(best);
+            if (topv) topv[qrow * s.k + rk] = v;
+            if (topi) topi[qrow * s.k + rk] = key;
+#pragma unroll
+            for (int i = 0; i < KM; ++i)
+                if (i == first + rk) mv[i] = v;
+            if (key >= 0) m.flags[key / TILE] = 1;
+#pragma unroll
+            for (int g = 0; g < NW; ++g)
+                if (g == bg) {
+                    ++pos[g];
+                    cur[g] = pos[g] < KM ? lists[(g * KM + pos[g]) * TILE + row] : 0ull;
+                }
+        }
+    }
+    asm volatile("bar.sync 2, %0;" ::"n"(NE) : "memory");
+}
+
+// Stand-alone τ / mask kernel: the phase, its merge, and the mask row; τ is
+// solved from the written top-k by k1_tau_solve.
 template <int D, int KM, int NW>
 __global__ void __launch_bounds__(64 + 128 * NW, 1)
 k1_tau_mask(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK, Shape s,
             const int32_t* __restrict__ Qidx, const int32_t* __restrict__ Kidx, Bounds bd,
             float* __restrict__ topv, int32_t* __restrict__ topi, uint8_t* __restrict__ M, int* err) {
     constexpr int NE = 128 * NW;              // epilogue threads
-    constexpr int CP = 4 / NW;                // 32-column chunks per thread per tile
-    constexpr int S = 3;                      // K stages
-    constexpr int NB = 4;                     // S buffers in TMEM (128 columns each)
     constexpr int TB = D * TILE * 2;
-    constexpr int GSZ = TILE / KM;            // seed group size: KM groups per tile row
     extern __shared__ uint8_t smem_raw[];
     uint8_t* base = align1024(smem_raw, err);
-    uint8_t* sQ = base;
-    uint8_t* sK = base + TB;
-    float4* cbuf = reinterpret_cast<float4*>(sK + S * TB);              // [NE][CP][8] chunk copies
-    float* thr_s = reinterpret_cast<float*>(cbuf + NE * CP * 8);        // [3][NW][128] published bounds
-    float* seed_s = thr_s + 3 * NW * TILE;                              // [NW][128] seed bounds
-    uint64_t* bars = reinterpret_cast<uint64_t*>(seed_s + NW * TILE);
-    uint64_t* q_full = bars;
-    uint64_t* k_full = bars + 1;
-    uint64_t* k_empty = bars + 1 + S;
-    uint64_t* s_full = bars + 1 + 2 * S;      // [NB]
-    uint64_t* s_free = s_full + NB;           // [NB]
-    uint64_t* fixed = s_free + NB;            // K of a tile-load-zeroing tile fixed
-    uint64_t* drain = fixed + 1;              // exit-time MMA drain (after a timed-out wait)
+    MaskPhase m;
+    m.sQ = base;
+    m.sK = base + TB;
+    m.cbuf = reinterpret_cast<float4*>(m.sK + MASK_S * TB);
+    m.thr_s = reinterpret_cast<float*>(m.cbuf + NE * (4 / NW) * 8);
+    m.seed_s = m.thr_s + 3 * NW * TILE;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(m.seed_s + NW * TILE);
+    m.q_full = bars;
+    m.k_full = bars + 1;
+    m.k_empty = bars + 1 + MASK_S;
+    m.s_full = bars + 1 + 2 * MASK_S;
+    m.s_free = m.s_full + MASK_NB;
+    m.fixed = m.s_free + MASK_NB;
+    m.drain = m.fixed + 1;
     uint32_t* holder = reinterpret_cast<uint32_t*>(bars + 24);
     int* qidx_blk = reinterpret_cast<int*>(holder + 4);      // [128]
-    int* misc = qidx_blk + TILE;                             // [8] warp counts, tile count, fix run
+    int* misc = qidx_blk + TILE;                             // [8] warp counts, tile count
     uint32_t* sched = reinterpret_cast<uint32_t*>(misc + 16);   // [nKB]
-    uint8_t* flags = reinterpret_cast<uint8_t*>(sched + s.nKB);
-    // merge staging (after the tile loop, over the K stages): [NW][KM][128] ordered keys
-    unsigned long long* lists = reinterpret_cast<unsigned long long*>(sK);
+    m.flags = reinterpret_cast<uint8_t*>(sched + s.nKB);
+    m.qidx_blk = qidx_blk;
+    m.sched = sched;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int bh = blockIdx.y;
@@ -579,18 +857,14 @@ k1_tau_mask(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
     const int32_t* Kidx_bh = Kidx + (size_t)bh * s.NK;
 
     if (threadIdx.x == 0) {
-        mbar_init(q_full, 1);
-        for (int i = 0; i < S; ++i) { mbar_init(&k_full[i], 1); mbar_init(&k_empty[i], 1); }
-        for (int i = 0; i < NB; ++i) { mbar_init(&s_full[i], 1); mbar_init(&s_free[i], NE / 32); }
-        mbar_init(fixed, 4);
-        mbar_init(drain, 1);
+        mask_init_barriers<MASK_NB>(m, NE);
         fence_barrier_init();
         // Q does not depend on the schedule built below: issue it now
         tma_prefetch_desc(&tmQ);
         tma_prefetch_desc(&tmK);
-        mbar_expect_tx(q_full, TB);
+        mbar_expect_tx(m.q_full, TB);
         for (int bx = 0; bx < D / BOX; ++bx)
-            tma_load_3d(sQ + bx * BOX_BYTES, &tmQ, q_full, bx * BOX, qb * TILE, bh);
+            tma_load_3d(m.sQ + bx * BOX_BYTES, &tmQ, m.q_full, bx * BOX, qb * TILE, bh);
     }
     if (warp == 1) { tmem_alloc(holder, 512); tmem_relinquish(); }
     if (threadIdx.x >= EPI0) {
@@ -599,8 +873,8 @@ k1_tau_mask(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
             const int q = qb * TILE + r;
             qidx_blk[r] = (q < s.NQ && s.causal) ? Qidx[(size_t)bh * s.NQ + q] : INT_MAX;
         }
-        for (int i = r; i < 3 * NW * TILE; i += NE) thr_s[i] = ASA_SENTINEL;
-        for (int i = r; i < s.nKB; i += NE) flags[i] = 0;
+        for (int i = r; i < 3 * NW * TILE; i += NE) m.thr_s[i] = ASA_SENTINEL;
+        for (int i = r; i < s.nKB; i += NE) m.flags[i] = 0;
         if (r < NEPI) {                       // the schedule builders' barrier counts NEPI threads
             const int n = sched_visible(sched, misc, s, bd, bh, qb, r);
             if (r == 0) misc[8] = n;
@@ -611,225 +885,25 @@ k1_tau_mask(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
     tc_fence_after();
     const uint32_t tbase = *holder;
     const int qmin_blk = s.causal ? bd.qmin[bh * s.nQB + qb] : INT_MIN;
-    const int T = misc[8];
+    m.T = misc[8];
 
     if (warp == 0) {
-        if (lane == 0 && T > 0) {
-            for (int j = 0; j < T; ++j) {
-                const int kb = (int)(sched[j] & SCHED_IDX);
-                const int st = j % S;
-                mbar_wait(&k_empty[st], ((j / S) & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
-                mbar_expect_tx(&k_full[st], TB);
-                for (int bx = 0; bx < D / BOX; ++bx)
-                    tma_load_3d(sK + st * TB + bx * BOX_BYTES, &tmK, &k_full[st], bx * BOX, kb * TILE, bh);
-            }
-        }
-        if (lane == 0 && error_set(err)) {   // a wait gave up: let this CTA's loads land
-            mbar_drain(q_full, 0);
-            drain_ring(k_full, S, T);
-        }
+        if (lane == 0) mask_produce<D>(m, &tmK, s, bh, err);
     } else if (warp == 1) {
-        constexpr uint32_t idesc = idesc_bf16(128, 128, 0, 0);
-        mbar_wait(q_full, 0, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);   // issued at set-up even when T = 0
-        int nfix = 0;
-        for (int j = 0; j < T; ++j) {
-            const uint32_t e = sched[j];
-            const int st = j % S, b = j % NB;
-            uint8_t* kt = sK + st * TB;
-            mbar_wait(&k_full[st], (j / S) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
-            if (e & SCHED_FIX)     // four epilogue warps zero K of this tile
-                mbar_wait(fixed, (nfix++) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
-            __syncwarp();
-            mbar_wait(&s_free[b], ((j / NB) & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
-            tc_fence_after();
-            if (lane == 0) {
-#pragma unroll
-                for (int kk = 0; kk < D / 16; ++kk)
-                    mma_bf16_ss(tbase + b * 128, kdesc(sQ, kk), kdesc(kt, kk), idesc, kk > 0);
-                mma_commit(&s_full[b]);
-                mma_commit(&k_empty[st]);
-            }
-            __syncwarp();
-        }
-        if (lane == 0 && error_set(err)) {   // a wait gave up: let this CTA's MMAs finish
-            mma_commit(drain);
-            mbar_drain(drain, 0);
-        }
-        __syncwarp();
+        mask_mma<D>(m, s, tbase, lane, err);
     } else {
         const int row = (warp & 3) * 32 + lane;
         const int et = threadIdx.x - EPI0;
-        const int h = et / TILE;                  // column slice of each tile
         const int q = qb * TILE + row;
         const bool qv = q < s.NQ;
         const int qpos = !qv ? INT_MIN : (s.causal ? Qidx[(size_t)bh * s.NQ + q] : INT_MAX);
-        const uint32_t tl = tmem_lane_base(tbase, warp);
-        const bool scale_pos = s.scale > 0.0f;
-        const float inv_scale = scale_pos ? 1.0f / s.scale : 0.0f;
-        float4* my = cbuf + et * CP * 8;
-        const int sw = lane & 7;                  // 16-byte slot swizzle: conflict-free chunk stores
-        // Published bounds of the row's k-th score (each list holds distinct
-        // scores): b0 = this list's k-th; b1 = its ceil(k/NW)-th (the minimum
-        // over the NW lists bounds k scores); b2 = its ceil(k/2)-th (the
-        // second largest over the lists bounds k scores).
-        const int first = KM - s.k;
-        const int i1 = first + (s.k + NW - 1) / NW - 1, i2 = first + (s.k + 1) / 2 - 1;
         TopK<KM> tk;
-        tk.init(s.k);
-        for (int j = 0; j < T; ++j) {
-            const uint32_t e = sched[j];
-            const int kb = (int)(e & SCHED_IDX);
-            const int b = j % NB;
-            const bool all = (e & SCHED_ALL) != 0;
-            if ((e & SCHED_FIX) && et < 4 * 32) {
-                // the reference's tile-load zeroing of K, 32 rows per warp
-                mbar_wait(&k_full[j % S], (j / S) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
-                fix_tile<D, 1>(sK + (j % S) * TB, qidx_blk, qmin_blk, Kidx_bh, kb, s.NK, lane, 32 * (et >> 5));
-                fence_async_smem();
-                epi_arrive(fixed);
-            }
-            float lim = tk.threshold();
-            {
-                float m1 = __uint_as_float(0x7f800000u), x2 = neg_inf(), y2 = neg_inf();
-#pragma unroll
-                for (int g = 0; g < NW; ++g) {
-                    const volatile float* t = thr_s + g * TILE + row;
-                    if (g != h) lim = fmaxf(lim, t[0]);
-                    m1 = fminf(m1, t[NW * TILE]);
-                    const float c2 = t[2 * NW * TILE];
-                    y2 = fmaxf(y2, fminf(x2, c2));
-                    x2 = fmaxf(x2, c2);
-                }
-                lim = fmaxf(lim, fmaxf(m1, NW > 2 ? y2 : neg_inf()));
-            }
-            mbar_wait(&s_full[b], (j / NB) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
-            tc_fence_after();
-            uint32_t r2[CP][32];
-#pragma unroll
-            for (int cc = 0; cc < CP; ++cc) tmem_ld32(tl + b * 128 + (h * CP + cc) * 32, r2[cc]);
-            tmem_ld_wait();
-            tc_fence_before();
-            epi_arrive(&s_free[b]);          // S is in registers: release the buffer
-            uint32_t vis[CP];
-#pragma unroll
-            for (int cc = 0; cc < CP; ++cc) {
-                vis[cc] = 0xffffffffu;
-                if (!all) {
-                    vis[cc] = vis_mask32(Kidx_bh, kb * TILE + (h * CP + cc) * 32, s.NK, s.causal, qpos);
-#pragma unroll
-                    for (int i = 0; i < 32; ++i)
-                        if (!((vis[cc] >> i) & 1u)) r2[cc][i] = 0xff800000u;   // -inf: never a candidate
-                }
-            }
-            if (j == 0 && all && scale_pos) {
-                // Seed on a fully visible first tile: the KM groups of GSZ
-                // consecutive scores of the row's 128 have KM distinct
-                // maxima, so the smallest bounds the row's k-th score.
-                float t0 = __uint_as_float(0x7f800000u);
-#pragma unroll
-                for (int g = 0; g < CP * 32 / GSZ; ++g) {
-                    float m = __uint_as_float(r2[(g * GSZ) / 32][(g * GSZ) % 32]);
-#pragma unroll
-                    for (int i = 1; i < GSZ; ++i)
-                        m = fmaxf(m, __uint_as_float(r2[(g * GSZ + i) / 32][(g * GSZ + i) % 32]));
-                    t0 = fminf(t0, m);
-                }
-                seed_s[h * TILE + row] = t0;
-                asm volatile("bar.sync 2, %0;" ::"n"(NE) : "memory");   // uniform: same schedule everywhere
-#pragma unroll
-                for (int g = 0; g < NW; ++g) t0 = fminf(t0, seed_s[g * TILE + row]);
-                lim = fmaxf(lim, clamp_score(t0, s.scale));
-            }
-#pragma unroll
-            for (int cc = 0; cc < CP; ++cc) {
-                const int kn0 = kb * TILE + (h * CP + cc) * 32;
-                const uint32_t (&r)[32] = r2[cc];
-                // candidate mask: bit i set when score i may reach lim
-                uint32_t cand;
-                if (scale_pos && lim > -10.0f) {
-                    const float rlo = (lim - fmaf(fabsf(lim), 0x1p-20f, 0x1p-100f)) * inv_scale;
-                    const float2 lo2 = make_float2(rlo, rlo), m1 = make_float2(-1.0f, -1.0f);
-                    uint32_t c4[4] = {0u, 0u, 0u, 0u};
-#pragma unroll
-                    for (int i = 3; i >= 0; --i) {
-#pragma unroll
-                        for (int q4 = 0; q4 < 4; ++q4) {
-                            const int i0 = q4 * 8 + 2 * i;
-                            const float2 dlt = __ffma2_rn(make_float2(__uint_as_float(r[i0]),
-                                                                      __uint_as_float(r[i0 + 1])), m1, lo2);
-                            c4[q4] = __funnelshift_l(__float_as_uint(dlt.y), c4[q4], 1);
-                            c4[q4] = __funnelshift_l(__float_as_uint(dlt.x), c4[q4], 1);
-                        }
-                    }
-                    cand = (c4[0] | (c4[1] << 8) | (c4[2] << 16) | (c4[3] << 24)) & vis[cc];
-                } else {
-                    cand = vis[cc];               // no bound above the clamp floor yet: every score
-                }
-                if (cand) {
-#pragma unroll
-                    for (int m = 0; m < 8; ++m)
-                        my[cc * 8 + (m ^ sw)] = make_float4(__uint_as_float(r[4 * m]), __uint_as_float(r[4 * m + 1]),
-                                                            __uint_as_float(r[4 * m + 2]), __uint_as_float(r[4 * m + 3]));
-                }
-                const float* myf = reinterpret_cast<const float*>(my + cc * 8);
-                while (cand) {
-                    const int i = __ffs(cand) - 1;
-                    cand &= cand - 1;
-                    const float v = clamp_score(myf[(((i >> 2) ^ sw) << 2) | (i & 3)], s.scale);
-                    if (v > tk.threshold()) tk.insert(v, kn0 + i);   // keys ascend per thread
-                }
-            }
-            {
-                float v1 = tk.v[KM - 1], v2 = tk.v[KM - 1];
-#pragma unroll
-                for (int i = 0; i < KM; ++i) {
-                    if (i == i1) v1 = tk.v[i];
-                    if (i == i2) v2 = tk.v[i];
-                }
-                volatile float* t = thr_s + h * TILE + row;
-                t[0] = tk.threshold();
-                t[NW * TILE] = v1;
-                t[2 * NW * TILE] = v2;
-            }
-        }
-        // Merge: one thread per row walks the NW sorted lists (64-bit keys
-        // ordered like (score desc, key index asc); identical keys -- the
-        // -1e6 seeds -- go by list number) and emits the row's top-k in
-        // order; τ is solved from them by k1_tau_solve.
-        asm volatile("bar.sync 2, %0;" ::"n"(NE) : "memory");   // K stages no longer read
-#pragma unroll
-        for (int i = 0; i < KM; ++i) lists[(h * KM + i) * TILE + row] = order_key(tk.v[i], tk.i[i]);
-        asm volatile("bar.sync 2, %0;" ::"n"(NE) : "memory");
-        if (h == 0 && qv) {
-            int pos[NW];
-            unsigned long long cur[NW];
-#pragma unroll
-            for (int g = 0; g < NW; ++g) {
-                pos[g] = first;
-                cur[g] = lists[(g * KM + first) * TILE + row];
-            }
-            float* out = topv + ((size_t)bh * s.NQ + q) * s.k;
-            for (int rk = 0; rk < s.k; ++rk) {
-                int bg = 0;
-                unsigned long long best = cur[0];
-#pragma unroll
-                for (int g = 1; g < NW; ++g)
-                    if (cur[g] > best) { best = cur[g]; bg = g; }
-                out[rk] = order_value(best);
-                const int key = order_index(best);
-                if (topi) topi[((size_t)bh * s.NQ + q) * s.k + rk] = key;
-                if (key >= 0) flags[key / TILE] = 1;
-#pragma unroll
-                for (int g = 0; g < NW; ++g)
-                    if (g == bg) {
-                        ++pos[g];
-                        cur[g] = pos[g] < KM ? lists[(g * KM + pos[g]) * TILE + row] : 0ull;
-                    }
-            }
-        }
-        asm volatile("bar.sync 2, %0;" ::"n"(NE) : "memory");
+        mask_epilogue<D, KM, NW>(m, s, Kidx_bh, qmin_blk, tbase, warp, lane, et, qpos, tk, err);
+        float mv[KM];
+        mask_merge<KM, NW>(m, s, tk, reinterpret_cast<unsigned long long*>(m.sK), row, et / TILE, qv,
+                           (size_t)bh * s.NQ + (qv ? q : 0), topv, topi, mv);
         uint8_t* Mrow = M + ((size_t)bh * s.nQB + qb) * s.nKB;
-        for (int i = et; i < s.nKB; i += NE) Mrow[i] = flags[i];
+        for (int i = et; i < s.nKB; i += NE) Mrow[i] = m.flags[i];
     }
     tc_fence_before();
     __syncthreads();
@@ -1104,39 +1178,367 @@ __device__ __forceinline__ void store_out32(TO* dst_row, int c, const float (&o)
 // writes P back over its own S columns as bf16 hi/lo pairs (each 16-key
 // group: 8 hi columns then 8 lo columns), which the tensor cores read as the
 // A operand of O += P·V; a buffer is reused once that P·V completes.  The MMA
-// warp issues S two tiles ahead of the P·V it waits for.
-template <int D, typename TO, int PINV>
-__global__ void __launch_bounds__(K3_THREADS, 1)
+// warp issues S two tiles ahead of the P·V it waits for.  NW epilogue
+// warpgroups split each tile by columns (128/NW per thread).
+//
+// Written as role functions over a shared-memory view, shared by the
+// stand-alone forward and the fused τ/mask + forward kernel.
+constexpr int FWD_S = 3;     // K stages
+constexpr int FWD_SV = 2;    // V stages
+constexpr int FWD_NB = 3;    // S / P buffers in TMEM
+constexpr uint32_t FWD_TO = 384;   // TMEM column of O
+
+struct FwdPhase {
+    uint8_t* sQ;
+    uint8_t* sK;              // FWD_S stages
+    uint8_t* sV;              // FWD_SV stages
+    uint64_t* k_full;
+    uint64_t* k_empty;
+    uint64_t* v_full;
+    uint64_t* v_empty;
+    uint64_t* s_full;         // [FWD_NB]
+    uint64_t* s_free;         // [FWD_NB]
+    uint64_t* p_full;         // [FWD_NB]
+    uint64_t* o_full;
+    uint64_t* fixed;          // K/V of a tile-load-zeroing tile fixed
+    uint64_t* drain;          // [2] exit-time MMA drains (after a timed-out wait)
+    float* nsum;              // [NW][128] partial row sums
+    const int* qidx_blk;
+    const uint32_t* sched;    // [T] active key blocks
+    int T;
+};
+constexpr int FWD_BARS = 2 * FWD_S + 2 * FWD_SV + 3 * FWD_NB + 4;
+
+// Barriers start at `bars` (FWD_BARS of them); epilogue warps ew arrive.
+__device__ __forceinline__ void fwd_init_barriers(FwdPhase& f, uint64_t* bars, int ew) {
+    f.k_full = bars;
+    f.k_empty = f.k_full + FWD_S;
+    f.v_full = f.k_empty + FWD_S;
+    f.v_empty = f.v_full + FWD_SV;
+    f.s_full = f.v_empty + FWD_SV;
+    f.s_free = f.s_full + FWD_NB;
+    f.p_full = f.s_free + FWD_NB;
+    f.o_full = f.p_full + FWD_NB;
+    f.fixed = f.o_full + 1;
+    f.drain = f.fixed + 1;
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < FWD_S; ++i) { mbar_init(&f.k_full[i], 1); mbar_init(&f.k_empty[i], 1); }
+        for (int i = 0; i < FWD_SV; ++i) { mbar_init(&f.v_full[i], 1); mbar_init(&f.v_empty[i], 1); }
+        for (int i = 0; i < FWD_NB; ++i) {
+            mbar_init(&f.s_full[i], 1); mbar_init(&f.s_free[i], 1); mbar_init(&f.p_full[i], ew);
+        }
+        mbar_init(f.o_full, 1);
+        mbar_init(f.fixed, ew);
+        mbar_init(&f.drain[0], 1);
+        mbar_init(&f.drain[1], 1);
+    }
+}
+
+// Producers: lane 0 the K ring, lane 1 the V ring (V's ring, freed after
+// P·V, must not hold back K's, freed after S), from tile j0 on (tiles before
+// it were issued at set-up).
+template <int D>
+__device__ void fwd_produce(const FwdPhase& f, const CUtensorMap* tmK, const CUtensorMap* tmV, const Shape& s,
+                            int bh, int lane, int j0, const uint64_t* q_full, int* err) {
+    constexpr int TB = D * TILE * 2;
+    if (lane == 0) {
+        for (int j = j0; j < f.T; ++j) {
+            const int kb = (int)(f.sched[j] & SCHED_IDX);
+            const int st = j % FWD_S;
+            mbar_wait(&f.k_empty[st], ((j / FWD_S) & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+            mbar_expect_tx(&f.k_full[st], TB);
+            for (int bx = 0; bx < D / BOX; ++bx)
+                tma_load_3d(f.sK + st * TB + bx * BOX_BYTES, tmK, &f.k_full[st], bx * BOX, kb * TILE, bh);
+        }
+    } else if (lane == 1) {
+        for (int j = j0; j < f.T; ++j) {
+            const int kb = (int)(f.sched[j] & SCHED_IDX);
+            const int sv = j % FWD_SV;
+            mbar_wait(&f.v_empty[sv], ((j / FWD_SV) & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+            mbar_expect_tx(&f.v_full[sv], TB);
+            for (int bx = 0; bx < D / BOX; ++bx)
+                tma_load_3d(f.sV + sv * TB + bx * BOX_BYTES, tmV, &f.v_full[sv], bx * BOX, kb * TILE, bh);
+        }
+    }
+    __syncwarp();
+    if (lane == 0 && f.T > 0 && error_set(err)) {   // a wait gave up: let this CTA's loads land
+        if (q_full) mbar_drain(const_cast<uint64_t*>(q_full), 0);
+        drain_ring(f.k_full, FWD_S, f.T);
+        drain_ring(f.v_full, FWD_SV, f.T);
+    }
+}
+
+// S = Q·K^T issuer.  tcgen05.mma issue blocks at the tensor pipe's rate, so
+// S and P·V come from two warps: while one waits for its inputs the other
+// keeps the pipe fed.  S(n) needs its K tile and TMEM buffer n % NB, which
+// P·V(n - NB) frees.  q_full: the Q barrier to wait on first, or null when
+// Q is known to be resident.
+template <int D>
+__device__ void fwd_mma_s(const FwdPhase& f, const Shape& s, uint32_t tbase, int lane, uint64_t* q_full,
+                          int* err) {
+    constexpr int TB = D * TILE * 2;
+    constexpr uint32_t idS = idesc_bf16(128, 128, 0, 0);
+    if (f.T > 0 && q_full) mbar_wait(q_full, 0, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+    const uint64_t dQ = kdesc(f.sQ, 0);
+    int nfix = 0;
+    for (int n = 0; n < f.T; ++n) {
+        const uint32_t e = f.sched[n];
+        const int st = n % FWD_S, b = n % FWD_NB;
+        uint8_t* kt = f.sK + st * TB;
+        mbar_wait(&f.k_full[st], (n / FWD_S) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+        if (e & SCHED_FIX)     // the epilogue warps zero K and V of this tile
+            mbar_wait(f.fixed, (nfix++) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+        __syncwarp();
+        mbar_wait(&f.s_free[b], ((n / FWD_NB) & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+        tc_fence_after();
+        if (lane == 0) {
+            const uint64_t dK = kdesc(kt, 0);
+#pragma unroll
+            for (int kk = 0; kk < D / 16; ++kk)
+                mma_bf16_ss(tbase + b * 128, kdesc_step(dQ, kk), kdesc_step(dK, kk), idS, kk > 0);
+            mma_commit(&f.s_full[b]);
+            mma_commit(&f.k_empty[st]);
+        }
+        __syncwarp();
+    }
+    if (lane == 0 && error_set(err)) {   // a wait gave up: let this warp's MMAs finish
+        mma_commit(&f.drain[0]);
+        mbar_drain(&f.drain[0], 0);
+    }
+    __syncwarp();
+}
+
+// O += P·V issuer: P·V(m) needs its V tile and the epilogue's P.  P·V(m)
+// needs no wait on `fixed`: p_full(m) completes only after every epilogue
+// warp's arrival, and the warps that zero V of a tile-load-zeroing tile
+// arrive after that zeroing and its proxy fence.
+template <int D>
+__device__ void fwd_mma_pv(const FwdPhase& f, const Shape& s, uint32_t tbase, int lane, int split, int* err) {
+    constexpr int TB = D * TILE * 2;
+    constexpr uint32_t idPV = idesc_bf16(128, D, 0, 1);
+    for (int m = 0; m < f.T; ++m) {
+        const int b = m % FWD_NB, sv = m % FWD_SV;
+        uint8_t* vt = f.sV + sv * TB;
+        mbar_wait(&f.v_full[sv], (m / FWD_SV) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+        __syncwarp();
+        mbar_wait(&f.p_full[b], (m / FWD_NB) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+        tc_fence_after();
+        if (lane == 0) {
+            const uint32_t pb = tbase + b * 128;
+            const uint64_t dV = mndesc(vt, 0);
+#pragma unroll
+            for (int kk = 0; kk < TILE / 16; ++kk)
+                mma_bf16_ts(tbase + FWD_TO, pb + kk * 16, mndesc_step(dV, kk), idPV, (m > 0 || kk > 0));
+            if (split) {
+#pragma unroll
+                for (int kk = 0; kk < TILE / 16; ++kk)
+                    mma_bf16_ts(tbase + FWD_TO, pb + kk * 16 + 8, mndesc_step(dV, kk), idPV, 1);
+            }
+            mma_commit(&f.s_free[b]);
+            mma_commit(&f.v_empty[sv]);
+        }
+        __syncwarp();
+    }
+    if (lane == 0) mma_commit(f.o_full);
+    if (lane == 0 && error_set(err)) {   // a wait gave up: let this warp's MMAs finish
+        mma_commit(&f.drain[1]);
+        mbar_drain(&f.drain[1], 0);
+    }
+    __syncwarp();
+}
+
+// Epilogue thread et (row = TMEM lane, column slice h = et / 128): entmax
+// weights of every scheduled tile written back to TMEM as P, the row sum,
+// then O / (n + EPS) stored (fp32 copy O32 and/or O in TO).  tq: the row's τ.
+template <int D, typename TO, int PINV, int NW>
+__device__ void fwd_epilogue(const FwdPhase& f, const Shape& s, const int32_t* __restrict__ Kidx_bh,
+                             int qmin_blk, uint32_t tbase, int warp, int lane, int et, int bh, int qb,
+                             int qpos, float tq, TO* __restrict__ O, float* __restrict__ O32,
+                             float* __restrict__ rownorm, int split, int* err) {
+    constexpr int NE = 128 * NW;
+    constexpr int CP = 4 / NW;                // 32-column chunks per thread per tile
+    constexpr int TB = D * TILE * 2;
+    const int row = (warp & 3) * 32 + lane;
+    const int h = et / TILE;
+    const int q = qb * TILE + row;
+    const bool qv = q < s.NQ;
+    const size_t qrow = (size_t)bh * s.NQ + (qv ? q : 0);
+    const uint32_t tl = tmem_lane_base(tbase, warp);
+    float n = 0.0f;
+    constexpr bool kPacked = PINV == 1 || PINV == 2 || PINV == 4;
+    const float2 c1 = make_float2(__fmul_rn(s.am1, s.scale), __fmul_rn(s.am1, s.scale));
+    const float2 mtau = make_float2(-tq, -tq);
+    const float uhi = __fmaf_rn(s.am1, 10.0f, -tq);
+    // warp-uniform: the packed path issues warp-collective TMEM loads/stores
+    const bool packed_row = __all_sync(0xffffffffu, kPacked && split && __fmaf_rn(s.am1, -10.0f, -tq) <= 0.0f);
+    float2 n2 = make_float2(0.0f, 0.0f);
+    for (int j = 0; j < f.T; ++j) {
+        const uint32_t e = f.sched[j];
+        const int kb = (int)(e & SCHED_IDX);
+        const bool all = (e & SCHED_ALL) != 0;
+        const int b = j % FWD_NB;
+        if (e & SCHED_FIX) {
+            // The reference's tile-load zeroing of this tile's K and V, by
+            // eight epilogue warps (32 rows each of K or V) instead of one
+            // control warp: S and P·V wait for it.
+            const int ew = et >> 5;
+            if (ew < 8) {
+                uint8_t* tile;
+                if (ew < 4) {
+                    mbar_wait(&f.k_full[j % FWD_S], (j / FWD_S) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+                    tile = f.sK + (j % FWD_S) * TB;
+                } else {
+                    mbar_wait(&f.v_full[j % FWD_SV], (j / FWD_SV) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+                    tile = f.sV + (j % FWD_SV) * TB;
+                }
+                fix_tile<D, 1>(tile, f.qidx_blk, qmin_blk, Kidx_bh, kb, s.NK, lane, 32 * (ew & 3));
+                fence_async_smem();
+            }
+            epi_arrive(f.fixed);
+        }
+        mbar_wait(&f.s_full[b], (j / FWD_NB) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+        tc_fence_after();
+        if (kPacked && packed_row) {
+            // the thread's chunks loaded at once, packed math; on partially
+            // visible tiles invisible keys are masked to p = 0
+            uint32_t r[CP][32];
+#pragma unroll
+            for (int cc = 0; cc < CP; ++cc) tmem_ld32(tl + b * 128 + (h * CP + cc) * 32, r[cc]);
+            uint32_t vis[CP];
+#pragma unroll
+            for (int cc = 0; cc < CP; ++cc)
+                vis[cc] = all ? 0xffffffffu : vis_mask32(Kidx_bh, kb * TILE + (h * CP + cc) * 32, s.NK, s.causal, qpos);
+            tmem_ld_wait();
+#pragma unroll
+            for (int cc = 0; cc < CP; ++cc) {
+                const uint32_t col = tl + b * 128 + (h * CP + cc) * 32;
+#pragma unroll
+                for (int g = 0; g < 2; ++g) {
+                    uint32_t hi[8], lo[8];
+#pragma unroll
+                    for (int m = 0; m < 8; ++m) {
+                        float2 pp = entmax_pair<PINV>(r[cc][16 * g + 2 * m], r[cc][16 * g + 2 * m + 1],
+                                                      c1, mtau, uhi);
+                        const int bit = 16 * g + 2 * m;
+                        pp.x = (vis[cc] >> bit) & 1u ? pp.x : 0.0f;
+                        pp.y = (vis[cc] >> (bit + 1)) & 1u ? pp.y : 0.0f;
+                        n2 = __fadd2_rn(n2, pp);
+                        split_pair(pp, hi[m], lo[m]);
+                    }
+                    tmem_st8(col + g * 16, hi);
+                    tmem_st8(col + g * 16 + 8, lo);
+                }
+            }
+            tmem_st_wait();
+            tc_fence_before();
+            epi_arrive(&f.p_full[b]);
+            continue;
+        }
+#pragma unroll
+        for (int cc = 0; cc < CP; ++cc) {
+            const int c = h * CP + cc;
+            uint32_t r[32];
+            tmem_ld32(tl + b * 128 + c * 32, r);
+            tmem_ld_wait();
+            float p[32];
+            if (all) {
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                    const float u = __fmaf_rn(s.am1, clamp_score(__uint_as_float(r[i]), s.scale), -tq);
+                    p[i] = entmax_pk<PINV>(u, s.pinv.e);
+                    n += p[i];
+                }
+            } else {
+                const uint32_t vis = vis_mask32(Kidx_bh, kb * TILE + c * 32, s.NK, s.causal, qpos);
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                    const bool v = (vis >> i) & 1u;
+                    const float u = __fmaf_rn(s.am1, clamp_score(__uint_as_float(r[i]), s.scale), -tq);
+                    p[i] = v ? entmax_pk<PINV>(u, s.pinv.e) : 0.0f;
+                    n += p[i];
+                }
+            }
+            // two 16-key groups: hi then lo columns over the group's own S columns
+#pragma unroll
+            for (int g = 0; g < 2; ++g) {
+                uint32_t hi[8], lo[8];
+#pragma unroll
+                for (int m = 0; m < 8; ++m) {
+                    const float x0 = p[16 * g + 2 * m], x1 = p[16 * g + 2 * m + 1];
+                    const __nv_bfloat162 hh = __floats2bfloat162_rn(x0, x1);
+                    const float2 hf = __bfloat1622float2(hh);
+                    hi[m] = *reinterpret_cast<const uint32_t*>(&hh);
+                    lo[m] = pack_bf16(x0 - hf.x, x1 - hf.y);
+                }
+                tmem_st8(tl + b * 128 + c * 32 + g * 16, hi);
+                if (split) tmem_st8(tl + b * 128 + c * 32 + g * 16 + 8, lo);
+            }
+        }
+        tmem_st_wait();
+        tc_fence_before();
+        epi_arrive(&f.p_full[b]);
+    }
+    n += n2.x + n2.y;
+    // row sum: the warpgroups' partial sums added in group order
+    f.nsum[h * TILE + row] = n;
+    asm volatile("bar.sync 2, %0;" ::"n"(NE) : "memory");
+    if (h == 0) {
+        for (int g = 1; g < NW; ++g) n += f.nsum[g * TILE + row];
+        if (qv) rownorm[qrow] = n;
+        f.nsum[row] = n;
+    }
+    asm volatile("bar.sync 2, %0;" ::"n"(NE) : "memory");
+    n = f.nsum[row];
+    mbar_wait(f.o_full, 0, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+    tc_fence_after();
+    const float inv = __fdiv_rn(1.0f, __fadd_rn(n, ASA_EPS));
+    // every MMA is done: the K stages are free for the store staging
+    float* stage = reinterpret_cast<float*>(f.sK) + (et >> 5) * (32 * 33);
+    const int q0 = qb * TILE + (warp & 3) * 32;
+    const int nrows = min(32, s.NQ - q0);
+    const size_t row0 = (size_t)bh * s.NQ + q0;
+#pragma unroll 1
+    for (int c = h; c < D / 32; c += NW) {
+        uint32_t r[32];
+        tmem_ld32(tl + FWD_TO + c * 32, r);
+        tmem_ld_wait();
+        if (nrows <= 0) continue;
+        float o[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+            float v = f.T > 0 ? __uint_as_float(r[i]) * inv : 0.0f;
+            o[i] = isfinite(v) ? v : 0.0f;
+        }
+        if (O32) warp_store_rows<float>(O32 + row0 * D, D, nrows, c * 32, o, stage, lane);
+        if (sizeof(TO) == 2 || (void*)O != (void*)O32) warp_store_rows<TO>(O + row0 * D, D, nrows, c * 32, o, stage, lane);
+    }
+}
+
+template <int NW>
+constexpr int fwd_threads() { return K3_EPI0 + 128 * NW; }
+
+template <int D, typename TO, int PINV, int NW>
+__global__ void __launch_bounds__(fwd_threads<NW>(), 1)
 k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
            const __grid_constant__ CUtensorMap tmV, Shape s, const int32_t* __restrict__ Qidx,
            const int32_t* __restrict__ Kidx, Bounds bd, const float* __restrict__ tau,
            const int32_t* __restrict__ ptr, const int32_t* __restrict__ idx, TO* __restrict__ O,
            float* __restrict__ O32, float* __restrict__ rownorm, int split, int* err) {
-    constexpr int S = 3;                      // K stages
-    constexpr int SV = 2;                     // V stages
-    constexpr int NB = 3;                     // S / P buffers in TMEM
     constexpr int TB = D * TILE * 2;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* base = align1024(smem_raw, err);
-    uint8_t* sQ = base;
-    uint8_t* sK = base + TB;                  // S stages
-    uint8_t* sV = sK + S * TB;                // SV stages
-    uint64_t* bars = reinterpret_cast<uint64_t*>(sV + SV * TB);
+    FwdPhase f;
+    f.sQ = base;
+    f.sK = base + TB;
+    f.sV = f.sK + FWD_S * TB;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(f.sV + FWD_SV * TB);
     uint64_t* q_full = bars;
-    uint64_t* k_full = bars + 1;
-    uint64_t* k_empty = k_full + S;
-    uint64_t* v_full = k_empty + S;
-    uint64_t* v_empty = v_full + SV;
-    uint64_t* s_full = v_empty + SV;          // [NB]
-    uint64_t* s_free = s_full + NB;           // [NB]
-    uint64_t* p_full = s_free + NB;           // [NB]
-    uint64_t* o_full = p_full + NB;
-    uint64_t* fixed = o_full + 1;             // K/V of a tile-load-zeroing tile fixed
-    uint64_t* drain = fixed + 1;              // [2] exit-time MMA drains (after a timed-out wait)
     uint32_t* holder = reinterpret_cast<uint32_t*>(bars + 24);
-    float* nsum = reinterpret_cast<float*>(holder + 4);     // [NWG][128]
-    int* qidx_blk = reinterpret_cast<int*>(nsum + NWG * TILE);    // [128]
+    f.nsum = reinterpret_cast<float*>(holder + 4);                    // [NW][128]
+    int* qidx_blk = reinterpret_cast<int*>(f.nsum + NW * TILE);       // [128]
     uint32_t* sched = reinterpret_cast<uint32_t*>(qidx_blk + TILE);   // [T]
+    f.qidx_blk = qidx_blk;
+    f.sched = sched;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int bh = blockIdx.y;
@@ -1144,21 +1546,13 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
     const int32_t* Kidx_bh = Kidx + (size_t)bh * s.NK;
     const int32_t* list = idx + (size_t)bh * s.nQB * s.nKB;
     const int e0 = ptr[(size_t)bh * (s.nQB + 1) + qb];
-    const int T = ptr[(size_t)bh * (s.nQB + 1) + qb + 1] - e0;
+    f.T = ptr[(size_t)bh * (s.nQB + 1) + qb + 1] - e0;
 
+    fwd_init_barriers(f, bars + 1, 4 * NW);
     if (threadIdx.x == 0) {
         mbar_init(q_full, 1);
-        for (int i = 0; i < S; ++i) { mbar_init(&k_full[i], 1); mbar_init(&k_empty[i], 1); }
-        for (int i = 0; i < SV; ++i) { mbar_init(&v_full[i], 1); mbar_init(&v_empty[i], 1); }
-        for (int i = 0; i < NB; ++i) {
-            mbar_init(&s_full[i], 1); mbar_init(&s_free[i], 1); mbar_init(&p_full[i], EPI_WARPS);
-        }
-        mbar_init(o_full, 1);
-        mbar_init(fixed, EPI_WARPS);
-        mbar_init(&drain[0], 1);
-        mbar_init(&drain[1], 1);
         fence_barrier_init();
-        if (T > 0) {
+        if (f.T > 0) {
             // Q and the first K/V tiles do not depend on the schedule being
             // built below: issue them now so their latency hides the set-up
             const int kb0 = list[e0];
@@ -1166,12 +1560,12 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
             tma_prefetch_desc(&tmK);
             tma_prefetch_desc(&tmV);
             mbar_expect_tx(q_full, TB);
-            mbar_expect_tx(&k_full[0], TB);
-            mbar_expect_tx(&v_full[0], TB);
+            mbar_expect_tx(&f.k_full[0], TB);
+            mbar_expect_tx(&f.v_full[0], TB);
             for (int bx = 0; bx < D / BOX; ++bx) {
-                tma_load_3d(sQ + bx * BOX_BYTES, &tmQ, q_full, bx * BOX, qb * TILE, bh);
-                tma_load_3d(sK + bx * BOX_BYTES, &tmK, &k_full[0], bx * BOX, kb0 * TILE, bh);
-                tma_load_3d(sV + bx * BOX_BYTES, &tmV, &v_full[0], bx * BOX, kb0 * TILE, bh);
+                tma_load_3d(f.sQ + bx * BOX_BYTES, &tmQ, q_full, bx * BOX, qb * TILE, bh);
+                tma_load_3d(f.sK + bx * BOX_BYTES, &tmK, &f.k_full[0], bx * BOX, kb0 * TILE, bh);
+                tma_load_3d(f.sV + bx * BOX_BYTES, &tmV, &f.v_full[0], bx * BOX, kb0 * TILE, bh);
             }
         }
     }
@@ -1180,268 +1574,197 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
         const int r = threadIdx.x - K3_EPI0;
         const int q = qb * TILE + r;
         if (r < TILE) qidx_blk[r] = (q < s.NQ && s.causal) ? Qidx[(size_t)bh * s.NQ + q] : INT_MAX;
-        sched_from_list(sched, list + e0, T, s, bd, bh, qb, false, r);
+        if (r < NEPI) sched_from_list(sched, list + e0, f.T, s, bd, bh, qb, false, r);
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tbase = *holder;
-    constexpr uint32_t tO = 384;
     const int qmin_blk = s.causal ? bd.qmin[bh * s.nQB + qb] : INT_MIN;
 
     if (warp == 0) {
-        if (lane == 0 && T > 0) {
-            for (int j = 1; j < T; ++j) {   // Q and tile 0 were issued at set-up
-                const int kb = (int)(sched[j] & SCHED_IDX);
-                const int st = j % S;
-                mbar_wait(&k_empty[st], ((j / S) & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
-                mbar_expect_tx(&k_full[st], TB);
-                for (int bx = 0; bx < D / BOX; ++bx)
-                    tma_load_3d(sK + st * TB + bx * BOX_BYTES, &tmK, &k_full[st], bx * BOX, kb * TILE, bh);
-            }
-        } else if (lane == 1 && T > 0) {
-            // V runs on its own thread: its ring (freed after P·V) must not
-            // hold back the K ring (freed after S)
-            for (int j = 1; j < T; ++j) {
-                const int kb = (int)(sched[j] & SCHED_IDX);
-                const int sv = j % SV;
-                mbar_wait(&v_empty[sv], ((j / SV) & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
-                mbar_expect_tx(&v_full[sv], TB);
-                for (int bx = 0; bx < D / BOX; ++bx)
-                    tma_load_3d(sV + sv * TB + bx * BOX_BYTES, &tmV, &v_full[sv], bx * BOX, kb * TILE, bh);
-            }
-        }
-        __syncwarp();
-        if (lane == 0 && T > 0 && error_set(err)) {   // a wait gave up: let this CTA's loads land
-            mbar_drain(q_full, 0);
-            drain_ring(k_full, S, T);
-            drain_ring(v_full, SV, T);
-        }
+        fwd_produce<D>(f, &tmK, &tmV, s, bh, lane, 1, q_full, err);
     } else if (warp == 1) {
-        // S = Q·K^T issuer.  tcgen05.mma issue blocks at the tensor pipe's
-        // rate, so S and P·V come from two warps: while one waits for its
-        // inputs the other keeps the pipe fed.  S(n) needs its K tile and
-        // TMEM buffer n % NB, which P·V(n - NB) frees.
-        constexpr uint32_t idS = idesc_bf16(128, 128, 0, 0);
-        if (T > 0) mbar_wait(q_full, 0, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
-        const uint64_t dQ = kdesc(sQ, 0);
-        int nfix = 0;
-        for (int n = 0; n < T; ++n) {
-            const uint32_t e = sched[n];
-            const int st = n % S, b = n % NB;
-            uint8_t* kt = sK + st * TB;
-            mbar_wait(&k_full[st], (n / S) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
-            if (e & SCHED_FIX)     // the epilogue warps zero K and V of this tile
-                mbar_wait(fixed, (nfix++) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
-            __syncwarp();
-            mbar_wait(&s_free[b], ((n / NB) & 1) ^ 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
-            tc_fence_after();
-            if (lane == 0) {
-                const uint64_t dK = kdesc(kt, 0);
-#pragma unroll
-                for (int kk = 0; kk < D / 16; ++kk)
-                    mma_bf16_ss(tbase + b * 128, kdesc_step(dQ, kk), kdesc_step(dK, kk), idS, kk > 0);
-                mma_commit(&s_full[b]);
-                mma_commit(&k_empty[st]);
-            }
-            __syncwarp();
-        }
-        if (lane == 0 && error_set(err)) {   // a wait gave up: let this warp's MMAs finish
-            mma_commit(&drain[0]);
-            mbar_drain(&drain[0], 0);
-        }
-        __syncwarp();
+        fwd_mma_s<D>(f, s, tbase, lane, q_full, err);
     } else if (warp == 2) {
-        // O += P·V issuer: P·V(m) needs its V tile and the epilogue's P.
-        // P·V(m) needs no wait on `fixed`: p_full(m) completes only after
-        // every epilogue warp's arrival, and the warps that zero V of a
-        // tile-load-zeroing tile arrive after that zeroing and its proxy fence.
-        constexpr uint32_t idPV = idesc_bf16(128, D, 0, 1);
-        for (int m = 0; m < T; ++m) {
-            const int b = m % NB, sv = m % SV;
-            uint8_t* vt = sV + sv * TB;
-            mbar_wait(&v_full[sv], (m / SV) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
-            __syncwarp();
-            mbar_wait(&p_full[b], (m / NB) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
-            tc_fence_after();
-            if (lane == 0) {
-                const uint32_t pb = tbase + b * 128;
-                const uint64_t dV = mndesc(vt, 0);
-#pragma unroll
-                for (int kk = 0; kk < TILE / 16; ++kk)
-                    mma_bf16_ts(tbase + tO, pb + kk * 16, mndesc_step(dV, kk), idPV, (m > 0 || kk > 0));
-                if (split) {
-#pragma unroll
-                    for (int kk = 0; kk < TILE / 16; ++kk)
-                        mma_bf16_ts(tbase + tO, pb + kk * 16 + 8, mndesc_step(dV, kk), idPV, 1);
-                }
-                mma_commit(&s_free[b]);
-                mma_commit(&v_empty[sv]);
-            }
-            __syncwarp();
-        }
-        if (lane == 0) mma_commit(o_full);
-        if (lane == 0 && error_set(err)) {   // a wait gave up: let this warp's MMAs finish
-            mma_commit(&drain[1]);
-            mbar_drain(&drain[1], 0);
-        }
-        __syncwarp();
+        fwd_mma_pv<D>(f, s, tbase, lane, split, err);
     } else {
         const int row = (warp & 3) * 32 + lane;
         const int et = threadIdx.x - K3_EPI0;
-        const int h = et / TILE;
         const int q = qb * TILE + row;
         const bool qv = q < s.NQ;
         const size_t qrow = (size_t)bh * s.NQ + (qv ? q : 0);
         const int qpos = !qv ? INT_MIN : (s.causal ? Qidx[qrow] : INT_MAX);
         const float tq = qv ? tau[qrow] : 0.0f;
-        const uint32_t tl = tmem_lane_base(tbase, warp);
-        float n = 0.0f;
-        constexpr bool kPacked = PINV == 1 || PINV == 2 || PINV == 4;
-        const float2 c1 = make_float2(__fmul_rn(s.am1, s.scale), __fmul_rn(s.am1, s.scale));
-        const float2 mtau = make_float2(-tq, -tq);
-        const float uhi = __fmaf_rn(s.am1, 10.0f, -tq);
-        // warp-uniform: the packed path issues warp-collective TMEM loads/stores
-        const bool packed_row = __all_sync(0xffffffffu, kPacked && split && __fmaf_rn(s.am1, -10.0f, -tq) <= 0.0f);
-        float2 n2 = make_float2(0.0f, 0.0f);
-        for (int j = 0; j < T; ++j) {
-            const uint32_t e = sched[j];
-            const int kb = (int)(e & SCHED_IDX);
-            const bool all = (e & SCHED_ALL) != 0;
-            const int b = j % NB;
-            if (e & SCHED_FIX) {
-                // The reference's tile-load zeroing of this tile's K and V, by
-                // the eight epilogue warps (32 rows each of K or V) instead of
-                // one control warp: S and P·V wait for it.
-                const int ew = et >> 5;
-                uint8_t* tile;
-                if (ew < 4) {
-                    mbar_wait(&k_full[j % S], (j / S) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
-                    tile = sK + (j % S) * TB;
-                } else {
-                    mbar_wait(&v_full[j % SV], (j / SV) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
-                    tile = sV + (j % SV) * TB;
-                }
-                fix_tile<D, 1>(tile, qidx_blk, qmin_blk, Kidx_bh, kb, s.NK, lane, 32 * (ew & 3));
-                fence_async_smem();
-                epi_arrive(fixed);
-            }
-            mbar_wait(&s_full[b], (j / NB) & 1, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
-            tc_fence_after();
-            if (kPacked && packed_row) {
-                // both chunks loaded at once, packed math; on partially
-                // visible tiles invisible keys are masked to p = 0
-                uint32_t r[CPT][32];
-#pragma unroll
-                for (int cc = 0; cc < CPT; ++cc) tmem_ld32(tl + b * 128 + (h * CPT + cc) * 32, r[cc]);
-                uint32_t vis[CPT];
-#pragma unroll
-                for (int cc = 0; cc < CPT; ++cc)
-                    vis[cc] = all ? 0xffffffffu : vis_mask32(Kidx_bh, kb * TILE + (h * CPT + cc) * 32, s.NK, s.causal, qpos);
-                tmem_ld_wait();
-#pragma unroll
-                for (int cc = 0; cc < CPT; ++cc) {
-                    const uint32_t col = tl + b * 128 + (h * CPT + cc) * 32;
-#pragma unroll
-                    for (int g = 0; g < 2; ++g) {
-                        uint32_t hi[8], lo[8];
-#pragma unroll
-                        for (int m = 0; m < 8; ++m) {
-                            float2 pp = entmax_pair<PINV>(r[cc][16 * g + 2 * m], r[cc][16 * g + 2 * m + 1],
-                                                          c1, mtau, uhi);
-                            const int bit = 16 * g + 2 * m;
-                            pp.x = (vis[cc] >> bit) & 1u ? pp.x : 0.0f;
-                            pp.y = (vis[cc] >> (bit + 1)) & 1u ? pp.y : 0.0f;
-                            n2 = __fadd2_rn(n2, pp);
-                            split_pair(pp, hi[m], lo[m]);
-                        }
-                        tmem_st8(col + g * 16, hi);
-                        tmem_st8(col + g * 16 + 8, lo);
-                    }
-                }
-                tmem_st_wait();
-                tc_fence_before();
-                epi_arrive(&p_full[b]);
-                continue;
-            }
-#pragma unroll
-            for (int cc = 0; cc < CPT; ++cc) {
-                const int c = h * CPT + cc;
-                uint32_t r[32];
-                tmem_ld32(tl + b * 128 + c * 32, r);
-                tmem_ld_wait();
-                float p[32];
-                if (all) {
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) {
-                        const float u = __fmaf_rn(s.am1, clamp_score(__uint_as_float(r[i]), s.scale), -tq);
-                        p[i] = entmax_pk<PINV>(u, s.pinv.e);
-                        n += p[i];
-                    }
-                } else {
-                    const uint32_t vis = vis_mask32(Kidx_bh, kb * TILE + c * 32, s.NK, s.causal, qpos);
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) {
-                        const bool v = (vis >> i) & 1u;
-                        const float u = __fmaf_rn(s.am1, clamp_score(__uint_as_float(r[i]), s.scale), -tq);
-                        p[i] = v ? entmax_pk<PINV>(u, s.pinv.e) : 0.0f;
-                        n += p[i];
-                    }
-                }
-                // two 16-key groups: hi then lo columns over the group's own S columns
-#pragma unroll
-                for (int g = 0; g < 2; ++g) {
-                    uint32_t hi[8], lo[8];
-#pragma unroll
-                    for (int m = 0; m < 8; ++m) {
-                        const float x0 = p[16 * g + 2 * m], x1 = p[16 * g + 2 * m + 1];
-                        const __nv_bfloat162 hh = __floats2bfloat162_rn(x0, x1);
-                        const float2 hf = __bfloat1622float2(hh);
-                        hi[m] = *reinterpret_cast<const uint32_t*>(&hh);
-                        lo[m] = pack_bf16(x0 - hf.x, x1 - hf.y);
-                    }
-                    tmem_st8(tl + b * 128 + c * 32 + g * 16, hi);
-                    if (split) tmem_st8(tl + b * 128 + c * 32 + g * 16 + 8, lo);
-                }
-            }
-            tmem_st_wait();
-            tc_fence_before();
-            epi_arrive(&p_full[b]);
-        }
-        n += n2.x + n2.y;
-        // row sum: the warpgroups' partial sums added in group order
-        nsum[h * TILE + row] = n;
-        epi_bar();
-        if (h == 0) {
-            for (int g = 1; g < NWG; ++g) n += nsum[g * TILE + row];
-            if (qv) rownorm[qrow] = n;
-            nsum[row] = n;
-        }
-        epi_bar();
-        n = nsum[row];
-        mbar_wait(o_full, 0, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
+        fwd_epilogue<D, TO, PINV, NW>(f, s, Kidx_bh, qmin_blk, tbase, warp, lane, et, bh, qb, qpos, tq, O, O32,
+                                      rownorm, split, err);
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
         tc_fence_after();
-        const float inv = __fdiv_rn(1.0f, __fadd_rn(n, ASA_EPS));
-        // every MMA is done: the K stages are free for the store staging
-        float* stage = reinterpret_cast<float*>(sK) + (et >> 5) * (32 * 33);
-        const int q0 = qb * TILE + (warp & 3) * 32;
-        const int nrows = min(32, s.NQ - q0);
-        const size_t row0 = (size_t)bh * s.NQ + q0;
-#pragma unroll 1
-        for (int c = h; c < D / 32; c += NWG) {
-            uint32_t r[32];
-            tmem_ld32(tl + tO + c * 32, r);
-            tmem_ld_wait();
-            if (nrows <= 0) continue;
-            float o[32];
-#pragma unroll
-            for (int i = 0; i < 32; ++i) {
-                float v = T > 0 ? __uint_as_float(r[i]) * inv : 0.0f;
-                o[i] = isfinite(v) ? v : 0.0f;
-            }
-            if (O32) warp_store_rows<float>(O32 + row0 * D, D, nrows, c * 32, o, stage, lane);
-            if (sizeof(TO) == 2 || (void*)O != (void*)O32) warp_store_rows<TO>(O + row0 * D, D, nrows, c * 32, o, stage, lane);
+        tmem_dealloc(tbase, 512);
+    }
+}
+
+// ===========================================================================
+// K13: the fused forward -- τ / mask and the forward in one CTA per query
+// block (no counterpart in the reference, whose forward is three launches).
+// Phase A is the τ / mask pass over the visible tiles; its merge yields the
+// row's top-k, τ (solved by the row's merging thread with the same solve as
+// k1_tau_solve), and the block's active key blocks, which become phase B's
+// schedule directly: no tile lists are read, and Q stays in shared memory.
+// Phase B's loads and S MMAs start while the τ solves run; its epilogue
+// waits for τ.  TMEM: four S buffers in phase A, three S buffers and O in
+// phase B.  Shared memory: Q, three K stages, then phase A's chunk copies
+// and bounds, over which phase B's two V stages are laid.
+// ===========================================================================
+template <int D, int NW>
+constexpr size_t fused_region_bytes() {
+    return mask_extra_bytes<D, NW>() > (size_t)FWD_SV * D * TILE * 2 ? mask_extra_bytes<D, NW>()
+                                                                      : (size_t)FWD_SV * D * TILE * 2;
+}
+
+template <int D, typename TO, int KM, int PINV, int NW>
+__global__ void __launch_bounds__(fwd_threads<NW>(), 1)
+k13_fused(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+          const __grid_constant__ CUtensorMap tmV, Shape s, const int32_t* __restrict__ Qidx,
+          const int32_t* __restrict__ Kidx, Bounds bd, float* __restrict__ tau, uint8_t* __restrict__ M,
+          TO* __restrict__ O, float* __restrict__ O32, float* __restrict__ rownorm, int split, int* err) {
+    constexpr int NE = 128 * NW;
+    constexpr int TB = D * TILE * 2;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* base = align1024(smem_raw, err);
+    MaskPhase m;
+    FwdPhase f;
+    m.sQ = f.sQ = base;
+    m.sK = f.sK = base + TB;
+    uint8_t* region = base + TB + MASK_S * TB;
+    m.cbuf = reinterpret_cast<float4*>(region);
+    m.thr_s = reinterpret_cast<float*>(m.cbuf + NE * (4 / NW) * 8);
+    m.seed_s = m.thr_s + 3 * NW * TILE;
+    f.sV = region;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(region + fused_region_bytes<D, NW>());
+    m.q_full = bars;
+    m.k_full = bars + 1;
+    m.k_empty = bars + 1 + MASK_S;
+    m.s_full = bars + 1 + 2 * MASK_S;
+    m.s_free = m.s_full + MASK_NB;
+    m.fixed = m.s_free + MASK_NB;
+    m.drain = m.fixed + 1;
+    uint64_t* fbars = bars + 24;                                        // FWD_BARS
+    uint32_t* holder = reinterpret_cast<uint32_t*>(bars + 48);
+    f.nsum = reinterpret_cast<float*>(holder + 4);                      // [NW][128]
+    float* tau_s = f.nsum + NW * TILE;                                  // [128]
+    int* qidx_blk = reinterpret_cast<int*>(tau_s + TILE);               // [128]
+    int* misc = qidx_blk + TILE;                                        // [16]
+    uint32_t* sched_a = reinterpret_cast<uint32_t*>(misc + 16);         // [nKB]
+    uint32_t* sched_b = sched_a + s.nKB;                                // [nKB]
+    m.flags = reinterpret_cast<uint8_t*>(sched_b + s.nKB);              // [nKB]
+    m.qidx_blk = f.qidx_blk = qidx_blk;
+    m.sched = sched_a;
+    f.sched = sched_b;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int bh = blockIdx.y;
+    const int qb = s.causal ? (int)(gridDim.x - 1 - blockIdx.x) : (int)blockIdx.x;
+    const int32_t* Kidx_bh = Kidx + (size_t)bh * s.NK;
+
+    fwd_init_barriers(f, fbars, 4 * NW);
+    if (threadIdx.x == 0) {
+        mask_init_barriers<MASK_NB>(m, NE);
+        fence_barrier_init();
+        tma_prefetch_desc(&tmQ);
+        tma_prefetch_desc(&tmK);
+        tma_prefetch_desc(&tmV);
+        mbar_expect_tx(m.q_full, TB);
+        for (int bx = 0; bx < D / BOX; ++bx)
+            tma_load_3d(m.sQ + bx * BOX_BYTES, &tmQ, m.q_full, bx * BOX, qb * TILE, bh);
+    }
+    if (warp == 1) { tmem_alloc(holder, 512); tmem_relinquish(); }
+    if (threadIdx.x >= K3_EPI0) {
+        const int r = threadIdx.x - K3_EPI0;
+        if (r < TILE) {
+            const int q = qb * TILE + r;
+            qidx_blk[r] = (q < s.NQ && s.causal) ? Qidx[(size_t)bh * s.NQ + q] : INT_MAX;
         }
+        for (int i = r; i < 3 * NW * TILE; i += NE) m.thr_s[i] = ASA_SENTINEL;
+        for (int i = r; i < s.nKB; i += NE) m.flags[i] = 0;
+        if (r < NEPI) {                       // the schedule builders' barrier counts NEPI threads
+            const int n = sched_visible(sched_a, misc, s, bd, bh, qb, r);
+            if (r == 0) misc[8] = n;
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tbase = *holder;
+    const int qmin_blk = s.causal ? bd.qmin[bh * s.nQB + qb] : INT_MIN;
+    m.T = misc[8];
+
+    // ---- phase A: top-k and the block's active key blocks
+    const int row = (warp & 3) * 32 + lane;
+    const int et = threadIdx.x - K3_EPI0;
+    const int q = qb * TILE + row;
+    const bool qv = q < s.NQ;
+    const size_t qrow = (size_t)bh * s.NQ + (qv ? q : 0);
+    const int qpos = !qv ? INT_MIN : (s.causal ? Qidx[qrow] : INT_MAX);
+    float mv[KM];
+    if (warp == 0) {
+        if (lane == 0) mask_produce<D>(m, &tmK, s, bh, err);
+    } else if (warp == 1) {
+        mask_mma<D>(m, s, tbase, lane, err);
+    } else if (warp >= K3_EPI0 / 32) {
+        TopK<KM> tk;
+        mask_epilogue<D, KM, NW>(m, s, Kidx_bh, qmin_blk, tbase, warp, lane, et, qpos, tk, err);
+        mask_merge<KM, NW>(m, s, tk, reinterpret_cast<unsigned long long*>(m.sK), row, et / TILE, qv, qrow,
+                           nullptr, nullptr, mv);
+        uint8_t* Mrow = M + ((size_t)bh * s.nQB + qb) * s.nKB;
+        for (int i = et; i < s.nKB; i += NE) Mrow[i] = m.flags[i];
+        // phase B's schedule: the active key blocks in ascending order
+        if (et < NEPI) {
+            const int w = et >> 5;
+            int total = 0;
+            for (int b0 = 0; b0 < s.nKB; b0 += NEPI) {
+                const int kb = b0 + et;
+                const bool v = kb < s.nKB && m.flags[kb];
+                const uint32_t bal = __ballot_sync(0xffffffffu, v);
+                if (lane == 0) misc[w] = __popc(bal);
+                epi_bar();
+                int before = 0, all = 0;
+                for (int i = 0; i < NEPI / 32; ++i) {
+                    before += i < w ? misc[i] : 0;
+                    all += misc[i];
+                }
+                if (v) sched_b[total + before + __popc(bal & ((1u << lane) - 1))] = sched_entry(s, bd, bh, qb, kb, kb);
+                total += all;
+                epi_bar();
+            }
+            if (et == 0) misc[9] = total;
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    f.T = misc[9];
+
+    // ---- phase B: the forward over the active key blocks
+    if (warp == 0) {
+        fwd_produce<D>(f, &tmK, &tmV, s, bh, lane, 0, nullptr, err);
+    } else if (warp == 1) {
+        fwd_mma_s<D>(f, s, tbase, lane, nullptr, err);
+    } else if (warp == 2) {
+        fwd_mma_pv<D>(f, s, tbase, lane, split, err);
+    } else {
+        if (et < TILE) {
+            // τ from the merged top-k (k1_tau_solve's solve on the same values)
+            const float tq = qv ? ref_tau<KM>(mv, s.k, s.alpha) : 0.0f;
+            if (qv) tau[qrow] = tq;
+            tau_s[row] = tq;
+        }
+        asm volatile("bar.sync 2, %0;" ::"n"(NE) : "memory");
+        fwd_epilogue<D, TO, PINV, NW>(f, s, Kidx_bh, qmin_blk, tbase, warp, lane, et, bh, qb, qpos, tau_s[row],
+                                      O, O32, rownorm, split, err);
     }
     tc_fence_before();
     __syncthreads();
@@ -2449,7 +2772,10 @@ cudaError_t prep(F* f, size_t smem) {
     return cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
 }
 
-constexpr size_t kSmemTail = 24 * 8 + 16 + (NWG + 1) * 128 * 4 + 64;  // barriers, TMEM holder, per-row arrays
+// The forward's epilogue width: four warpgroups (one 32-column chunk of each
+// tile per thread) when the fused kernel runs the same width, so both forwards
+// add a row's weights in the same order.
+bool fwd_wide(const Shape& s) { return s.k <= 8; }
 constexpr size_t kSmemTailBwd = 16 * 8 + 16 + 2 * 6 * 128 * 4 + 128 * 4;  // + per-query arrays x2
 
 bool is_sm100() {
@@ -2466,7 +2792,8 @@ bool is_sm100() {
 }  // namespace
 
 #ifndef ASA_TC_PART
-#define ASA_TC_PART 0   // 0: everything; 1: τ/mask + sizing, 2: forward, 3: backward prologue + dQ, 4: dK/dV
+#define ASA_TC_PART 0   // 0: everything; 1: τ/mask + sizing, 2: forward, 3: backward prologue + dQ, 4: dK/dV,
+                        // 5: fused forward
 #endif
 #define ASA_PART(n) (ASA_TC_PART == 0 || ASA_TC_PART == (n))
 
@@ -2592,19 +2919,74 @@ cudaError_t tc_forward(const Shape& s, const void* Q, const void* K, const void*
         constexpr int D = decltype(dtag)::value;
         using TO = std::remove_pointer_t<decltype(out)>;
         return with_alpha(s, [&](auto ac) -> cudaError_t {
-            auto k = k3_forward<D, TO, decltype(ac)::pinv>;
-            const size_t smem = (size_t)D * TILE * 2 * 6 + kSmemTail + (size_t)s.nKB * 4;
-            cudaError_t r = prep(k, smem);
-            if (r != cudaSuccess) return r;
-            k<<<grid, K3_THREADS, smem, st>>>(mQ, mK, mV, s, Qidx, Kidx, bd, tau, ptr, idx, (TO*)O, O32,
-                                            rownorm, split, err);
-            note_launch();
-            return cudaGetLastError();
+            auto go = [&](auto k, auto nw) -> cudaError_t {
+                constexpr int NW = decltype(nw)::value;
+                // Q, K and V stages, barriers + TMEM holder, per-row arrays, the schedule
+                const size_t smem = (size_t)D * TILE * 2 * 6 + 24 * 8 + 16 + (size_t)(NW + 1) * TILE * 4 + 64 +
+                                    (size_t)s.nKB * 4;
+                cudaError_t r = prep(k, smem);
+                if (r != cudaSuccess) return r;
+                k<<<grid, fwd_threads<NW>(), smem, st>>>(mQ, mK, mV, s, Qidx, Kidx, bd, tau, ptr, idx, (TO*)O,
+                                                         O32, rownorm, split, err);
+                note_launch();
+                return cudaGetLastError();
+            };
+            constexpr int PI = decltype(ac)::pinv;
+            if (fwd_wide(s)) return go(k3_forward<D, TO, PI, 4>, std::integral_constant<int, 4>{});
+            return go(k3_forward<D, TO, PI, 2>, std::integral_constant<int, 2>{});
         });
     });
 }
 
 #endif  // part 2
+
+#if ASA_PART(5)
+bool tc_fused_supported(const Shape& s) {
+    return !s.exact_tau && s.out_dtype == ASA_DTYPE_BF16 && s.k <= 16;
+}
+
+cudaError_t tc_fused_forward(const Shape& s, const void* Q, const void* K, const void* V, const int32_t* Qidx,
+                             const int32_t* Kidx, float* tau, uint8_t* M, void* O, float* O32, float* rownorm,
+                             void* ws, int* err, cudaStream_t st) {
+    if (!tc_fused_supported(s)) return cudaErrorInvalidValue;
+    cudaError_t e = launch_bounds(s, Qidx, Kidx, ws, st);
+    if (e != cudaSuccess) return e;
+    CUtensorMap mQ, mK, mV;
+    if (!make_map(&mQ, Q, s.BH, s.NQ, s.d) || !make_map(&mK, K, s.BH, s.NK, s.d) ||
+        !make_map(&mV, V, s.BH, s.NK, s.d))
+        return cudaErrorInvalidValue;
+    Bounds bd = bounds_at(s, ws);
+    dim3 grid(s.nQB, s.BH);
+    const int split = s.split;
+    using bf = __nv_bfloat16;
+    return with_alpha(s, [&](auto ac) -> cudaError_t {
+        constexpr int PI = decltype(ac)::pinv;
+        auto go = [&](auto k, auto dtag, auto nw) -> cudaError_t {
+            constexpr int D = decltype(dtag)::value, NW = decltype(nw)::value;
+            // Q, K stages, the phase region, 48 barriers + TMEM holder, row
+            // sums, τ, positions, counts, two schedules and the flags
+            const size_t smem = (size_t)D * TILE * 2 * (1 + MASK_S) + fused_region_bytes<D, NW>() + 48 * 8 + 16 +
+                                (size_t)(NW + 2) * TILE * 4 + 16 * 4 + (size_t)s.nKB * 9 + 64;
+            cudaError_t r = prep(k, smem);
+            if (r != cudaSuccess) return r;
+            k<<<grid, fwd_threads<NW>(), smem, st>>>(mQ, mK, mV, s, Qidx, Kidx, bd, tau, M, (bf*)O, O32, rownorm,
+                                                     split, err);
+            note_launch();
+            return cudaGetLastError();
+        };
+        using I64 = std::integral_constant<int, 64>;
+        using I128 = std::integral_constant<int, 128>;
+        using W2 = std::integral_constant<int, 2>;
+        using W4 = std::integral_constant<int, 4>;
+        if (s.d == 128) {
+            if (s.k <= 8) return go(k13_fused<128, bf, 8, PI, 4>, I128{}, W4{});
+            return go(k13_fused<128, bf, 16, PI, 2>, I128{}, W2{});
+        }
+        if (s.k <= 8) return go(k13_fused<64, bf, 8, PI, 4>, I64{}, W4{});
+        return go(k13_fused<64, bf, 16, PI, 2>, I64{}, W2{});
+    });
+}
+#endif  // part 5
 
 // Backward launch arguments shared by the dQ and dK/dV launchers.
 struct BwdArgs {

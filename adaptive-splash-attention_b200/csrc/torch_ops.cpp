@@ -10,7 +10,8 @@
 //
 //   splash_attention::forward(Q, K, V, Q_idx?, K_idx?, alpha, sm_scale, k_keep,
 //       block_m, block_n, causal, backend, precision, out_f32, ref_tile_load,
-//       tau_mode, grad_mode, need_o32) -> (O, O32, tau, M, csr_ptr, csr_idx, rownorm)
+//       tau_mode, grad_mode, fused_forward, need_o32)
+//       -> (O, O32, tau, M, csr_ptr, csr_idx, rownorm)
 //   splash_attention::backward(Q, K, V, Q_idx?, K_idx?, O32, tau, M, csr_ptr,
 //       csr_idx, rownorm, dO, alpha, sm_scale, k_keep, block_m, block_n,
 //       causal, backend, precision, out_f32, ref_tile_load, tau_mode,
@@ -172,7 +173,7 @@ FwdOut forward_cuda(const Tensor& Q_, const Tensor& K_, const Tensor& V_,
                     double alpha, double sm_scale, int64_t k_keep, int64_t block_m,
                     int64_t block_n, bool causal, int64_t backend, int64_t precision,
                     bool out_f32, bool ref_tile_load, int64_t tau_mode, int64_t grad_mode,
-                    bool need_o32) {
+                    bool fused_forward, bool need_o32) {
     TORCH_CHECK(Q_.is_cuda() && K_.is_cuda() && V_.is_cuda(),
                 "splash_attention: tensors must be on a CUDA device");   // reference :543
     TORCH_CHECK(V_.sizes() == K_.sizes() && V_.scalar_type() == Q_.scalar_type() &&
@@ -183,6 +184,7 @@ FwdOut forward_cuda(const Tensor& Q_, const Tensor& K_, const Tensor& V_,
     const Cfg c = cfg_of(alpha, sm_scale, k_keep, block_m, block_n, causal, backend, precision,
                          out_f32, ref_tile_load, tau_mode, grad_mode);
     asa_params p = make_params(Q, K, c);
+    p.fused_forward = fused_forward ? 1 : 0;
     check_positions(Qidx, (int64_t)p.B * p.H, p.NQ, "Q_idx", causal);
     check_positions(Kidx, (int64_t)p.B * p.H, p.NK, "K_idx", causal);
     FwdOut out = forward_shapes(Q, K, c, need_o32, Q.options());
@@ -210,7 +212,7 @@ FwdOut forward_meta(const Tensor& Q, const Tensor& K, const Tensor& V,
                     double alpha, double sm_scale, int64_t k_keep, int64_t block_m,
                     int64_t block_n, bool causal, int64_t backend, int64_t precision,
                     bool out_f32, bool ref_tile_load, int64_t tau_mode, int64_t grad_mode,
-                    bool need_o32) {
+                    bool fused_forward, bool need_o32) {
     const Cfg c = cfg_of(alpha, sm_scale, k_keep, block_m, block_n, causal, backend, precision,
                          out_f32, ref_tile_load, tau_mode, grad_mode);
     return forward_shapes(Q, K, c, need_o32, Q.options());
@@ -271,7 +273,7 @@ TORCH_LIBRARY(splash_attention, m) {
         "forward(Tensor Q, Tensor K, Tensor V, Tensor? Q_idx, Tensor? K_idx, float alpha, "
         "float sm_scale, int k_keep, int block_m, int block_n, bool causal, int backend, "
         "int precision, bool out_f32, bool ref_tile_load, int tau_mode, int grad_mode, "
-        "bool need_o32) -> "
+        "bool fused_forward, bool need_o32) -> "
         "(Tensor, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor)");
     m.def(
         "backward(Tensor Q, Tensor K, Tensor V, Tensor? Q_idx, Tensor? K_idx, Tensor O32, "

@@ -62,15 +62,15 @@ def _setup_context(ctx, inputs, output):
     O, O32, tau, M, ptr, idx, rown = output
     ctx.mark_non_differentiable(O32, tau, M, ptr, idx, rown)
     ctx.save_for_backward(Q, K, V, Qi, Ki, O32 if O32.numel() else O, tau, M, ptr, idx, rown)
-    ctx.cfg = tuple(inputs[5:-1])      # everything but need_o32
+    ctx.cfg = tuple(inputs[5:-2])      # everything but fused_forward and need_o32
 
 
 def _backward(ctx, dO, *_unused):
     Q, K, V, Qi, Ki, O32, tau, M, ptr, idx, rown = ctx.saved_tensors
     if dO is None:
-        return (None,) * 18
+        return (None,) * 19
     dQ, dK, dV = _ops.backward(Q, K, V, Qi, Ki, O32, tau, M, ptr, idx, rown, dO, *ctx.cfg)
-    return (dQ.to(Q.dtype), dK.to(K.dtype), dV.to(V.dtype)) + (None,) * 15
+    return (dQ.to(Q.dtype), dK.to(K.dtype), dV.to(V.dtype)) + (None,) * 16
 
 
 torch.library.register_autograd("splash_attention::forward", _backward,
@@ -79,7 +79,8 @@ torch.library.register_autograd("splash_attention::forward", _backward,
 
 def splash_attention(Q, K, V, Q_idx=None, K_idx=None, *, alpha=1.5, sm_scale=None, k_keep=8,
                      block_m=128, block_n=128, causal=True, backend="auto", precision="split",
-                     out_dtype=None, ref_tile_load=True, tau_mode="reference", grad_mode="reference"):
+                     out_dtype=None, ref_tile_load=True, tau_mode="reference", grad_mode="reference",
+                     fused_forward=True):
     """α-entmax block-sparse attention with autograd.  Q, K, V: [B, H, N, d]
     float32 or bfloat16 on CUDA; Q_idx / K_idx: positions [B*H, N] (any
     integer dtype; [N] broadcasts).  Key k is visible to query q iff
@@ -98,7 +99,12 @@ def splash_attention(Q, K, V, Q_idx=None, K_idx=None, *, alpha=1.5, sm_scale=Non
     α-entmax threshold over every visible key (and the mask by every tile
     holding a positive weight); grad_mode="jacobian" replaces the fixed-τ
     gradient by the α-entmax Jacobian.  Both together give exact α-entmax
-    attention and its exact gradient."""
+    attention and its exact gradient.
+
+    fused_forward=True runs the tcgen05 forward (bf16 output, k_keep <= 16,
+    reference τ) as one kernel per query block -- τ / mask and the forward
+    together; False runs them as separate launches.  The outputs agree
+    either way."""
     st = Settings(alpha=alpha, sm_scale=sm_scale, k_keep=k_keep, block_m=block_m,
                   block_n=block_n, causal=causal, backend=backend, precision=precision,
                   out_dtype=out_dtype, ref_tile_load=ref_tile_load, tau_mode=tau_mode,
@@ -109,7 +115,7 @@ def splash_attention(Q, K, V, Q_idx=None, K_idx=None, *, alpha=1.5, sm_scale=Non
     qi = _index(Q_idx, BH, Q.shape[2], Q.device, "Q_idx") if causal else None
     ki = _index(K_idx, BH, K.shape[2], Q.device, "K_idx") if causal else None
     need_o32 = torch.is_grad_enabled() and any(t.requires_grad for t in (Q, K, V))
-    return _ops.forward(Q, K, V, qi, ki, *_op_config(Q, st), need_o32)[0]
+    return _ops.forward(Q, K, V, qi, ki, *_op_config(Q, st), bool(fused_forward), need_o32)[0]
 
 
 class AdaptiveSplashAttention(torch.nn.Module):

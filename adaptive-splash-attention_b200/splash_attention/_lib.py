@@ -37,7 +37,8 @@ class Params(ctypes.Structure):
                 ("in_dtype", ctypes.c_int), ("out_dtype", ctypes.c_int),
                 ("backend", ctypes.c_int), ("precision", ctypes.c_int),
                 ("timeout_spins", ctypes.c_longlong), ("ref_tile_load", ctypes.c_int),
-                ("tau_mode", ctypes.c_int), ("grad_mode", ctypes.c_int)]
+                ("tau_mode", ctypes.c_int), ("grad_mode", ctypes.c_int),
+                ("fused_forward", ctypes.c_int)]
 
 
 class AsaError(RuntimeError):

@@ -54,6 +54,9 @@ class Settings:
     tau_mode: str = "reference"
     # "reference": the fixed-τ gradient; "jacobian": the α-entmax Jacobian
     grad_mode: str = "reference"
+    # tcgen05 forward: one fused τ / mask + forward kernel (include/asa.h
+    # fused_forward); False runs the separate launches
+    fused_forward: bool = True
 
 
 def make_params(Q, K, st: Settings):
@@ -81,6 +84,7 @@ def make_params(Q, K, st: Settings):
                          f"grad_mode in {tuple(L.GRAD_MODE)}")
     p.tau_mode = L.TAU_MODE[st.tau_mode]
     p.grad_mode = L.GRAD_MODE[st.grad_mode]
+    p.fused_forward = 1 if st.fused_forward else 0
     return p
 
 

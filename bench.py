@@ -120,9 +120,10 @@ def make_inputs(c, h0, h1, device):
     return (*out, idx)
 
 
-def settings(c, backend="auto", precision="split"):
+def settings(c, backend="auto", precision="split", fused=True):
     return dict(alpha=c["alpha"], sm_scale=c["sm_scale"], k_keep=c["k_keep"], block_m=c["BM"],
-                block_n=c["BN"], causal=c["causal"], backend=backend, precision=precision)
+                block_n=c["BN"], causal=c["causal"], backend=backend, precision=precision,
+                fused_forward=fused)
 
 
 class Clocks:
@@ -270,7 +271,7 @@ def measure(a, c, name, rank, world, dev, scaling, dist, with_extras=True):
 
     total_heads, (h0, h1) = head_range(c, rank, world, scaling)
     Q, K, V, dO, idx = make_inputs(c, h0, h1, dev)
-    st = settings(c, a.backend, a.precision)
+    st = settings(c, a.backend, a.precision, not a.unfused)
     q, k, v = (x.detach().requires_grad_(not c["fwd_only"]) for x in (Q, K, V))
 
     def step():
@@ -351,6 +352,7 @@ def measure(a, c, name, rank, world, dev, scaling, dist, with_extras=True):
                             + "; tau/mask pass timed, not counted",
            "gpu_launches": launches, "clocks": clk.summary()}
     in_bytes = sum(x.numel() * x.element_size() for x in (Q, K, V, dO))
+    rec["config"]["fused_forward"] = st["fused_forward"]
     rec["config"]["l2"] = (f"inputs {in_bytes / 2**20:.0f} MiB per rank "
                            + ("exceed the 126 MB L2; no flush" if in_bytes > 126e6
                               else "fit in L2: L2 flushed between steps is NOT done; small case"))
@@ -361,7 +363,7 @@ def measure(a, c, name, rank, world, dev, scaling, dist, with_extras=True):
     with ops.profile() as prof:
         step()
     kern = prof.result
-    fwd_labels = ("tau_mask", "tile_lists", "forward")
+    fwd_labels = ("tau_mask", "tile_lists", "forward", "forward_fused")
     rec["fwd_ms"] = sum(kern.get(x, (0, 0))[0] for x in fwd_labels)
     rec["bwd_ms"] = sum(v_[0] for k_, v_ in kern.items() if k_ not in fwd_labels)
     peak_b, peak_s, hbm, peak_kind = load_peaks()
@@ -370,6 +372,8 @@ def measure(a, c, name, rank, world, dev, scaling, dist, with_extras=True):
     pairs = h_local * (N * (N + 1) // 2 if c["causal"] else N * N)
     if dom_label == "tau_mask":
         dom_flops = 2.0 * c["d"] * pairs
+    elif dom_label == "forward_fused":   # the τ/mask pass's S over visible pairs + the forward
+        dom_flops = 2.0 * c["d"] * pairs + TILE_UNITS["forward"] * unit_flops * T_local
     else:
         dom_flops = TILE_UNITS.get(dom_label, 0) * unit_flops * T_local
     per_launch_ms = dom_ms / max(dom_n, 1)
@@ -468,6 +472,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--backend", default="auto")
     ap.add_argument("--precision", default="split")
+    ap.add_argument("--unfused", action="store_true",
+                    help="separate τ/mask, tile-list and forward launches instead of the fused forward")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--e2e-chunk", type=int, default=4, help="heads per chunk in the e2e leg")

@@ -100,11 +100,16 @@ typedef struct asa_params {
                            /* 0: every visible key is read in full.              */
     int tau_mode;          /* asa_tau_mode (default ASA_TAU_REFERENCE)            */
     int grad_mode;         /* asa_grad_mode (default ASA_GRAD_REFERENCE)          */
+    int fused_forward;     /* tcgen05 forward with reference τ, bf16 out, k <= 16: */
+                           /* 1 (default) one kernel per query block runs τ /     */
+                           /* mask and the forward (Q read once, no tile lists    */
+                           /* between them); 0: separate τ / mask, tile-list and  */
+                           /* forward launches.  Same outputs either way.         */
 } asa_params;
 
 /* Defaults: block 128x128, k_keep 8, α 1.5, sm_scale 0 (set it), causal,
  * bf16 in / bf16 out, AUTO backend, SPLIT precision, ref_tile_load 1,
- * reference τ and gradient. */
+ * reference τ and gradient, fused_forward 1. */
 void asa_params_default(asa_params* p);
 
 /* Workspace each call needs, in bytes (16-byte multiples).

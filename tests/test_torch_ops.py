@@ -27,7 +27,7 @@ def test_meta_shapes(B, H, NQ, NK, d, out_dtype):
     ki = torch.arange(NK, dtype=torch.int32, device="meta")
     cfg = sa._op_config(q, sa.Settings(out_dtype=out_dtype))
     O, O32, tau, M, ptr, idx, rown = torch.ops.splash_attention.forward(
-        q, k, k, qi.expand(B * H, NQ).contiguous(), ki.expand(B * H, NK).contiguous(), *cfg, True)
+        q, k, k, qi.expand(B * H, NQ).contiguous(), ki.expand(B * H, NK).contiguous(), *cfg, True, True)
     nqb, nkb = -(-NQ // 128), -(-NK // 128)
     assert O.shape == (B, H, NQ, d) and O.dtype == (out_dtype or torch.bfloat16)
     assert O32.numel() == (0 if out_dtype == torch.float32 else B * H * NQ * d)

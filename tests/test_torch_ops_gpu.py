@@ -30,6 +30,6 @@ def test_opcheck(cuda):
     import splash_attention as sa
     Q, K, V, dO, Qi, Ki = (x.to(cuda) for x in make_inputs(1, 2, 256, 256, 128, seed=4,
                                                           dtype=torch.bfloat16))
-    args = (Q, K, V, Qi, Ki) + sa._op_config(Q, sa.Settings()) + (True,)
+    args = (Q, K, V, Qi, Ki) + sa._op_config(Q, sa.Settings()) + (True, True)
     torch.library.opcheck(torch.ops.splash_attention.forward.default, args,
                           test_utils=("test_schema", "test_faketensor", "test_autograd_registration"))
