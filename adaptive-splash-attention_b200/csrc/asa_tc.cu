@@ -744,11 +744,23 @@ __device__ void mask_epilogue(const MaskPhase& m, const Shape& s, const int32_t*
                                                          __uint_as_float(r[4 * q8 + 2]), __uint_as_float(r[4 * q8 + 3]));
             }
             const float* myf = reinterpret_cast<const float*>(my + cc * 8);
-            while (cand) {
-                const int i = __ffs(cand) - 1;
-                cand &= cand - 1;
-                const float v = clamp_score(myf[(((i >> 2) ^ sw) << 2) | (i & 3)], s.scale);
-                if (v > tk.threshold()) tk.insert(v, kn0 + i);   // keys ascend per thread
+            // the next candidate's shared-memory read is issued before the
+            // current one is inserted, so its latency overlaps the insertion
+            if (cand) {
+                int i = __ffs(cand) - 1;
+                float x = myf[(((i >> 2) ^ sw) << 2) | (i & 3)];
+                for (;;) {
+                    cand &= cand - 1;
+                    const int ci = i;
+                    const float cx = x;
+                    if (cand) {
+                        i = __ffs(cand) - 1;
+                        x = myf[(((i >> 2) ^ sw) << 2) | (i & 3)];
+                    }
+                    const float v = clamp_score(cx, s.scale);
+                    if (v > tk.threshold()) tk.insert(v, kn0 + ci);   // keys ascend per thread
+                    if (!cand) break;
+                }
             }
         }
         {
