@@ -436,6 +436,19 @@ __device__ __forceinline__ uint32_t vis_mask32(const int32_t* __restrict__ Kidx_
     return vis;
 }
 
+// Shared-memory float4 loads / stores that other threads' writes may change
+// between calls (the compiler must not cache or merge them).
+__device__ __forceinline__ float4 ld_volatile_f4(const float* p) {
+    float4 v;
+    asm volatile("ld.volatile.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(smem_u32(p)) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_volatile_f4(float* p, float4 v) {
+    asm volatile("st.volatile.shared.v4.f32 [%0], {%1, %2, %3, %4};"
+                 :: "r"(smem_u32(p)), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w) : "memory");
+}
+
 __device__ __forceinline__ uint32_t tmem_lane_base(uint32_t tbase, int warp) {
     return tbase + ((uint32_t)((warp & 3) * 32) << 16);
 }
@@ -541,7 +554,7 @@ struct MaskPhase {
     uint8_t* sQ;
     uint8_t* sK;              // MASK_S stages
     float4* cbuf;             // [NE][CP][8] chunk copies
-    float* thr_s;             // [3][NW][128] published bounds
+    float* thr_s;             // [NW][128] float4: published bounds (b0, b1, b2, unused)
     float* seed_s;            // [NW][128] seed bounds
     uint64_t* q_full;
     uint64_t* k_full;         // [MASK_S]
@@ -559,7 +572,7 @@ struct MaskPhase {
 // Shared memory the phase needs beyond Q and the K stages.
 template <int D, int NW>
 constexpr size_t mask_extra_bytes() {
-    return (size_t)128 * NW * (4 / NW) * 8 * 16 + (size_t)3 * NW * TILE * 4 + (size_t)NW * TILE * 4;
+    return (size_t)128 * NW * (4 / NW) * 8 * 16 + (size_t)4 * NW * TILE * 4 + (size_t)NW * TILE * 4;
 }
 
 template <int NB_>
@@ -665,12 +678,11 @@ __device__ void mask_epilogue(const MaskPhase& m, const Shape& s, const int32_t*
             float m1 = __uint_as_float(0x7f800000u), x2 = neg_inf(), y2 = neg_inf();
 #pragma unroll
             for (int g = 0; g < NW; ++g) {
-                const volatile float* t = m.thr_s + g * TILE + row;
-                if (g != h) lim = fmaxf(lim, t[0]);
-                m1 = fminf(m1, t[NW * TILE]);
-                const float c2 = t[2 * NW * TILE];
-                y2 = fmaxf(y2, fminf(x2, c2));
-                x2 = fmaxf(x2, c2);
+                const float4 t = ld_volatile_f4(m.thr_s + 4 * (g * TILE + row));
+                if (g != h) lim = fmaxf(lim, t.x);
+                m1 = fminf(m1, t.y);
+                y2 = fmaxf(y2, fminf(x2, t.z));
+                x2 = fmaxf(x2, t.z);
             }
             lim = fmaxf(lim, fmaxf(m1, NW > 2 ? y2 : neg_inf()));
         }
@@ -765,15 +777,17 @@ __device__ void mask_epilogue(const MaskPhase& m, const Shape& s, const int32_t*
         }
         {
             float v1 = tk.v[KM - 1], v2 = tk.v[KM - 1];
+            if (first == 0) {   // k = KM: the indices are constants
+                v1 = tk.v[(KM + NW - 1) / NW - 1];
+                v2 = tk.v[(KM + 1) / 2 - 1];
+            } else {
 #pragma unroll
-            for (int i = 0; i < KM; ++i) {
-                if (i == i1) v1 = tk.v[i];
-                if (i == i2) v2 = tk.v[i];
+                for (int i = 0; i < KM; ++i) {
+                    if (i == i1) v1 = tk.v[i];
+                    if (i == i2) v2 = tk.v[i];
+                }
             }
-            volatile float* t = m.thr_s + h * TILE + row;
-            t[0] = tk.threshold();
-            t[NW * TILE] = v1;
-            t[2 * NW * TILE] = v2;
+            st_volatile_f4(m.thr_s + 4 * (h * TILE + row), make_float4(tk.threshold(), v1, v2, 0.0f));
         }
     }
 }
@@ -846,7 +860,7 @@ k1_tau_mask(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
     m.sK = base + TB;
     m.cbuf = reinterpret_cast<float4*>(m.sK + MASK_S * TB);
     m.thr_s = reinterpret_cast<float*>(m.cbuf + NE * (4 / NW) * 8);
-    m.seed_s = m.thr_s + 3 * NW * TILE;
+    m.seed_s = m.thr_s + 4 * NW * TILE;
     uint64_t* bars = reinterpret_cast<uint64_t*>(m.seed_s + NW * TILE);
     m.q_full = bars;
     m.k_full = bars + 1;
@@ -885,7 +899,7 @@ k1_tau_mask(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
             const int q = qb * TILE + r;
             qidx_blk[r] = (q < s.NQ && s.causal) ? Qidx[(size_t)bh * s.NQ + q] : INT_MAX;
         }
-        for (int i = r; i < 3 * NW * TILE; i += NE) m.thr_s[i] = ASA_SENTINEL;
+        for (int i = r; i < 4 * NW * TILE; i += NE) m.thr_s[i] = ASA_SENTINEL;
         for (int i = r; i < s.nKB; i += NE) m.flags[i] = 0;
         if (r < NEPI) {                       // the schedule builders' barrier counts NEPI threads
             const int n = sched_visible(sched, misc, s, bd, bh, qb, r);
@@ -1654,7 +1668,7 @@ k13_fused(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUten
     uint8_t* region = base + TB + MASK_S * TB;
     m.cbuf = reinterpret_cast<float4*>(region);
     m.thr_s = reinterpret_cast<float*>(m.cbuf + NE * (4 / NW) * 8);
-    m.seed_s = m.thr_s + 3 * NW * TILE;
+    m.seed_s = m.thr_s + 4 * NW * TILE;
     f.sV = region;
     uint64_t* bars = reinterpret_cast<uint64_t*>(region + fused_region_bytes<D, NW>());
     m.q_full = bars;
@@ -1700,7 +1714,7 @@ k13_fused(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUten
             const int q = qb * TILE + r;
             qidx_blk[r] = (q < s.NQ && s.causal) ? Qidx[(size_t)bh * s.NQ + q] : INT_MAX;
         }
-        for (int i = r; i < 3 * NW * TILE; i += NE) m.thr_s[i] = ASA_SENTINEL;
+        for (int i = r; i < 4 * NW * TILE; i += NE) m.thr_s[i] = ASA_SENTINEL;
         for (int i = r; i < s.nKB; i += NE) m.flags[i] = 0;
         if (r < NEPI) {                       // the schedule builders' barrier counts NEPI threads
             const int n = sched_visible(sched_a, misc, s, bd, bh, qb, r);
@@ -2864,8 +2878,13 @@ cudaError_t tc_tau_mask(const Shape& s, const void* Q, const void* K, const int3
     const size_t rows = (size_t)s.BH * s.NQ;
     auto go = [&](auto kern, auto solve, int D, int NW) -> cudaError_t {
         const int S = 3;
-        const size_t smem = (size_t)D * TILE * 2 * (1 + S) + (size_t)128 * 128 * 4 + (size_t)NW * TILE * 16 +
-                            24 * 8 + 16 + 2 * TILE * 4 + 64 + (size_t)s.nKB * 5 + 64;
+        // Q, the K stages, chunk copies and bounds, barriers + TMEM holder,
+        // positions, counts, the schedule and the flags, alignment slack
+        const size_t smem = (size_t)D * TILE * 2 * (1 + S) + (D == 128 ? (NW == 4 ? mask_extra_bytes<128, 4>()
+                                                                               : mask_extra_bytes<128, 2>())
+                                                                    : (NW == 4 ? mask_extra_bytes<64, 4>()
+                                                                               : mask_extra_bytes<64, 2>())) +
+                            24 * 8 + 16 + TILE * 4 + 16 * 4 + (size_t)s.nKB * 5 + 64;
         cudaError_t r = prep(kern, smem);
         if (r != cudaSuccess) return r;
         kern<<<grid, 64 + 128 * NW, smem, st>>>(mQ, mK, s, Qidx, Kidx, bd, topv, topi_out, M, err);
