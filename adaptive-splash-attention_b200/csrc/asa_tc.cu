@@ -7,6 +7,9 @@
 //                TMEM (four buffers), epilogue warps stream each score row
 //                through the reference top-k (reference build_mask_kernel
 //                :150-217); k1_tau_solve then solves τ per row
+//   k13_fused    the two above in one CTA per query block: the top-k phase,
+//                τ from the merged lists, then the forward over the block's
+//                active key blocks (no tile lists read; Q loaded once)
 //   k3_forward   O = Σ p v / (Σ p + EPS) over the CSR tile list: S = Q·K^T,
 //                entmax p in the epilogue warps, P written back to TMEM as a
 //                bf16 hi/lo pair, O += P_hi·V + P_lo·V in TMEM
