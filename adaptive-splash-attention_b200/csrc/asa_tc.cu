@@ -7,7 +7,7 @@
 //                TMEM (four buffers), epilogue warps stream each score row
 //                through the reference top-k (reference build_mask_kernel
 //                :150-217); k1_tau_solve then solves τ per row
-//   k13_fused    the two above in one CTA per query block: the top-k phase,
+//   k13_fused    k1_tau_mask and k3_forward in one CTA per query block: top-k,
 //                τ from the merged lists, then the forward over the block's
 //                active key blocks (no tile lists read; Q loaded once)
 //   k3_forward   O = Σ p v / (Σ p + EPS) over the CSR tile list: S = Q·K^T,
@@ -2745,15 +2745,17 @@ __global__ void k4_pre(const float* __restrict__ O32, const __nv_bfloat16* __res
 // ===========================================================================
 // host side
 // ===========================================================================
+// Looked up once per process; a function-local static's initialisation is
+// thread-safe, so concurrent first calls from several host threads are fine.
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-    if (!fn) {
+    static const PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
         void* p = nullptr;
         cudaDriverEntryPointQueryResult q;
         if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
             q == cudaDriverEntryPointSuccess)
-            fn = (PFN_cuTensorMapEncodeTiled_v12000)p;
-    }
+            return (PFN_cuTensorMapEncodeTiled_v12000)p;
+        return (PFN_cuTensorMapEncodeTiled_v12000) nullptr;
+    }();
     return fn;
 }
 
@@ -2807,15 +2809,12 @@ cudaError_t prep(F* f, size_t smem) {
 bool fwd_wide(const Shape& s) { return s.k <= 8; }
 constexpr size_t kSmemTailBwd = 16 * 8 + 16 + 2 * 6 * 128 * 4 + 128 * 4;  // + per-query arrays x2
 
+// Whether the current device is sm_100 (per call: a process may use several
+// devices; the attribute query is cheap).
 bool is_sm100() {
-    static int cached = -1;
-    if (cached < 0) {
-        int dev = 0, major = 0;
-        cached = (cudaGetDevice(&dev) == cudaSuccess &&
-                  cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) == cudaSuccess &&
-                  major == 10) ? 1 : 0;
-    }
-    return cached == 1;
+    int dev = 0, major = 0;
+    return cudaGetDevice(&dev) == cudaSuccess &&
+           cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) == cudaSuccess && major == 10;
 }
 
 }  // namespace
