@@ -104,6 +104,21 @@ __device__ __forceinline__ bool needs_fix(const Shape& s, const Bounds& b, int b
     return b.kmax[bh * s.nKB + kb] > b.qmin[bh * s.nQB + qb];
 }
 
+// Block order of the one-dimensional grids over (head, row block): groups
+// of kGroupHeads heads, and inside a group the heads fastest, so each group's
+// heaviest blocks (causal: the last query blocks) are dispatched first while
+// the K/V of only a few heads are live in L2 at a time.  Returns (head,
+// block); reverse: block nb-1 is the first dispatched.
+constexpr int kGroupHeads = 4;
+__device__ __forceinline__ int2 grid_order(int BH, int nb, bool reverse) {
+    const int L = (int)blockIdx.x;
+    const int g = L / (kGroupHeads * nb);
+    const int gh = min(kGroupHeads, BH - g * kGroupHeads);
+    const int idx = L - g * kGroupHeads * nb;
+    const int rank = idx / gh;
+    return make_int2(g * kGroupHeads + idx % gh, reverse ? nb - 1 - rank : rank);
+}
+
 // ---- per-CTA tile schedule ----------------------------------------------------
 // Each CTA stages its tile sequence in shared memory once, so no role chases
 // a global list -> bounds dependency per tile: entry = block index (low 24
@@ -881,8 +896,8 @@ k1_tau_mask(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
     m.sched = sched;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int bh = blockIdx.y;
-    const int qb = s.causal ? (int)(gridDim.x - 1 - blockIdx.x) : (int)blockIdx.x;
+    const int2 bq = grid_order(s.BH, s.nQB, s.causal != 0);
+    const int bh = bq.x, qb = bq.y;
     const int32_t* Kidx_bh = Kidx + (size_t)bh * s.NK;
 
     if (threadIdx.x == 0) {
@@ -986,8 +1001,8 @@ k1_exact(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtens
     uint8_t* flags = reinterpret_cast<uint8_t*>(sched + s.nKB);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int bh = blockIdx.y;
-    const int qb = s.causal ? (int)(gridDim.x - 1 - blockIdx.x) : (int)blockIdx.x;
+    const int2 bq = grid_order(s.BH, s.nQB, s.causal != 0);
+    const int bh = bq.x, qb = bq.y;
     const int32_t* Kidx_bh = Kidx + (size_t)bh * s.NK;
 
     if (threadIdx.x == 0) {
@@ -1570,8 +1585,8 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
     f.sched = sched;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int bh = blockIdx.y;
-    const int qb = s.causal ? (int)(gridDim.x - 1 - blockIdx.x) : (int)blockIdx.x;
+    const int2 bq = grid_order(s.BH, s.nQB, s.causal != 0);
+    const int bh = bq.x, qb = bq.y;
     const int32_t* Kidx_bh = Kidx + (size_t)bh * s.NK;
     const int32_t* list = idx + (size_t)bh * s.nQB * s.nKB;
     const int e0 = ptr[(size_t)bh * (s.nQB + 1) + qb];
@@ -1695,8 +1710,8 @@ k13_fused(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUten
     f.sched = sched_b;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int bh = blockIdx.y;
-    const int qb = s.causal ? (int)(gridDim.x - 1 - blockIdx.x) : (int)blockIdx.x;
+    const int2 bq = grid_order(s.BH, s.nQB, s.causal != 0);
+    const int bh = bq.x, qb = bq.y;
     const int32_t* Kidx_bh = Kidx + (size_t)bh * s.NK;
 
     fwd_init_barriers(f, fbars, 4 * NW);
@@ -1847,8 +1862,8 @@ k4_dq(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
     uint32_t* sched = reinterpret_cast<uint32_t*>(qidx_blk + TILE);   // [T]
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int bh = blockIdx.y;
-    const int qb = s.causal ? (int)(gridDim.x - 1 - blockIdx.x) : (int)blockIdx.x;
+    const int2 bq = grid_order(s.BH, s.nQB, s.causal != 0);
+    const int bh = bq.x, qb = bq.y;
     const int32_t* Kidx_bh = Kidx + (size_t)bh * s.NK;
     const int32_t* list = idx + (size_t)bh * s.nQB * s.nKB;
     const int e0 = ptr[(size_t)bh * (s.nQB + 1) + qb];
@@ -2167,8 +2182,8 @@ k4_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtenso
     uint32_t* sched = reinterpret_cast<uint32_t*>(qidx_blk + TILE);   // [T]
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int bh = blockIdx.y;
-    const int kb = blockIdx.x;
+    const int2 bk = grid_order(s.BH, s.nKB, false);   // low key blocks (seen by most queries) first
+    const int bh = bk.x, kb = bk.y;
     const int32_t* Kidx_bh = Kidx + (size_t)bh * s.NK;
     const int32_t* Qidx_bh = Qidx + (size_t)bh * s.NQ;
     const int32_t* list = cidx + (size_t)bh * s.nKB * s.nQB;
@@ -2529,8 +2544,8 @@ k4_jac(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensor
     uint32_t* sched = reinterpret_cast<uint32_t*>(qidx_blk + TILE);   // [T]
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int bh = blockIdx.y;
-    const int qb = s.causal ? (int)(gridDim.x - 1 - blockIdx.x) : (int)blockIdx.x;
+    const int2 bq = grid_order(s.BH, s.nQB, s.causal != 0);
+    const int bh = bq.x, qb = bq.y;
     const int32_t* Kidx_bh = Kidx + (size_t)bh * s.NK;
     const int32_t* list = idx + (size_t)bh * s.nQB * s.nKB;
     const int e0 = ptr[(size_t)bh * (s.nQB + 1) + qb];
@@ -2873,7 +2888,7 @@ cudaError_t tc_tau_mask(const Shape& s, const void* Q, const void* K, const int3
     CUtensorMap mQ, mK;
     if (!make_map(&mQ, Q, s.BH, s.NQ, s.d) || !make_map(&mK, K, s.BH, s.NK, s.d)) return cudaErrorInvalidValue;
     Bounds bd = bounds_at(s, ws);
-    dim3 grid(s.nQB, s.BH);
+    dim3 grid(s.BH * s.nQB);
     // the rows' top-k scores (and keys) in order: the caller's buffers, or
     // the workspace when only τ and the mask are wanted
     float* topv = topv_out ? topv_out : (float*)((char*)ws + topv_offset(s));
@@ -2916,7 +2931,7 @@ cudaError_t tc_exact_tau(const Shape& s, const void* Q, const void* K, const int
     CUtensorMap mQ, mK;
     if (!make_map(&mQ, Q, s.BH, s.NQ, s.d) || !make_map(&mK, K, s.BH, s.NK, s.d)) return cudaErrorInvalidValue;
     Bounds bd = bounds_at(s, ws);
-    dim3 grid(s.nQB, s.BH);
+    dim3 grid(s.BH * s.nQB);
     return with_alpha(s, [&](auto ac) -> cudaError_t {
         constexpr int PI = decltype(ac)::pinv, PE = decltype(ac)::pe2;
         auto go = [&](auto kern, int D) -> cudaError_t {
@@ -2946,7 +2961,7 @@ cudaError_t tc_forward(const Shape& s, const void* Q, const void* K, const void*
         !make_map(&mV, V, s.BH, s.NK, s.d))
         return cudaErrorInvalidValue;
     Bounds bd = bounds_at(s, ws);   // filled by tc_tau_mask
-    dim3 grid(s.nQB, s.BH);
+    dim3 grid(s.BH * s.nQB);
     const int split = s.split;
     return with_dtype_d(s, [&](auto dtag, auto* out) -> cudaError_t {
         constexpr int D = decltype(dtag)::value;
@@ -2989,7 +3004,7 @@ cudaError_t tc_fused_forward(const Shape& s, const void* Q, const void* K, const
         !make_map(&mV, V, s.BH, s.NK, s.d))
         return cudaErrorInvalidValue;
     Bounds bd = bounds_at(s, ws);
-    dim3 grid(s.nQB, s.BH);
+    dim3 grid(s.BH * s.nQB);
     const int split = s.split;
     using bf = __nv_bfloat16;
     return with_alpha(s, [&](auto ac) -> cudaError_t {
@@ -3054,7 +3069,7 @@ cudaError_t tc_launch_dq(const Shape& s, const BwdArgs& a, cudaStream_t st) {
             const size_t smem = smem_for(two ? 2 : 1);
             cudaError_t r = prep(kdq, smem);
             if (r != cudaSuccess) return r;
-            kdq<<<dim3(s.nQB, s.BH), DQ_THREADS, smem, st>>>(a.mQ, a.mK, a.mV, a.mdO, s, a.Qidx, a.Kidx, a.bd,
+            kdq<<<dim3(s.BH * s.nQB), DQ_THREADS, smem, st>>>(a.mQ, a.mK, a.mV, a.mdO, s, a.Qidx, a.Kidx, a.bd,
                                                              a.tau, a.invNv, a.Dq, a.ptr, a.idx, (TO*)a.dQ,
                                                              split, a.err);
             note_launch();
@@ -3098,7 +3113,7 @@ cudaError_t tc_backward(const Shape& s, const void* Q, const void* K, const void
                                         TILE * 4 + (size_t)s.nKB * 4 + 64;
                     cudaError_t r = prep(kern, smem);
                     if (r != cudaSuccess) return r;
-                    kern<<<dim3(s.nQB, s.BH), DQ_THREADS, smem, st>>>(a.mQ, a.mK, a.mV, a.mdO, s, Qidx, Kidx, bd,
+                    kern<<<dim3(s.BH * s.nQB), DQ_THREADS, smem, st>>>(a.mQ, a.mK, a.mV, a.mdO, s, Qidx, Kidx, bd,
                                                                      tau, ptr, idx, Dq, err);
                     note_launch();
                     return cudaGetLastError();
@@ -3132,7 +3147,7 @@ cudaError_t tc_launch_dkdv(const Shape& s, const BwdArgs& a, cudaStream_t st) {
             const size_t smem = bwd_smem<TO>(s, D);
             cudaError_t r = prep(kkv, smem);
             if (r != cudaSuccess) return r;
-            kkv<<<dim3(s.nKB, s.BH), DKV_THREADS, smem, st>>>(a.mQ, a.mK, a.mV, a.mdO, s, a.Qidx, a.Kidx, a.bd,
+            kkv<<<dim3(s.BH * s.nKB), DKV_THREADS, smem, st>>>(a.mQ, a.mK, a.mV, a.mdO, s, a.Qidx, a.Kidx, a.bd,
                                                           a.tau, a.invNv, a.Dq, a.cptr, a.cidx, (TO*)a.dK,
                                                           (TO*)a.dV, split, a.err);
             note_launch();
