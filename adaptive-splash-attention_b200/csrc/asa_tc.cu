@@ -2914,11 +2914,11 @@ cudaError_t tc_tau_mask(const Shape& s, const void* Q, const void* K, const int3
     };
     if (s.d == 128) {
         if (s.k <= 8) return go(k1_tau_mask<128, 8, 4>, k1_tau_solve<8>, 128, 4);
-        if (s.k <= 16) return go(k1_tau_mask<128, 16, 2>, k1_tau_solve<16>, 128, 2);
+        if (s.k <= 16) return go(k1_tau_mask<128, 16, 4>, k1_tau_solve<16>, 128, 4);
         return go(k1_tau_mask<128, 32, 2>, k1_tau_solve<32>, 128, 2);
     }
     if (s.k <= 8) return go(k1_tau_mask<64, 8, 4>, k1_tau_solve<8>, 64, 4);
-    if (s.k <= 16) return go(k1_tau_mask<64, 16, 2>, k1_tau_solve<16>, 64, 2);
+    if (s.k <= 16) return go(k1_tau_mask<64, 16, 4>, k1_tau_solve<16>, 64, 4);
     return go(k1_tau_mask<64, 32, 2>, k1_tau_solve<32>, 64, 2);
 }
 
@@ -2989,8 +2989,11 @@ cudaError_t tc_forward(const Shape& s, const void* Q, const void* K, const void*
 #endif  // part 2
 
 #if ASA_PART(5)
+// k <= 8: there the fused kernel (four epilogue warpgroups in both phases)
+// is as fast as the separate launches; for k <= 16 the separate forward with
+// two warpgroups is faster than either four-warpgroup variant.
 bool tc_fused_supported(const Shape& s) {
-    return !s.exact_tau && s.out_dtype == ASA_DTYPE_BF16 && s.k <= 16;
+    return !s.exact_tau && s.out_dtype == ASA_DTYPE_BF16 && s.k <= 8;
 }
 
 cudaError_t tc_fused_forward(const Shape& s, const void* Q, const void* K, const void* V, const int32_t* Qidx,
@@ -3024,14 +3027,9 @@ cudaError_t tc_fused_forward(const Shape& s, const void* Q, const void* K, const
         };
         using I64 = std::integral_constant<int, 64>;
         using I128 = std::integral_constant<int, 128>;
-        using W2 = std::integral_constant<int, 2>;
         using W4 = std::integral_constant<int, 4>;
-        if (s.d == 128) {
-            if (s.k <= 8) return go(k13_fused<128, bf, 8, PI, 4>, I128{}, W4{});
-            return go(k13_fused<128, bf, 16, PI, 2>, I128{}, W2{});
-        }
-        if (s.k <= 8) return go(k13_fused<64, bf, 8, PI, 4>, I64{}, W4{});
-        return go(k13_fused<64, bf, 16, PI, 2>, I64{}, W2{});
+        if (s.d == 128) return go(k13_fused<128, bf, 8, PI, 4>, I128{}, W4{});
+        return go(k13_fused<64, bf, 8, PI, 4>, I64{}, W4{});
     });
 }
 #endif  // part 5

@@ -101,7 +101,7 @@ def splash_attention(Q, K, V, Q_idx=None, K_idx=None, *, alpha=1.5, sm_scale=Non
     gradient by the α-entmax Jacobian.  Both together give exact α-entmax
     attention and its exact gradient.
 
-    fused_forward=True runs the tcgen05 forward (bf16 output, k_keep <= 16,
+    fused_forward=True runs the tcgen05 forward (bf16 output, k_keep <= 8,
     reference τ) as one kernel per query block -- τ / mask and the forward
     together; False runs them as separate launches.  The outputs agree
     either way."""

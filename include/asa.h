@@ -100,7 +100,7 @@ typedef struct asa_params {
                            /* 0: every visible key is read in full.              */
     int tau_mode;          /* asa_tau_mode (default ASA_TAU_REFERENCE)            */
     int grad_mode;         /* asa_grad_mode (default ASA_GRAD_REFERENCE)          */
-    int fused_forward;     /* tcgen05 forward with reference τ, bf16 out, k <= 16: */
+    int fused_forward;     /* tcgen05 forward with reference τ, bf16 out, k <= 8:  */
                            /* 1 (default) one kernel per query block runs τ /     */
                            /* mask and the forward (Q read once, no tile lists    */
                            /* between them); 0: separate τ / mask, tile-list and  */

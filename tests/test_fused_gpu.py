@@ -7,7 +7,8 @@ the same epilogue width, so every output must be bit-identical: O, O32, τ,
 the block mask, the CSR and Σp.  The oracle parity of the default (fused)
 path is covered by the other GPU parity tests; this file pins that the
 fusion itself changes nothing, including on ragged shapes, saturated rows,
-partial query blocks, empty query blocks and k = 16.
+partial query blocks and empty query blocks; with k = 16 (served by the
+separate launches) the request must fall back and still agree.
 """
 import pytest
 import torch
@@ -49,7 +50,9 @@ def test_fused_forward_equals_separate_launches(name, cuda):
     base = dict(alpha=alpha, k_keep=k, sm_scale=d ** -0.5, causal=causal, backend="tc")
     with ops.profile() as prof:
         Of, sf = forward(dev, ops.Settings(fused_forward=True, **base))
-    assert "forward_fused" in prof.result and "tau_mask" not in prof.result
+    # the fused kernel serves k <= 8; larger k runs the separate launches
+    assert ("forward_fused" in prof.result) == (k <= 8)
+    assert ("tau_mask" in prof.result) == (k > 8)
     with ops.profile() as prof:
         Os, ss = forward(dev, ops.Settings(fused_forward=False, **base))
     assert "forward_fused" not in prof.result and "tau_mask" in prof.result
