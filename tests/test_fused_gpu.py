@@ -26,6 +26,10 @@ CASES = {
     "saturated": (1, 2, 1024, 1024, 128, 8, 1.5, 8.0, True, 0, 0),
     "clusters": (1, 2, 2048, 2048, 128, 8, 2.0, 1.0, True, 0, 16),
     "alpha13": (1, 2, 1024, 1024, 64, 8, 1.3, 1.0, True, 0, 0),
+    # odd query-block counts: the separate forward pairs query blocks per CTA
+    "odd_blocks": (1, 2, 640, 640, 128, 8, 1.5, 1.0, True, 0, 0),
+    "odd_partial": (2, 1, 300, 900, 64, 8, 2.0, 1.0, True, 600, 0),
+    "odd_noncausal": (1, 2, 384, 1000, 128, 8, 1.5, 1.0, False, 0, 0),
     # queries whose positions precede every key: an empty first query block
     "empty_blocks": (1, 1, 512, 512, 128, 8, 1.5, 1.0, True, -200, 0),
 }
