@@ -1196,6 +1196,41 @@ __device__ __forceinline__ void warp_store_rows(TO* base, int ld, int nrows, int
     __syncwarp();
 }
 
+// A warp's 32 rows x 32 columns (lane = row, values o[0..31]) staged in
+// shared memory in the store maps' swizzled layouts -- fp32 rows of 128 B
+// (16-byte chunk j of row r at j ^ (r & 7)), bf16 rows of 64 B (chunk j at
+// j ^ ((r >> 1) & 3)) -- and written by TMA: to mA (fp32) when wA, to mB
+// when wB (fp32 from the same staging if B16 is false, else bf16).  stage:
+// 6 KB, 1024-byte aligned; the caller waits (bulk_wait_read) before reusing
+// it.  Rows past the tensor's end are clipped by the TMA unit.
+template <bool B16>
+__device__ __forceinline__ void warp_tma_store(const CUtensorMap* mA, bool wA, const CUtensorMap* mB, bool wB,
+                                               uint8_t* stage, const float (&o)[32], int lane, int x, int y,
+                                               int z) {
+    if (wA || (wB && !B16)) {
+        float4* st = reinterpret_cast<float4*>(stage);
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+            st[lane * 8 + (j ^ (lane & 7))] = make_float4(o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]);
+    }
+    if (wB && B16) {
+        uint4* st = reinterpret_cast<uint4*>(stage + 4096);
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+            st[lane * 4 + (j ^ ((lane >> 1) & 3))] =
+                make_uint4(pack_bf16(o[8 * j], o[8 * j + 1]), pack_bf16(o[8 * j + 2], o[8 * j + 3]),
+                           pack_bf16(o[8 * j + 4], o[8 * j + 5]), pack_bf16(o[8 * j + 6], o[8 * j + 7]));
+    }
+    fence_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+        if (wA) tma_store_3d(mA, stage, x, y, z);
+        if (wB) tma_store_3d(mB, B16 ? stage + 4096 : stage, x, y, z);
+        bulk_commit();
+    }
+    __syncwarp();
+}
+
 // Store this thread's fp32 values o[0..31] (columns [32c, 32c+32) of `row`)
 // to a row-major [rows][D] output of type TO.
 template <int D, typename TO>
@@ -1398,7 +1433,8 @@ template <int D, typename TO, int PINV, int NW>
 __device__ void fwd_epilogue(const FwdPhase& f, const Shape& s, const int32_t* __restrict__ Kidx_bh,
                              int qmin_blk, uint32_t tbase, int warp, int lane, int et, int bh, int qb,
                              int qpos, float tq, TO* __restrict__ O, float* __restrict__ O32,
-                             float* __restrict__ rownorm, int split, int* err) {
+                             const CUtensorMap* mO32, const CUtensorMap* mO, float* __restrict__ rownorm,
+                             int split, int* err) {
     constexpr int NE = 128 * NW;
     constexpr int CP = 4 / NW;                // 32-column chunks per thread per tile
     constexpr int TB = D * TILE * 2;
@@ -1536,11 +1572,14 @@ __device__ void fwd_epilogue(const FwdPhase& f, const Shape& s, const int32_t* _
     mbar_wait(f.o_full, 0, s.spins, err, ASA_ERR_DEVICE_TIMEOUT);
     tc_fence_after();
     const float inv = __fdiv_rn(1.0f, __fadd_rn(n, ASA_EPS));
-    // every MMA is done: the K stages are free for the store staging
-    float* stage = reinterpret_cast<float*>(f.sK) + (et >> 5) * (32 * 33);
+    // every MMA is done: the K stages are free for the store staging (6 KB
+    // per storing warp: at most 16 warps x 6 KB = the three K stages at
+    // D = 128; at D = 64 only the first eight warps store)
+    uint8_t* stage = f.sK + (et >> 5) * 6144;
     const int q0 = qb * TILE + (warp & 3) * 32;
     const int nrows = min(32, s.NQ - q0);
-    const size_t row0 = (size_t)bh * s.NQ + q0;
+    const bool wA = O32 != nullptr, wB = sizeof(TO) == 2 || (void*)O != (void*)O32;
+    bool pending = false;
 #pragma unroll 1
     for (int c = h; c < D / 32; c += NW) {
         uint32_t r[32];
@@ -1553,9 +1592,15 @@ __device__ void fwd_epilogue(const FwdPhase& f, const Shape& s, const int32_t* _
             float v = f.T > 0 ? __uint_as_float(r[i]) * inv : 0.0f;
             o[i] = isfinite(v) ? v : 0.0f;
         }
-        if (O32) warp_store_rows<float>(O32 + row0 * D, D, nrows, c * 32, o, stage, lane);
-        if (sizeof(TO) == 2 || (void*)O != (void*)O32) warp_store_rows<TO>(O + row0 * D, D, nrows, c * 32, o, stage, lane);
+        if (pending) {   // the previous chunk's stores have read the staging
+            if (lane == 0) bulk_wait_read();
+            __syncwarp();
+        }
+        warp_tma_store<sizeof(TO) == 2>(mO32, wA, mO, wB, stage, o, lane, c * 32, q0, bh);
+        pending = true;
     }
+    if (pending && lane == 0) bulk_wait_read();   // before the CTA's shared memory is released
+    __syncwarp();
 }
 
 template <int NW>
@@ -1564,7 +1609,8 @@ constexpr int fwd_threads() { return K3_EPI0 + 128 * NW; }
 template <int D, typename TO, int PINV, int NW>
 __global__ void __launch_bounds__(fwd_threads<NW>(), 1)
 k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-           const __grid_constant__ CUtensorMap tmV, Shape s, const int32_t* __restrict__ Qidx,
+           const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO32,
+           const __grid_constant__ CUtensorMap tmO, Shape s, const int32_t* __restrict__ Qidx,
            const int32_t* __restrict__ Kidx, Bounds bd, const float* __restrict__ tau,
            const int32_t* __restrict__ ptr, const int32_t* __restrict__ idx, TO* __restrict__ O,
            float* __restrict__ O32, float* __restrict__ rownorm, int split, int* err) {
@@ -1641,7 +1687,7 @@ k3_forward(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUte
         const int qpos = !qv ? INT_MIN : (s.causal ? Qidx[qrow] : INT_MAX);
         const float tq = qv ? tau[qrow] : 0.0f;
         fwd_epilogue<D, TO, PINV, NW>(f, s, Kidx_bh, qmin_blk, tbase, warp, lane, et, bh, qb, qpos, tq, O, O32,
-                                      rownorm, split, err);
+                                      &tmO32, &tmO, rownorm, split, err);
     }
     tc_fence_before();
     __syncthreads();
@@ -1672,7 +1718,8 @@ constexpr size_t fused_region_bytes() {
 template <int D, typename TO, int KM, int PINV, int NW>
 __global__ void __launch_bounds__(fwd_threads<NW>(), 1)
 k13_fused(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-          const __grid_constant__ CUtensorMap tmV, Shape s, const int32_t* __restrict__ Qidx,
+          const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO32,
+          const __grid_constant__ CUtensorMap tmO, Shape s, const int32_t* __restrict__ Qidx,
           const int32_t* __restrict__ Kidx, Bounds bd, float* __restrict__ tau, uint8_t* __restrict__ M,
           TO* __restrict__ O, float* __restrict__ O32, float* __restrict__ rownorm, int split, int* err) {
     constexpr int NE = 128 * NW;
@@ -1808,7 +1855,7 @@ k13_fused(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUten
         }
         asm volatile("bar.sync 2, %0;" ::"n"(NE) : "memory");
         fwd_epilogue<D, TO, PINV, NW>(f, s, Kidx_bh, qmin_blk, tbase, warp, lane, et, bh, qb, qpos, tau_s[row],
-                                      O, O32, rownorm, split, err);
+                                      O, O32, &tmO32, &tmO, rownorm, split, err);
     }
     tc_fence_before();
     __syncthreads();
@@ -2789,6 +2836,23 @@ bool make_map(CUtensorMap* m, const void* ptr, int BH, int N, int d) {
     return r == CUDA_SUCCESS;
 }
 
+// Store map of an output [BH][N][d] (fp32 or bf16): boxes of 32 x 32 x 1,
+// swizzled rows (128 B fp32, 64 B bf16) as warp_tma_store stages them.
+bool make_store_map(CUtensorMap* m, const void* ptr, int BH, int N, int d, bool f32) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    const int es = f32 ? 4 : 2;
+    cuuint64_t dims[3] = {(cuuint64_t)d, (cuuint64_t)N, (cuuint64_t)BH};
+    cuuint64_t strides[2] = {(cuuint64_t)d * es, (cuuint64_t)N * d * es};
+    cuuint32_t box[3] = {32, 32, 1};
+    cuuint32_t est[3] = {1, 1, 1};
+    CUresult r = fn(m, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3,
+                    const_cast<void*>(ptr), dims, strides, box, est, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    f32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
 size_t bounds_ints(const Shape& s) { return (size_t)2 * s.BH * (s.nQB + s.nKB); }
 
 Bounds bounds_at(const Shape& s, void* ws) {
@@ -2956,10 +3020,13 @@ cudaError_t tc_exact_tau(const Shape& s, const void* Q, const void* K, const int
 cudaError_t tc_forward(const Shape& s, const void* Q, const void* K, const void* V, const int32_t* Qidx,
                        const int32_t* Kidx, const float* tau, const int32_t* ptr, const int32_t* idx,
                        void* O, float* O32, float* rownorm, void* ws, int* err, cudaStream_t st) {
-    CUtensorMap mQ, mK, mV;
+    CUtensorMap mQ, mK, mV, mO32, mO;
     if (!make_map(&mQ, Q, s.BH, s.NQ, s.d) || !make_map(&mK, K, s.BH, s.NK, s.d) ||
-        !make_map(&mV, V, s.BH, s.NK, s.d))
+        !make_map(&mV, V, s.BH, s.NK, s.d) ||
+        !make_store_map(&mO, O, s.BH, s.NQ, s.d, s.out_dtype == ASA_DTYPE_F32))
         return cudaErrorInvalidValue;
+    if (!O32) mO32 = mO;   // not stored
+    else if (!make_store_map(&mO32, O32, s.BH, s.NQ, s.d, true)) return cudaErrorInvalidValue;
     Bounds bd = bounds_at(s, ws);   // filled by tc_tau_mask
     dim3 grid(s.BH * s.nQB);
     const int split = s.split;
@@ -2974,8 +3041,8 @@ cudaError_t tc_forward(const Shape& s, const void* Q, const void* K, const void*
                                     (size_t)s.nKB * 4;
                 cudaError_t r = prep(k, smem);
                 if (r != cudaSuccess) return r;
-                k<<<grid, fwd_threads<NW>(), smem, st>>>(mQ, mK, mV, s, Qidx, Kidx, bd, tau, ptr, idx, (TO*)O,
-                                                         O32, rownorm, split, err);
+                k<<<grid, fwd_threads<NW>(), smem, st>>>(mQ, mK, mV, mO32, mO, s, Qidx, Kidx, bd, tau, ptr, idx,
+                                                         (TO*)O, O32, rownorm, split, err);
                 note_launch();
                 return cudaGetLastError();
             };
@@ -3002,10 +3069,13 @@ cudaError_t tc_fused_forward(const Shape& s, const void* Q, const void* K, const
     if (!tc_fused_supported(s)) return cudaErrorInvalidValue;
     cudaError_t e = launch_bounds(s, Qidx, Kidx, ws, st);
     if (e != cudaSuccess) return e;
-    CUtensorMap mQ, mK, mV;
+    CUtensorMap mQ, mK, mV, mO32, mO;
     if (!make_map(&mQ, Q, s.BH, s.NQ, s.d) || !make_map(&mK, K, s.BH, s.NK, s.d) ||
-        !make_map(&mV, V, s.BH, s.NK, s.d))
+        !make_map(&mV, V, s.BH, s.NK, s.d) ||
+        !make_store_map(&mO, O, s.BH, s.NQ, s.d, s.out_dtype == ASA_DTYPE_F32))
         return cudaErrorInvalidValue;
+    if (!O32) mO32 = mO;   // not stored
+    else if (!make_store_map(&mO32, O32, s.BH, s.NQ, s.d, true)) return cudaErrorInvalidValue;
     Bounds bd = bounds_at(s, ws);
     dim3 grid(s.BH * s.nQB);
     const int split = s.split;
@@ -3020,8 +3090,8 @@ cudaError_t tc_fused_forward(const Shape& s, const void* Q, const void* K, const
                                 (size_t)(NW + 2) * TILE * 4 + 16 * 4 + (size_t)s.nKB * 9 + 64;
             cudaError_t r = prep(k, smem);
             if (r != cudaSuccess) return r;
-            k<<<grid, fwd_threads<NW>(), smem, st>>>(mQ, mK, mV, s, Qidx, Kidx, bd, tau, M, (bf*)O, O32, rownorm,
-                                                     split, err);
+            k<<<grid, fwd_threads<NW>(), smem, st>>>(mQ, mK, mV, mO32, mO, s, Qidx, Kidx, bd, tau, M, (bf*)O, O32,
+                                                     rownorm, split, err);
             note_launch();
             return cudaGetLastError();
         };
