@@ -85,7 +85,7 @@ def load_traffic(label, cfg_name):
 def head_range(c, rank, world, scaling):
     """(global heads, this rank's [h0, h1)) under the given scaling."""
     from splash_attention.shard import partition
-    per_cfg = c["B"] * c["H"]
+    per_cfg = c.get("heads") or c["B"] * c["H"]
     total = per_cfg * world if scaling == "weak" else per_cfg
     return total, partition(total, world)[rank]
 
@@ -476,9 +476,14 @@ def main():
                     help="separate τ/mask, tile-list and forward launches instead of the fused forward")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--heads", type=int, default=None,
+                    help="global heads per configuration instead of B*H (small profiling cases; "
+                         "the line's config then names the reduced count)")
     ap.add_argument("--e2e-chunk", type=int, default=4, help="heads per chunk in the e2e leg")
     a = ap.parse_args()
     c = dict(CONFIGS[a.config])
+    if a.heads:
+        c["heads"] = a.heads
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
     if a.impl == "reference":
