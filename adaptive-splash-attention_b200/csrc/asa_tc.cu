@@ -2784,21 +2784,31 @@ k4_jac(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensor
 }
 
 // ===========================================================================
-// K4 pre: D_q = Σ_t O_t · dO_t (fp32 O, bf16 dO) and 1/(n+EPS), one warp per row.
+// K4 pre: D_q = Σ_t O_t · dO_t (fp32 O, bf16 dO) and 1/(n+EPS).  D/4 lanes
+// per row, each reading one float4 of O and four bf16 of dO (16- and 8-byte
+// loads: the kernel is HBM-bound); d = 64 puts two rows in a warp.
 // ===========================================================================
 template <int D>
 __global__ void k4_pre(const float* __restrict__ O32, const __nv_bfloat16* __restrict__ dO,
                        const float* __restrict__ rownorm, float* __restrict__ Dq,
                        float* __restrict__ invN, size_t rows) {
-    const size_t r = (size_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    constexpr int LPR = D / 4;                // lanes per row
+    constexpr int RPW = 32 / LPR;             // rows per warp
     const int lane = threadIdx.x & 31;
-    if (r >= rows) return;
+    const int l = lane % LPR;
+    const size_t r = ((size_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * RPW + lane / LPR;
     float acc = 0.0f;
+    if (r < rows) {
+        const float4 o = __ldg(reinterpret_cast<const float4*>(O32 + r * D) + l);
+        const uint2 g = __ldg(reinterpret_cast<const uint2*>(dO + r * D) + l);
+        acc = fmaf(o.x, __uint_as_float(g.x << 16), acc);
+        acc = fmaf(o.y, __uint_as_float(g.x & 0xffff0000u), acc);
+        acc = fmaf(o.z, __uint_as_float(g.y << 16), acc);
+        acc = fmaf(o.w, __uint_as_float(g.y & 0xffff0000u), acc);
+    }
 #pragma unroll
-    for (int t = lane; t < D; t += 32) acc = fmaf(O32[r * D + t], __bfloat162float(dO[r * D + t]), acc);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-    if (lane == 0) {
+    for (int off = LPR / 2; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+    if (l == 0 && r < rows) {
         Dq[r] = acc;
         invN[r] = __fdiv_rn(1.0f, __fadd_rn(rownorm[r], ASA_EPS));   // reference :435
     }
@@ -3161,13 +3171,15 @@ cudaError_t tc_backward(const Shape& s, const void* Q, const void* K, const void
                       make_map(&a.mV, V, s.BH, s.NK, s.d) && make_map(&a.mdO, dO, s.BH, s.NQ, s.d);
     if (!maps && (stages & 6 || s.jacobian)) return cudaErrorInvalidValue;
     if (stages & 1) {
+        // k4_pre reads O (fp32) and dO (bf16) rows as 16- and 8-byte vectors
+        if (((uintptr_t)O32 & 15) || ((uintptr_t)dO & 15)) return cudaErrorInvalidValue;
         e = launch_bounds(s, Qidx, Kidx, ws, st);
         if (e != cudaSuccess) return e;
         if (s.d == 128)
             k4_pre<128><<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(O32, (const __nv_bfloat16*)dO, rownorm, Dq,
                                                                      invNv, rows);
         else
-            k4_pre<64><<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(O32, (const __nv_bfloat16*)dO, rownorm, Dq,
+            k4_pre<64><<<(unsigned)((rows + 15) / 16), 256, 0, st>>>(O32, (const __nv_bfloat16*)dO, rownorm, Dq,
                                                                     invNv, rows);
         note_launch();
         e = cudaGetLastError();
