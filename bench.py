@@ -68,17 +68,19 @@ def load_peaks():
         return 1590.0, 1400.0, 6650.0, "fallback"
 
 
-def load_traffic(label, cfg_name):
+def load_traffic(label, cfg_name, head_frac=1.0):
     """Per-launch DRAM bytes of `label` copied from a committed ncu capture
-    (profiles/traffic.txt: `label config bytes_per_launch source`), or None.
-    Not measured by this run: ncu cannot run inside a timed bench."""
+    (profiles/traffic.txt: `label config bytes_per_launch source`, bytes of
+    a launch over the configuration's B*H heads), times `head_frac` (this
+    rank's heads / B*H: every head's tensors are read and written once), or
+    None.  Not measured by this run: ncu cannot run inside a timed bench."""
     path = os.path.join(ROOT, "profiles", "traffic.txt")
     if not os.path.exists(path):
         return None
     for line in open(path):
         f = line.split()
         if len(f) >= 3 and not line.startswith("#") and f[0] == label and f[1] == cfg_name:
-            return {"bytes": float(f[2]), "source": " ".join(f[3:]) or "profiles/traffic.txt"}
+            return {"bytes": float(f[2]) * head_frac, "source": " ".join(f[3:]) or "profiles/traffic.txt"}
     return None
 
 
@@ -378,7 +380,7 @@ def measure(a, c, name, rank, world, dev, scaling, dist, with_extras=True):
         dom_flops = TILE_UNITS.get(dom_label, 0) * unit_flops * T_local
     per_launch_ms = dom_ms / max(dom_n, 1)
     achieved = dom_flops / max(dom_n, 1) / (per_launch_ms * 1e-3) / 1e12
-    traffic = load_traffic(dom_label, name)
+    traffic = load_traffic(dom_label, name, (h1 - h0) / (c["B"] * c["H"]))
     # kernels are timed inside one short step (milliseconds), so the burst
     # peak is the denominator
     rec["roofline"] = {"kernel": dom_label, "bound": "tensor", "achieved": achieved,
