@@ -425,16 +425,16 @@ def measure(a, c, name, rank, world, dev, scaling, dist, with_extras=True):
             h2d = sum(x.numel() * x.element_size() for x in (hQ, hK, hV, hdO))
             d2h = sum(x.numel() * x.element_size() for x in outs)
 
-            # chunks of at least 16 MiB of inputs: small heads in tiny chunks
-            # leave the GPU idle between copies
-            head_bytes = 4 * N * c["d"] * Q.element_size()
-            chunk = max(a.e2e_chunk, -(-(16 << 20) // head_bytes))
+            # heads per chunk: the API's default (chunks of at least 32 MiB
+            # of inputs) unless --e2e-chunk names a count
+            chunk = a.e2e_chunk
 
             def e2e_step():
                 sa.forward_backward_host(hQ, hK, hV, hdO, hidx, hidx, out=outs,
                                          heads_per_chunk=chunk, synchronize=False, **st)
-            api = (f"splash_attention.forward_backward_host (pinned host in/out, {chunk} "
-                   "heads per chunk, copies overlapped with kernels)")
+            api = ("splash_attention.forward_backward_host (pinned host in/out, "
+                   + (f"{chunk} heads per chunk" if chunk else "chunks of >= 32 MiB of inputs")
+                   + ", copies overlapped with kernels)")
         for _ in range(2):
             e2e_step()
         torch.cuda.synchronize()
@@ -481,7 +481,8 @@ def main():
     ap.add_argument("--heads", type=int, default=None,
                     help="global heads per configuration instead of B*H (small profiling cases; "
                          "the line's config then names the reduced count)")
-    ap.add_argument("--e2e-chunk", type=int, default=4, help="heads per chunk in the e2e leg")
+    ap.add_argument("--e2e-chunk", type=int, default=None,
+                    help="heads per chunk in the e2e leg (default: chunks of at least 32 MiB of inputs)")
     a = ap.parse_args()
     c = dict(CONFIGS[a.config])
     if a.heads:

@@ -9,7 +9,7 @@ from helpers import make_inputs
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("causal,chunk", [(True, 4), (False, 5), (True, 64)])
+@pytest.mark.parametrize("causal,chunk", [(True, 4), (False, 5), (True, 64), (True, None), (False, [1, 3, 2])])
 def test_streamed_matches_device_api(cuda, causal, chunk):
     import splash_attention as sa
     from splash_attention import ops
@@ -23,3 +23,11 @@ def test_streamed_matches_device_api(cuda, causal, chunk):
     torch.cuda.synchronize()
     for name, g, w in zip(("O", "dQ", "dK", "dV"), got, (O,) + tuple(grads)):
         assert torch.equal(g, w.cpu()), name
+
+
+def test_streamed_rejects_bad_chunk_sizes(cuda):
+    import splash_attention as sa
+    Q, K, V, dO, Qi, Ki = make_inputs(1, 2, 128, 128, 64, seed=3, dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="sum to B\\*H"):
+        sa.forward_backward_host(*(x.pin_memory() for x in (Q, K, V, dO)), Qi, Ki,
+                                 heads_per_chunk=[1, 2], alpha=1.5, k_keep=8)
