@@ -1489,26 +1489,33 @@ __device__ void fwd_epilogue(const FwdPhase& f, const Shape& s, const int32_t* _
             for (int cc = 0; cc < CP; ++cc)
                 vis[cc] = all ? 0xffffffffu : vis_mask32(Kidx_bh, kb * TILE + (h * CP + cc) * 32, s.NK, s.causal, qpos);
             tmem_ld_wait();
+            // fully visible tiles (almost all) skip the per-key visibility select
+            auto weights = [&](auto all_vis) {
 #pragma unroll
-            for (int cc = 0; cc < CP; ++cc) {
-                const uint32_t col = tl + b * 128 + (h * CP + cc) * 32;
+                for (int cc = 0; cc < CP; ++cc) {
+                    const uint32_t col = tl + b * 128 + (h * CP + cc) * 32;
 #pragma unroll
-                for (int g = 0; g < 2; ++g) {
-                    uint32_t hi[8], lo[8];
+                    for (int g = 0; g < 2; ++g) {
+                        uint32_t hi[8], lo[8];
 #pragma unroll
-                    for (int m = 0; m < 8; ++m) {
-                        float2 pp = entmax_pair<PINV>(r[cc][16 * g + 2 * m], r[cc][16 * g + 2 * m + 1],
-                                                      c1, mtau, uhi);
-                        const int bit = 16 * g + 2 * m;
-                        pp.x = (vis[cc] >> bit) & 1u ? pp.x : 0.0f;
-                        pp.y = (vis[cc] >> (bit + 1)) & 1u ? pp.y : 0.0f;
-                        n2 = __fadd2_rn(n2, pp);
-                        split_pair(pp, hi[m], lo[m]);
+                        for (int m = 0; m < 8; ++m) {
+                            float2 pp = entmax_pair<PINV>(r[cc][16 * g + 2 * m], r[cc][16 * g + 2 * m + 1],
+                                                          c1, mtau, uhi);
+                            if constexpr (!decltype(all_vis)::value) {
+                                const int bit = 16 * g + 2 * m;
+                                pp.x = (vis[cc] >> bit) & 1u ? pp.x : 0.0f;
+                                pp.y = (vis[cc] >> (bit + 1)) & 1u ? pp.y : 0.0f;
+                            }
+                            n2 = __fadd2_rn(n2, pp);
+                            split_pair(pp, hi[m], lo[m]);
+                        }
+                        tmem_st8(col + g * 16, hi);
+                        tmem_st8(col + g * 16 + 8, lo);
                     }
-                    tmem_st8(col + g * 16, hi);
-                    tmem_st8(col + g * 16 + 8, lo);
                 }
-            }
+            };
+            if (all) weights(std::true_type{});
+            else weights(std::false_type{});
             tmem_st_wait();
             tc_fence_before();
             epi_arrive(&f.p_full[b]);
